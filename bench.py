@@ -1,0 +1,354 @@
+"""Benchmark of the narrow-float quantise / block-scaled GEMM path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload mxfp8_quantize|...]
+
+One JSON line on rank 0. A "step" is one pass of the hot path over one batch of synthetic input:
+for ``mxfp8_quantize`` (the default, 8192 x 8192 bf16 -> E4M3 + UE8M0 per 32) one quantise
+launch. ``value`` is device-timed (CUDA events on the launching stream, max over ranks) with the
+inputs resident in HBM; ``e2e`` is the same metric through the public API with host buffers,
+including the host->device copy of the input and the device->host copy of the results.
+
+``--impl reference`` times the reference's conversion semantics on the host cores instead (the
+C oracle: the reference crate itself cannot be built here, it targets nvptx64 only), on the same
+workload, metric and unit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "ptx-std_b200")]
+
+METRIC = "Block-scaled FP8/FP4 GEMM TFLOPS/GPU (% tensor peak); quantise GB/s (% HBM)"
+HBM_FALLBACK_GBS = 6650.0
+BF16_FALLBACK_TFLOPS = 1590.0
+
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d.get("hbm_gbs", HBM_FALLBACK_GBS),
+                "bf16_tflops": d.get("bf16_tflops", BF16_FALLBACK_TFLOPS),
+                "source": "measured"}
+    return {"hbm_gbs": HBM_FALLBACK_GBS, "bf16_tflops": BF16_FALLBACK_TFLOPS,
+            "source": "fallback"}
+
+
+def profiled_traffic(kernel: str):
+    """DRAM bytes per launch recorded from an ncu capture of this kernel (profiles/traffic.json)."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    return json.load(open(p)).get(kernel, {}).get("dram_bytes_per_launch")
+
+
+# ---- clocks ---------------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---- distributed plumbing -------------------------------------------------------------------
+
+class Dist:
+    def __init__(self, n_gpus: int):
+        import torch
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != n_gpus and self.world > 1:
+            raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={self.world}")
+        torch.cuda.set_device(self.local)
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as td
+            td.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                  device_id=torch.device("cuda", self.local))
+            self.pg = td
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ---- workloads --------------------------------------------------------------------------------
+
+class MxFp8Quantize:
+    """bf16 [8192, 8192] -> E4M3 [8192, 8192] + UE8M0 [8192, 256] (row-major scales)."""
+
+    name = "mxfp8_quantize"
+    unit = "GB/s"
+    dtype = "bf16->e4m3+ue8m0"
+    rows = cols = 8192
+    kernel = "quantize_mxfp8_kernel"
+
+    def __init__(self):
+        self.in_bytes = self.rows * self.cols * 2
+        self.out_bytes = self.rows * self.cols + self.rows * self.cols // 32
+        self.bytes = self.in_bytes + self.out_bytes  # algorithmic bytes per step
+        self.config = {"workload": "mxfp8_quantize bf16 8192x8192 -> e4m3 + ue8m0/32",
+                       "rows": self.rows, "cols": self.cols, "sf_layout": "row-major",
+                       "l2": "inputs larger than L2 (197 MiB/step), 2 rotating buffer sets"}
+
+    def host_input(self):
+        if getattr(self, "_x", None) is None:
+            from ptxstd import workloads
+            self._x = workloads.mxfp8_activation(self.rows, self.cols)
+        return self._x
+
+    def setup(self, torch, x_np):
+        import numpy as np
+        xh = torch.from_numpy(x_np.view(np.int16)).view(torch.bfloat16)
+        self.x_host = xh.pin_memory()
+        self.sets = []
+        for _ in range(2):
+            x = self.x_host.cuda()
+            q = torch.empty((self.rows, self.cols), dtype=torch.uint8, device="cuda")
+            sf = torch.empty((self.rows, self.cols // 32), dtype=torch.uint8, device="cuda")
+            self.sets.append((x, q, sf))
+        self.q_host = torch.empty((self.rows, self.cols), dtype=torch.uint8, pin_memory=True)
+        self.sf_host = torch.empty((self.rows, self.cols // 32), dtype=torch.uint8,
+                                   pin_memory=True)
+
+    def step(self, i):
+        import ptxstd
+        x, q, sf = self.sets[i % 2]
+        ptxstd.quantize_mxfp8(x, out=(q, sf))
+        return 1  # kernel launches
+
+    def e2e_step(self, i):
+        """Public API from host buffers: H2D input, quantise, D2H payload + scales."""
+        import ptxstd
+        x, q, sf = self.sets[i % 2]
+        x.copy_(self.x_host, non_blocking=True)
+        ptxstd.quantize_mxfp8(x, out=(q, sf))
+        self.q_host.copy_(q, non_blocking=True)
+        self.sf_host.copy_(sf, non_blocking=True)
+        return 1
+
+    def value(self, seconds_per_step: float) -> float:
+        return self.bytes / seconds_per_step / 1e9
+
+    def cpu_sample(self, threads: int, budget_s: float):
+        """Oracle quantise of the full tensor, repeated up to budget_s of wall time."""
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        x = self.host_input()
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            O.quantize_mxfp8(x, threads)
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= budget_s or reps >= 20:
+                break
+        return self.bytes * reps / el / 1e9, f"{reps} x full 8192x8192 quantise"
+
+
+WORKLOADS = {"mxfp8_quantize": MxFp8Quantize}
+
+
+# ---- arms -----------------------------------------------------------------------------------
+
+def run_ours(args, wl) -> dict | None:
+    import torch
+    dist = Dist(args.gpus)
+    torch.manual_seed(0)
+    wl.setup(torch, wl.host_input())
+    stream = torch.cuda.current_stream()
+
+    for i in range(args.warmup):
+        wl.step(i)
+    torch.cuda.synchronize()
+
+    # device-timed region: K steps, inputs resident in HBM
+    sampler = ClockSampler(torch.cuda.current_device()) if dist.rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    ev0.record(stream)
+    for i in range(args.steps):
+        launches += wl.step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    clocks = sampler.stop() if sampler else None
+
+    # end-to-end through the public API with host buffers
+    for i in range(2):
+        wl.e2e_step(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        wl.e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    ms_max = dist.max(ms)
+    e2e_max = dist.max(e2e_ms)
+    rank = dist.rank
+    world = dist.world
+    dist.close()
+    if rank != 0:
+        return None
+
+    per_step_s = ms_max / 1e3 / args.steps
+    value = wl.value(per_step_s) * world
+    peaks = measured_peaks()
+    per_launch_s = per_step_s  # one launch per step
+    achieved = wl.bytes / per_launch_s / 1e9
+    traffic = profiled_traffic(wl.kernel)
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": wl.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+        "data": "synthetic (seeded numpy)", "config": dict(wl.config, parallelism=f"replicas{world}"),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                     "peak_source": peaks["source"] + " hbm_gbs (burst copy)",
+                     "algorithmic_bytes_per_launch": wl.bytes},
+        "e2e": {"value": round(wl.value(e2e_max / 1e3 / args.steps) * world, 2),
+                "unit": wl.unit, "h2d_bytes_per_step": wl.in_bytes,
+                "d2h_bytes_per_step": wl.out_bytes},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        v, sample = wl.cpu_sample(threads, budget_s=3.0)
+        out["cpu_baseline"] = {"value": round(v, 3), "unit": wl.unit, "cores": threads,
+                               "kind": "port", "sample": sample}
+    return out
+
+
+def run_reference(args, wl) -> dict | None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    vals = []
+    sample = ""
+    for _ in range(args.warmup):
+        wl.cpu_sample(threads, budget_s=0.0)
+    for _ in range(args.steps):
+        v, sample = wl.cpu_sample(threads, budget_s=0.0)
+        vals.append(v)
+    v = statistics.median(vals)
+    return {"metric": METRIC, "value": round(v, 3), "unit": wl.unit, "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": wl.dtype, "data": "synthetic (seeded numpy)",
+            "config": wl.config,
+            "cpu_baseline": {"value": round(v, 3), "unit": wl.unit, "cores": threads,
+                             "kind": "port",
+                             "sample": f"per step: {sample}; the C restatement of the "
+                                       "reference's conversion semantics (oracle/), all host "
+                                       "threads"},
+            "e2e": {"value": round(v, 3), "unit": wl.unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mxfp8_quantize")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    wl = WORKLOADS[args.workload]()
+    res = run_reference(args, wl) if args.impl == "reference" else run_ours(args, wl)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,145 @@
+/*
+ * ptxstd — B200 (sm_100a) narrow-float quantisation and block-scaled tcgen05 GEMM, C ABI.
+ *
+ * caelunshun/ptx-std is a device-only Rust crate: its "interface" is the set of device functions a
+ * user kernel calls (conversions of src/data_types/, the tcgen05 descriptors and instructions of
+ * src/tcgen05/, TMA of src/tma/, mbarriers of src/mbarrier.rs). This header is the host-callable
+ * boundary that a binding of that crate (Rust `extern "C"`, ctypes, cgo ...) links against: each
+ * entry point names the reference API whose semantics it implements, file:line in the reference.
+ *
+ * Conventions
+ *   - Every function returns a ptxstd_status; no C++ exception or abort crosses the boundary.
+ *   - Pointers named d_* are device pointers owned by the caller (16-byte aligned unless noted);
+ *     h_* are host pointers. Kernels are asynchronous on `stream` (a cudaStream_t, 0 = legacy).
+ *   - Narrow codes are stored as in the reference: element 0 in the least significant bits
+ *     (src/data_types/vector.rs:1-11); two E2M1 values per byte, element 0 in the low nibble
+ *     (src/data_types/float4.rs:5-6).
+ *   - bf16 is passed as uint16_t bit patterns.
+ *   - Device-side waits are bounded; a kernel that gives up records PTXSTD_ETIMEOUT in a
+ *     per-device error word read by ptxstd_last_device_error.
+ */
+#ifndef PTXSTD_H
+#define PTXSTD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum ptxstd_status {
+    PTXSTD_OK = 0,
+    PTXSTD_EINVAL = 1,      /* bad argument: shape, alignment, null pointer, unencodable value */
+    PTXSTD_ECUDA = 2,       /* a CUDA runtime or driver call failed */
+    PTXSTD_ENCCL = 3,       /* an NCCL call failed */
+    PTXSTD_ETIMEOUT = 4,    /* a bounded device-side wait gave up */
+    PTXSTD_EUNSUPPORTED = 5 /* not supported on this device (needs sm_100a) */
+} ptxstd_status;
+
+typedef void* ptxstd_stream; /* a cudaStream_t */
+
+#if defined(__GNUC__)
+#define PTXSTD_API __attribute__((visibility("default")))
+#else
+#define PTXSTD_API
+#endif
+
+/* ---- library ------------------------------------------------------------------------------- */
+PTXSTD_API const char* ptxstd_status_string(int status);
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+PTXSTD_API int ptxstd_version(void);
+/* PTXSTD_OK when `device` is an sm_100 part this library's cubins run on. */
+PTXSTD_API int ptxstd_device_supported(int device);
+/* Reads (and, if clear != 0, resets) the calling device's error word after synchronising
+ * `stream`. *code receives 0 or a ptxstd_status; *detail a kernel-specific location code. */
+PTXSTD_API int ptxstd_last_device_error(ptxstd_stream stream, int clear, int* code, uint32_t* detail);
+
+/* ---- data_types: element-wise conversions on device arrays --------------------------------- */
+/* Vector<f8e4m3, N>::from_f32::<RELU> (src/data_types/narrow.rs:354-361, pair form :156-162):
+ * RN, .satfinite, NaN -> 0x7f, optional .relu. One code per byte. n any size. */
+PTXSTD_API int ptxstd_cvt_f32_to_e4m3(const float* d_x, uint8_t* d_out, size_t n, int relu,
+                           ptxstd_stream stream);
+/* Vector<f8e5m2, N>::from_f32::<RELU> (same macro, src/data_types/float8.rs:111-126). */
+PTXSTD_API int ptxstd_cvt_f32_to_e5m2(const float* d_x, uint8_t* d_out, size_t n, int relu,
+                           ptxstd_stream stream);
+/* Vector<f4e2m1, N>::from_f32::<RELU> (src/data_types/float4.rs:52-69): n even, n/2 bytes out,
+ * element 2i in the low nibble of byte i; NaN -> +6. */
+PTXSTD_API int ptxstd_cvt_f32_to_e2m1x2(const float* d_x, uint8_t* d_out, size_t n, int relu,
+                             ptxstd_stream stream);
+/* f8e8m0::from_f32::<RND, OVERFLOW> (src/data_types/narrow.rs:600-617, semantics :585-593):
+ * round_up = 0 -> Rounding::TowardZero, 1 -> Rounding::Up; satfinite selects .satfinite. */
+PTXSTD_API int ptxstd_cvt_f32_to_ue8m0(const float* d_x, uint8_t* d_out, size_t n, int round_up,
+                            int satfinite, ptxstd_stream stream);
+/* to_f32 of each format: exact, via f16 for FP8/FP4 (src/data_types/narrow.rs:292-299) and via
+ * bf16 for ue8m0 (src/data_types/narrow.rs:683-690). e2m1x2 decodes 2*n_bytes values. */
+PTXSTD_API int ptxstd_cvt_e4m3_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_e5m2_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_e2m1x2_to_f32(const uint8_t* d_codes, float* d_out, size_t n_bytes,
+                             ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_ue8m0_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
+/* Exhaustive-sweep helper: encodes the n f32 bit patterns base, base+1, ... (no input array) with
+ * one of the variants 0 e4m3, 1 e5m2, 2 e2m1 (one nibble per byte), 3-5 the same with .relu,
+ * 6 ue8m0 RZ satfinite, 7 ue8m0 RP satfinite. base + n <= 2^32. */
+PTXSTD_API int ptxstd_cvt_sweep(int variant, uint64_t base, uint64_t n, uint8_t* d_out,
+                     ptxstd_stream stream);
+
+/* ---- quantisation kernels ------------------------------------------------------------------- */
+/* MXFP8: bf16 [rows, cols] row-major (cols % 32 == 0) -> E4M3 [rows, cols] and one UE8M0 scale
+ * per 32 contiguous elements, [rows, cols/32] row-major. Scale = f8e8m0::from_f32::<TowardZero,
+ * SaturateFinite>(block amax) - 8 (E4M3's emax), clamped at 0, NaN kept; elements
+ * f8e4m3::from_f32(x * 2^-(scale-127)) (src/data_types/narrow.rs:156-162, :600-617; block amax
+ * as reduce_f32::<Max, Absolute> with NaN, src/warp_collectives.rs:864). */
+PTXSTD_API int ptxstd_quantize_mxfp8(const uint16_t* d_x, int64_t rows, int64_t cols, uint8_t* d_q,
+                          uint8_t* d_sf, ptxstd_stream stream);
+/* NVFP4: bf16 [rows, cols] (cols % 16 == 0) with decode global scale g (finite, > 0) ->
+ * E2M1x2 [rows, cols/2] and one E4M3 scale per 16 elements [rows, cols/16]:
+ * sf = f8e4m3::from_f32(amax / (6 g)), q = f4e2m1::from_f32(x * (1 / (sf * g))), each f32
+ * operation one IEEE rounding (src/data_types/float4.rs:52-69, float8.rs:51-68). */
+PTXSTD_API int ptxstd_quantize_nvfp4(const uint16_t* d_x, int64_t rows, int64_t cols, float global_scale,
+                          uint8_t* d_q, uint8_t* d_sf, ptxstd_stream stream);
+/* The same two kernels with a choice of scale layout: sf_layout 0 = row-major [rows, cols/B]
+ * (B = 32 or 16); 1 = the blocked layout the block-scaled GEMMs read: tiles of 128 rows x 4
+ * scale columns, 512 contiguous bytes each, row-tile major, scale (r, s) of a tile at byte
+ * (r % 32) * 16 + ((r / 32) % 4) * 4 + s % 4 (the source of one tcgen05.cp.32x128b.warpx4,
+ * src/tcgen05/copy.rs:29-30). Layout 1 needs rows % 128 == 0 and cols % (4 B) == 0. */
+PTXSTD_API int ptxstd_quantize_mxfp8_layout(const uint16_t* d_x, int64_t rows, int64_t cols, uint8_t* d_q,
+                                 uint8_t* d_sf, int sf_layout, ptxstd_stream stream);
+PTXSTD_API int ptxstd_quantize_nvfp4_layout(const uint16_t* d_x, int64_t rows, int64_t cols,
+                                 float global_scale, uint8_t* d_q, uint8_t* d_sf, int sf_layout,
+                                 ptxstd_stream stream);
+
+/* ---- tcgen05 descriptors (src/tcgen05/descriptor.rs) ---------------------------------------- */
+/* InstrDescriptor::<KIND>::new for each kind. Element types use the reference's discriminants:
+ * F16ElementType F16 0 / Bf16 1; FloatAccumulator F16 0 / F32 1; F8f6f4ElementType E4m3 0,
+ * E5m2 1, E2m3 3, E3m2 4, E2m1 5; I8ElementType U8 0 / S8 1; Nvf4ScaleType Ue4m3 0, Ue8m0 1,
+ * Ue5m3 2 (descriptor.rs:285-392). PTXSTD_EINVAL where the reference asserts. */
+PTXSTD_API int ptxstd_idesc_f16(int a, int b, int d, uint32_t m, uint32_t n, uint32_t* out);   /* :520-527 */
+PTXSTD_API int ptxstd_idesc_tf32(uint32_t m, uint32_t n, uint32_t* out);                       /* :537-541 */
+PTXSTD_API int ptxstd_idesc_f8f6f4(int a, int b, int d, uint32_t m, uint32_t n, uint32_t* out); /* :555-564 */
+PTXSTD_API int ptxstd_idesc_i8(int a, int b, uint32_t m, uint32_t n, uint32_t* out);           /* :575-578 */
+PTXSTD_API int ptxstd_idesc_mxf8f6f4(int a, int b, uint32_t m, uint32_t n, uint32_t* out);     /* :601-611 */
+PTXSTD_API int ptxstd_idesc_mxf4(uint32_t m, uint32_t n, uint32_t* out);                       /* :625-628 */
+PTXSTD_API int ptxstd_idesc_mxf4nvf4(int scale_type, uint32_t m, uint32_t n, uint32_t* out);   /* :644-653 */
+/* The with_* setters (descriptor.rs:400-411, :660-813). kind: MmaKind F16 0, Tf32 1, F8f6f4 2,
+ * I8 3, Mxf8f6f4 4, Mxf4 5, Mxf4nvf4 6 (src/tcgen05/mod.rs:322-337). field: 0 sparsity,
+ * 1 sparsity_selector, 2 saturate, 3 negate_a, 4 negate_b, 5 major_a, 6 major_b, 7 max_b_shift,
+ * 8 scale_a_id, 9 scale_b_id, 10 k. PTXSTD_EINVAL when the kind has no such setter (a compile
+ * error in the reference) or the value does not fit. */
+PTXSTD_API int ptxstd_idesc_set(uint32_t desc, int kind, int field, uint32_t value, uint32_t* out);
+/* SmemDescriptor::from_shared_address (:152-162); swizzle is the Swizzle discriminant 0, 1, 2, 4
+ * or 6 (:31-45). with_base_offset (:176-183); add_start_bytes (:231-237). */
+PTXSTD_API int ptxstd_smem_desc(uint32_t start, uint32_t lbo, uint32_t sbo, int swizzle, uint64_t* out);
+PTXSTD_API int ptxstd_smem_desc_with_base_offset(uint64_t desc, uint32_t base_offset, uint64_t* out);
+PTXSTD_API int ptxstd_smem_desc_add_start_bytes(uint64_t desc, uint32_t bytes, uint64_t* out);
+/* ZeroColumnMask::new / with_sub_mask_start / with_column_shift (:870-921); first_span is
+ * ColumnSpan Used 0 / Zeroed 1. */
+PTXSTD_API int ptxstd_zero_mask_new(uint32_t zeroed, uint32_t used, uint64_t* out);
+PTXSTD_API int ptxstd_zero_mask_with_sub_mask_start(uint64_t mask, uint32_t sub_mask, int first_span,
+                                                    uint32_t start_count, uint64_t* out);
+PTXSTD_API int ptxstd_zero_mask_with_column_shift(uint64_t mask, uint32_t shift, uint64_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PTXSTD_H */

@@ -1,0 +1,751 @@
+/*
+ * CPU ORACLE — test infrastructure only (see oracle.h for what pins each part).
+ *
+ * Every function restates the reference's documented semantics in plain C; the file:line cited
+ * beside each is the reference code it follows. Built by oracle/Makefile into
+ * oracle/_build/liboracle.so; loaded by tests/ and bench.py's CPU-baseline leg through ctypes.
+ */
+#define _GNU_SOURCE
+#include "oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+#include <unistd.h>
+
+/* ------------------------------------------------------------------------------------------ */
+/* small helpers                                                                              */
+/* ------------------------------------------------------------------------------------------ */
+
+static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+int ptxo_hardware_threads(void) {
+    long n = sysconf(_SC_NPROCESSORS_ONLN);
+    return n > 0 ? (int)n : 1;
+}
+
+/* Runs fn(ctx, lo, hi) over [0, n) split into contiguous ranges on `threads` threads. */
+typedef void (*range_fn)(void* ctx, uint64_t lo, uint64_t hi);
+typedef struct { range_fn fn; void* ctx; uint64_t lo, hi; } range_job;
+
+static void* range_tramp(void* p) {
+    range_job* j = (range_job*)p;
+    j->fn(j->ctx, j->lo, j->hi);
+    return NULL;
+}
+
+static void parallel_for(uint64_t n, int threads, range_fn fn, void* ctx) {
+    if (threads <= 0) threads = ptxo_hardware_threads();
+    if ((uint64_t)threads > n) threads = n ? (int)n : 1;
+    if (threads <= 1) { fn(ctx, 0, n); return; }
+    pthread_t* tid = (pthread_t*)malloc(sizeof(pthread_t) * threads);
+    range_job* jobs = (range_job*)malloc(sizeof(range_job) * threads);
+    uint64_t per = n / threads, extra = n % threads, lo = 0;
+    for (int t = 0; t < threads; ++t) {
+        uint64_t len = per + ((uint64_t)t < extra ? 1 : 0);
+        jobs[t].fn = fn; jobs[t].ctx = ctx; jobs[t].lo = lo; jobs[t].hi = lo + len;
+        lo += len;
+        pthread_create(&tid[t], NULL, range_tramp, &jobs[t]);
+    }
+    for (int t = 0; t < threads; ++t) pthread_join(tid[t], NULL);
+    free(tid); free(jobs);
+}
+
+/* ------------------------------------------------------------------------------------------ */
+/* decode                                                                                     */
+/* ------------------------------------------------------------------------------------------ */
+
+/* Restates minifloat_to_f32 (src/data_types/vector.rs:61-95): sign at bit exp+man, the largest
+ * exponent encodes specials for IEEE formats (and only with all mantissa bits set for NaN-only
+ * formats), exponent 0 is subnormal with scale 2^(1-bias). */
+float ptxo_minifloat_to_f32(uint8_t bits8, uint32_t exp_bits, uint32_t man_bits, int32_t bias,
+                            int specials) {
+    uint32_t bits = bits8;
+    int negative = (bits >> (exp_bits + man_bits)) & 1;
+    uint32_t e = (bits >> man_bits) & ((1u << exp_bits) - 1);
+    uint32_t m = bits & ((1u << man_bits) - 1);
+    uint32_t max_e = (1u << exp_bits) - 1, max_m = (1u << man_bits) - 1;
+    int special = 0;
+    if (e == max_e) {
+        if (specials == 1) special = 1;              /* IEEE */
+        else if (specials == 2) special = (m == max_m); /* NaN only */
+    }
+    float mag;
+    if (special) {
+        mag = (m == 0) ? INFINITY : NAN;
+    } else {
+        float frac = (e == 0) ? 0.0f : 1.0f;
+        int32_t se = (e == 0) ? (1 - bias) : ((int32_t)e - bias);
+        float scale = u2f((uint32_t)(se + 127) << 23);
+        mag = (frac + (float)m / (float)(1u << man_bits)) * scale;
+    }
+    return negative ? -mag : mag;
+}
+
+/* f8e4m3 decode: minifloat_to_f32(bits, 4, 3, 7, NanOnly) (src/data_types/float8.rs:20). */
+float ptxo_e4m3_to_f32(uint8_t b) { return ptxo_minifloat_to_f32(b, 4, 3, 7, 2); }
+/* f8e5m2 decode: minifloat_to_f32(bits, 5, 2, 15, Ieee) (src/data_types/float8.rs:79). */
+float ptxo_e5m2_to_f32(uint8_t b) { return ptxo_minifloat_to_f32(b, 5, 2, 15, 1); }
+/* f4e2m1 decode: minifloat_to_f32(bits, 2, 1, 1, None) (src/data_types/float4.rs:24). */
+float ptxo_e2m1_to_f32(uint8_t b) { return ptxo_minifloat_to_f32(b & 0xF, 2, 1, 1, 0); }
+
+/* f8e8m0 decode (src/data_types/float8.rs:148-152): 0xff NaN, 0 -> 2^-127, else bits << 23. */
+float ptxo_ue8m0_to_f32(uint8_t b) {
+    if (b == 0xFF) return NAN;
+    if (b == 0) return u2f(0x00400000u);
+    return u2f((uint32_t)b << 23);
+}
+
+/* The device's `to_f32` goes through f16 (`cvt.rn.f16x2.<fmt>x2`, then the exact widening;
+ * src/data_types/narrow.rs:292-299). Finite values are exact either way; a NaN code becomes the
+ * f16 canonical NaN 0x7fff, widened to f32 0x7fffe000 (the sign of the NaN is not kept). */
+float ptxo_to_f32_via_half(int format, uint8_t bits) {
+    float v;
+    switch (format) {
+    case PTXO_E4M3: v = ptxo_e4m3_to_f32(bits); break;
+    case PTXO_E5M2: v = ptxo_e5m2_to_f32(bits); break;
+    default: v = ptxo_e2m1_to_f32(bits); break;
+    }
+    if (v != v) return u2f(0x7FFFE000u);
+    return v;
+}
+
+/* ue8m0 `to_f32` goes through bf16 (`cvt.rn.bf16x2.ue8m0x2`, src/data_types/narrow.rs:683-690):
+ * NaN becomes the bf16 canonical NaN 0x7fff, widened to 0x7fff0000. */
+float ptxo_ue8m0_to_f32_via_bf16(uint8_t bits) {
+    if (bits == 0xFF) return u2f(0x7FFF0000u);
+    return ptxo_ue8m0_to_f32(bits);
+}
+
+/* ------------------------------------------------------------------------------------------ */
+/* encode                                                                                     */
+/* ------------------------------------------------------------------------------------------ */
+
+typedef struct {
+    int exp_bits, man_bits, bias;
+    uint32_t max_mag;  /* largest finite magnitude code */
+    uint8_t nan_code;  /* code written for a NaN input */
+    uint8_t sign_bit;
+} narrow_fmt;
+
+/* E4M3: max 0x7E = 448, NaN 0x7F (src/data_types/float8.rs:32-35). */
+static const narrow_fmt FMT_E4M3 = {4, 3, 7, 0x7E, 0x7F, 0x80};
+/* E5M2: max 0x7B = 57344 (src/data_types/float8.rs:96-99); NaN written as 0x7F. */
+static const narrow_fmt FMT_E5M2 = {5, 2, 15, 0x7B, 0x7F, 0x80};
+/* E2M1: max 0x7 = 6 (src/data_types/float4.rs:35-36); no NaN, so NaN becomes +max
+ * (src/data_types/narrow.rs:125-130). */
+static const narrow_fmt FMT_E2M1 = {2, 1, 1, 0x7, 0x7, 0x8};
+
+static inline const narrow_fmt* fmt_of(int format) {
+    return format == PTXO_E4M3 ? &FMT_E4M3 : format == PTXO_E5M2 ? &FMT_E5M2 : &FMT_E2M1;
+}
+
+/* Round-to-nearest-even of a finite, non-negative f32 (given as bits) to the magnitude code of
+ * the format, saturating to the largest finite code (.satfinite). Integer formulation: the
+ * 24-bit significand is shifted to the quantum of the target binade (or of the subnormal range),
+ * with ties to even, then re-encoded. */
+static inline uint32_t encode_mag(const narrow_fmt* f, uint32_t a) {
+    uint32_t e32 = a >> 23;
+    if (e32 == 0) return 0; /* zero or f32 subnormal: far below half the smallest subnormal */
+    uint32_t sig = (a & 0x7FFFFFu) | 0x800000u;
+    int e = (int)e32 - 127;
+    int emin = 1 - f->bias;
+    int te = e < emin ? emin : e;
+    int shift = 23 - f->man_bits + (te - e);
+    uint32_t n;
+    if (shift >= 26) {
+        n = 0; /* sig < 2^24 <= half a quantum */
+    } else {
+        n = sig >> shift;
+        uint32_t rem = sig & ((1u << shift) - 1);
+        uint32_t half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (n & 1))) n++;
+    }
+    uint32_t one = 1u << f->man_bits;
+    if (n >= (one << 1)) { te++; n >>= 1; }
+    uint32_t code;
+    if (te == emin && n < one) code = n;
+    else code = ((uint32_t)(te + f->bias) << f->man_bits) | (n - one);
+    if (code > f->max_mag) code = f->max_mag;
+    return code;
+}
+
+/* RN .satfinite [.relu] conversion of one f32 (src/data_types/narrow.rs:125-130): out-of-range
+ * values and infinities clamp to the largest finite value of matching sign; NaN becomes the
+ * format's NaN (FP8) or the largest positive value (FP4); RELU clamps negative results to +0. */
+static inline uint8_t encode_narrow(const narrow_fmt* f, float x, int relu) {
+    uint32_t u = f2u(x);
+    uint32_t a = u & 0x7FFFFFFFu;
+    if (a > 0x7F800000u) return f->nan_code;
+    uint8_t sign = (u >> 31) ? f->sign_bit : 0;
+    if (relu && sign) return 0;
+    uint32_t mag = (a == 0x7F800000u) ? f->max_mag : encode_mag(f, a);
+    return (uint8_t)(mag | sign);
+}
+
+uint8_t ptxo_f32_to_e4m3(float x, int relu) { return encode_narrow(&FMT_E4M3, x, relu); }
+uint8_t ptxo_f32_to_e5m2(float x, int relu) { return encode_narrow(&FMT_E5M2, x, relu); }
+uint8_t ptxo_f32_to_e2m1(float x, int relu) { return encode_narrow(&FMT_E2M1, x, relu); }
+uint8_t ptxo_f32_to_narrow(int format, float x, int relu) {
+    return encode_narrow(fmt_of(format), x, relu);
+}
+
+/* ue8m0 encode (src/data_types/narrow.rs:585-593, :600-617): the format holds only powers of
+ * two, so RZ keeps the f32 exponent and RP bumps it when any mantissa bit is set; NaN -> 0xff;
+ * with .satfinite, overflow (and infinity) clamp to 0xfe = 2^127, without it they give 0xff.
+ * Values below 2^-127 (including zero) give the smallest code 0 under RZ; under RP everything in
+ * (0, 2^-127] gives 0 and (2^-127, 2^-126) gives 1. The sign is ignored (unsigned format). */
+uint8_t ptxo_f32_to_ue8m0(float x, int rnd_up, int satfinite) {
+    uint32_t a = f2u(x) & 0x7FFFFFFFu;
+    if (a > 0x7F800000u) return 0xFF;
+    if (a == 0x7F800000u) return satfinite ? 0xFE : 0xFF;
+    uint32_t e = a >> 23, m = a & 0x7FFFFFu;
+    if (e == 0) {
+        if (!rnd_up) return 0;
+        return (m > 0x400000u) ? 1 : 0;
+    }
+    uint32_t code = e + ((rnd_up && m) ? 1u : 0u);
+    if (code >= 0xFF) return satfinite ? 0xFE : 0xFF;
+    return (uint8_t)code;
+}
+
+/* bf16 RNE from f32 (src/data_types/bfloat16.rs:104-118); NaN keeps its sign and becomes quiet. */
+uint16_t ptxo_f32_to_bf16(float x) {
+    uint32_t u = f2u(x);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((u >> 16) | 0x40);
+    uint32_t lsb = (u >> 16) & 1;
+    u += 0x7FFFu + lsb;
+    return (uint16_t)(u >> 16);
+}
+float ptxo_bf16_to_f32(uint16_t h) { return u2f((uint32_t)h << 16); }
+
+/* ------------------------------------------------------------------------------------------ */
+/* bulk conversions                                                                           */
+/* ------------------------------------------------------------------------------------------ */
+
+typedef struct { int format, relu; const float* x; uint8_t* out; } enc_ctx;
+
+static void enc_range(void* p, uint64_t lo, uint64_t hi) {
+    enc_ctx* c = (enc_ctx*)p;
+    const narrow_fmt* f = fmt_of(c->format);
+    if (c->format == PTXO_E2M1) {
+        /* lo/hi count bytes (pairs); element 0 in the low nibble (src/data_types/float4.rs:5-6). */
+        for (uint64_t i = lo; i < hi; ++i) {
+            uint8_t l = encode_narrow(f, c->x[2 * i], c->relu);
+            uint8_t h = encode_narrow(f, c->x[2 * i + 1], c->relu);
+            c->out[i] = (uint8_t)(l | (h << 4));
+        }
+    } else {
+        for (uint64_t i = lo; i < hi; ++i) c->out[i] = encode_narrow(f, c->x[i], c->relu);
+    }
+}
+
+void ptxo_encode_array(int format, const float* x, uint8_t* out, size_t n, int relu,
+                       int threads) {
+    enc_ctx c = {format, relu, x, out};
+    parallel_for(format == PTXO_E2M1 ? n / 2 : n, threads, enc_range, &c);
+}
+
+typedef struct { int format; const uint8_t* codes; float* out; } dec_ctx;
+
+static void dec_range(void* p, uint64_t lo, uint64_t hi) {
+    dec_ctx* c = (dec_ctx*)p;
+    if (c->format == PTXO_E2M1) {
+        for (uint64_t i = lo; i < hi; ++i) {
+            c->out[2 * i] = ptxo_to_f32_via_half(PTXO_E2M1, c->codes[i] & 0xF);
+            c->out[2 * i + 1] = ptxo_to_f32_via_half(PTXO_E2M1, c->codes[i] >> 4);
+        }
+    } else {
+        for (uint64_t i = lo; i < hi; ++i) c->out[i] = ptxo_to_f32_via_half(c->format, c->codes[i]);
+    }
+}
+
+void ptxo_decode_array(int format, const uint8_t* codes, float* out, size_t n, int threads) {
+    dec_ctx c = {format, codes, out};
+    parallel_for(format == PTXO_E2M1 ? n / 2 : n, threads, dec_range, &c);
+}
+
+typedef struct { const float* x; uint8_t* out; int up, sat; } ue_ctx;
+
+static void ue_range(void* p, uint64_t lo, uint64_t hi) {
+    ue_ctx* c = (ue_ctx*)p;
+    for (uint64_t i = lo; i < hi; ++i) c->out[i] = ptxo_f32_to_ue8m0(c->x[i], c->up, c->sat);
+}
+
+void ptxo_ue8m0_encode_array(const float* x, uint8_t* out, size_t n, int rnd_up, int satfinite,
+                             int threads) {
+    ue_ctx c = {x, out, rnd_up, satfinite};
+    parallel_for(n, threads, ue_range, &c);
+}
+
+/* ------------------------------------------------------------------------------------------ */
+/* exhaustive sweep support                                                                   */
+/* ------------------------------------------------------------------------------------------ */
+
+uint8_t ptxo_encode_variant(int variant, float x) {
+    switch (variant) {
+    case PTXO_V_E4M3: return encode_narrow(&FMT_E4M3, x, 0);
+    case PTXO_V_E5M2: return encode_narrow(&FMT_E5M2, x, 0);
+    case PTXO_V_E2M1: return encode_narrow(&FMT_E2M1, x, 0);
+    case PTXO_V_E4M3_RELU: return encode_narrow(&FMT_E4M3, x, 1);
+    case PTXO_V_E5M2_RELU: return encode_narrow(&FMT_E5M2, x, 1);
+    case PTXO_V_E2M1_RELU: return encode_narrow(&FMT_E2M1, x, 1);
+    case PTXO_V_UE8M0_RZ: return ptxo_f32_to_ue8m0(x, 0, 1);
+    default: return ptxo_f32_to_ue8m0(x, 1, 1);
+    }
+}
+
+typedef struct {
+    int variant; uint64_t base; const uint8_t* dev;
+    uint32_t* report; uint64_t max_report;
+    uint64_t mismatches; pthread_mutex_t mu;
+} sweep_ctx;
+
+static void sweep_range(void* p, uint64_t lo, uint64_t hi) {
+    sweep_ctx* c = (sweep_ctx*)p;
+    uint64_t local = 0;
+    for (uint64_t i = lo; i < hi; ++i) {
+        uint32_t bits = (uint32_t)(c->base + i);
+        uint8_t want = ptxo_encode_variant(c->variant, u2f(bits));
+        uint8_t got = c->dev[i];
+        if (want != got) {
+            pthread_mutex_lock(&c->mu);
+            if (c->mismatches < c->max_report && c->report) {
+                c->report[3 * c->mismatches] = bits;
+                c->report[3 * c->mismatches + 1] = got;
+                c->report[3 * c->mismatches + 2] = want;
+            }
+            c->mismatches++;
+            pthread_mutex_unlock(&c->mu);
+            local++;
+        }
+    }
+    (void)local;
+}
+
+uint64_t ptxo_sweep_compare(int variant, uint64_t base, uint64_t n, const uint8_t* device_out,
+                            uint32_t* report, uint64_t max_report, int threads) {
+    sweep_ctx c;
+    c.variant = variant; c.base = base; c.dev = device_out; c.report = report;
+    c.max_report = max_report; c.mismatches = 0;
+    pthread_mutex_init(&c.mu, NULL);
+    parallel_for(n, threads, sweep_range, &c);
+    pthread_mutex_destroy(&c.mu);
+    return c.mismatches;
+}
+
+#define FNV_OFFSET 0xcbf29ce484222325ull
+#define FNV_PRIME 0x100000001b3ull
+
+uint64_t ptxo_fnv1a64(const uint8_t* data, size_t n, uint64_t seed) {
+    uint64_t h = seed ? seed : FNV_OFFSET;
+    for (size_t i = 0; i < n; ++i) { h ^= data[i]; h *= FNV_PRIME; }
+    return h;
+}
+
+typedef struct { int variant; uint64_t base; uint64_t* part; uint64_t chunk; } dig_ctx;
+
+static void dig_range(void* p, uint64_t lo, uint64_t hi) {
+    dig_ctx* c = (dig_ctx*)p;
+    for (uint64_t k = lo; k < hi; ++k) {
+        uint64_t h = FNV_OFFSET;
+        uint64_t b0 = c->base + k * c->chunk;
+        for (uint64_t i = 0; i < c->chunk; ++i) {
+            h ^= ptxo_encode_variant(c->variant, u2f((uint32_t)(b0 + i)));
+            h *= FNV_PRIME;
+        }
+        c->part[k] = h;
+    }
+}
+
+/* Digest of [base, base + n): FNV-1a 64 of each 2^16-input piece, then FNV-1a 64 over those
+ * digests' little-endian bytes (so that the pieces can be hashed in parallel). n must be a
+ * multiple of 2^16. */
+uint64_t ptxo_sweep_digest(int variant, uint64_t base, uint64_t n, int threads) {
+    const uint64_t chunk = 1u << 16;
+    uint64_t parts = n / chunk;
+    uint64_t* part = (uint64_t*)malloc(sizeof(uint64_t) * (parts ? parts : 1));
+    dig_ctx c = {variant, base, part, chunk};
+    parallel_for(parts, threads, dig_range, &c);
+    uint64_t h = ptxo_fnv1a64((const uint8_t*)part, parts * 8, 0);
+    free(part);
+    return h;
+}
+
+typedef struct { const uint8_t* data; uint64_t* part; uint64_t chunk; } digb_ctx;
+
+static void digb_range(void* p, uint64_t lo, uint64_t hi) {
+    digb_ctx* c = (digb_ctx*)p;
+    for (uint64_t k = lo; k < hi; ++k) c->part[k] = ptxo_fnv1a64(c->data + k * c->chunk, c->chunk, 0);
+}
+
+/* The same digest scheme as ptxo_sweep_digest, over given bytes (n a multiple of 2^16). */
+uint64_t ptxo_digest_bytes(const uint8_t* data, uint64_t n, int threads) {
+    const uint64_t chunk = 1u << 16;
+    uint64_t parts = n / chunk;
+    uint64_t* part = (uint64_t*)malloc(sizeof(uint64_t) * (parts ? parts : 1));
+    digb_ctx c = {data, part, chunk};
+    parallel_for(parts, threads, digb_range, &c);
+    uint64_t h = ptxo_fnv1a64((const uint8_t*)part, parts * 8, 0);
+    free(part);
+    return h;
+}
+
+/* ------------------------------------------------------------------------------------------ */
+/* block-scale recipes                                                                        */
+/* ------------------------------------------------------------------------------------------ */
+
+/* NaN-propagating max of |x| over a block (the `.NaN` form of redux.sync.max.abs.f32,
+ * src/warp_collectives.rs:679-700). */
+static inline float block_amax(const float* x, int n) {
+    float m = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        float a = fabsf(x[i]);
+        if (a != a) return a;
+        if (a > m) m = a;
+    }
+    return m;
+}
+
+/* 2^-(code-127) as an f32 (exact: 2^127 .. 2^-127, the last an f32 subnormal). */
+static inline float ue8m0_inverse(uint8_t code) {
+    if (code == 0xFF) return NAN;
+    int e = 127 - (int)code; /* -127 .. 127 */
+    if (e >= -126) return u2f((uint32_t)(e + 127) << 23);
+    return u2f(0x00400000u); /* 2^-127 */
+}
+
+/* MXFP8 scale of one 32-block: u = f8e8m0::from_f32::<TowardZero, SaturateFinite>(amax)
+ * (src/data_types/narrow.rs:600-617), minus E4M3's emax 8, clamped at 0; NaN stays NaN. */
+uint8_t ptxo_mxfp8_block(const float* x32, uint8_t* q32) {
+    float amax = block_amax(x32, 32);
+    uint8_t u = ptxo_f32_to_ue8m0(amax, 0, 1);
+    uint8_t code = (u == 0xFF) ? 0xFF : (u > 8 ? (uint8_t)(u - 8) : 0);
+    float inv = ue8m0_inverse(code);
+    for (int i = 0; i < 32; ++i) q32[i] = encode_narrow(&FMT_E4M3, x32[i] * inv, 0);
+    return code;
+}
+
+/* NVFP4 block of 16: sf = e4m3_rn_satfinite(amax / (6 g)); r = 1 / (sf g) (0 when sf g == 0);
+ * q = e2m1_rn_satfinite(x r). All f32 operations are single IEEE roundings. */
+uint8_t ptxo_nvfp4_block(const float* x16, float g, uint8_t* q16) {
+    float amax = block_amax(x16, 16);
+    float six_g = 6.0f * g;
+    float s = amax / six_g;
+    uint8_t sf = encode_narrow(&FMT_E4M3, s, 0);
+    float t = ptxo_e4m3_to_f32(sf) * g;
+    float r = (t == 0.0f) ? 0.0f : 1.0f / t;
+    for (int i = 0; i < 16; ++i) q16[i] = encode_narrow(&FMT_E2M1, x16[i] * r, 0);
+    return sf;
+}
+
+typedef struct {
+    const uint16_t* x; int64_t cols; uint8_t* q; uint8_t* sf; float g;
+} quant_ctx;
+
+static void mxfp8_rows(void* p, uint64_t lo, uint64_t hi) {
+    quant_ctx* c = (quant_ctx*)p;
+    float buf[32];
+    for (uint64_t r = lo; r < hi; ++r) {
+        const uint16_t* xr = c->x + r * c->cols;
+        for (int64_t b = 0; b < c->cols / 32; ++b) {
+            for (int i = 0; i < 32; ++i) buf[i] = ptxo_bf16_to_f32(xr[b * 32 + i]);
+            c->sf[r * (c->cols / 32) + b] = ptxo_mxfp8_block(buf, c->q + r * c->cols + b * 32);
+        }
+    }
+}
+
+void ptxo_quantize_mxfp8(const uint16_t* x, int64_t rows, int64_t cols, uint8_t* q, uint8_t* sf,
+                         int threads) {
+    quant_ctx c = {x, cols, q, sf, 0.0f};
+    parallel_for((uint64_t)rows, threads, mxfp8_rows, &c);
+}
+
+static void nvfp4_rows(void* p, uint64_t lo, uint64_t hi) {
+    quant_ctx* c = (quant_ctx*)p;
+    float buf[16];
+    uint8_t nib[16];
+    for (uint64_t r = lo; r < hi; ++r) {
+        const uint16_t* xr = c->x + r * c->cols;
+        uint8_t* qr = c->q + r * (c->cols / 2);
+        for (int64_t b = 0; b < c->cols / 16; ++b) {
+            for (int i = 0; i < 16; ++i) buf[i] = ptxo_bf16_to_f32(xr[b * 16 + i]);
+            c->sf[r * (c->cols / 16) + b] = ptxo_nvfp4_block(buf, c->g, nib);
+            for (int i = 0; i < 8; ++i) qr[b * 8 + i] = (uint8_t)(nib[2 * i] | (nib[2 * i + 1] << 4));
+        }
+    }
+}
+
+int ptxo_quantize_nvfp4(const uint16_t* x, int64_t rows, int64_t cols, float g, uint8_t* q,
+                        uint8_t* sf, int threads) {
+    if (!(g > 0.0f) || isinf(g)) return -1;
+    quant_ctx c = {x, cols, q, sf, g};
+    parallel_for((uint64_t)rows, threads, nvfp4_rows, &c);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------------------------ */
+/* GEMM references                                                                            */
+/* ------------------------------------------------------------------------------------------ */
+
+typedef struct {
+    const uint8_t *A, *B, *sfA, *sfB, *W, *sfW;
+    const uint16_t* x;
+    float sa, sb, ga, gb, gw;
+    int64_t M, N, K;
+    const int64_t *rows, *cols;
+    double *ref, *mag;
+} gemm_ctx;
+
+static void fp8_samples(void* p, uint64_t lo, uint64_t hi) {
+    gemm_ctx* c = (gemm_ctx*)p;
+    double lut[256];
+    for (int i = 0; i < 256; ++i) lut[i] = ptxo_e4m3_to_f32((uint8_t)i);
+    for (uint64_t s = lo; s < hi; ++s) {
+        const uint8_t* a = c->A + c->rows[s] * c->K;
+        const uint8_t* b = c->B + c->cols[s] * c->K;
+        double acc = 0, mag = 0;
+        for (int64_t k = 0; k < c->K; ++k) {
+            double t = lut[a[k]] * lut[b[k]];
+            acc += t; mag += fabs(t);
+        }
+        double sc = (double)c->sa * (double)c->sb;
+        c->ref[s] = acc * sc; c->mag[s] = mag * fabs(sc);
+    }
+}
+
+void ptxo_gemm_fp8_ref(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K,
+                       float sa, float sb, const int64_t* rows, const int64_t* cols,
+                       int64_t n_samples, double* ref, double* mag, int threads) {
+    gemm_ctx c; memset(&c, 0, sizeof c);
+    c.A = A; c.B = B; c.M = M; c.N = N; c.K = K; c.sa = sa; c.sb = sb;
+    c.rows = rows; c.cols = cols; c.ref = ref; c.mag = mag;
+    parallel_for((uint64_t)n_samples, threads, fp8_samples, &c);
+}
+
+static inline double nvfp4_elem(const uint8_t* q, const uint8_t* sf, int64_t k) {
+    uint8_t byte = q[k >> 1];
+    uint8_t nib = (k & 1) ? (byte >> 4) : (byte & 0xF);
+    return (double)ptxo_e2m1_to_f32(nib) * (double)ptxo_e4m3_to_f32(sf[k >> 4]);
+}
+
+static void nvfp4_samples(void* p, uint64_t lo, uint64_t hi) {
+    gemm_ctx* c = (gemm_ctx*)p;
+    for (uint64_t s = lo; s < hi; ++s) {
+        const uint8_t* a = c->A + c->rows[s] * (c->K / 2);
+        const uint8_t* sa = c->sfA + c->rows[s] * (c->K / 16);
+        const uint8_t* b = c->B + c->cols[s] * (c->K / 2);
+        const uint8_t* sb = c->sfB + c->cols[s] * (c->K / 16);
+        double acc = 0, mag = 0;
+        for (int64_t k = 0; k < c->K; ++k) {
+            double t = nvfp4_elem(a, sa, k) * nvfp4_elem(b, sb, k);
+            acc += t; mag += fabs(t);
+        }
+        double g = (double)c->ga * (double)c->gb;
+        c->ref[s] = acc * g; c->mag[s] = mag * fabs(g);
+    }
+}
+
+void ptxo_gemm_nvfp4_ref(const uint8_t* A, const uint8_t* sfA, float ga, const uint8_t* B,
+                         const uint8_t* sfB, float gb, int64_t M, int64_t N, int64_t K,
+                         const int64_t* rows, const int64_t* cols, int64_t n_samples, double* ref,
+                         double* mag, int threads) {
+    gemm_ctx c; memset(&c, 0, sizeof c);
+    c.A = A; c.sfA = sfA; c.ga = ga; c.B = B; c.sfB = sfB; c.gb = gb;
+    c.M = M; c.N = N; c.K = K; c.rows = rows; c.cols = cols; c.ref = ref; c.mag = mag;
+    parallel_for((uint64_t)n_samples, threads, nvfp4_samples, &c);
+}
+
+static void decode_samples(void* p, uint64_t lo, uint64_t hi) {
+    gemm_ctx* c = (gemm_ctx*)p;
+    int64_t K = c->K;
+    float* xf = (float*)malloc(sizeof(float) * K);
+    double* xv = (double*)malloc(sizeof(double) * K);
+    uint8_t q32[32];
+    int64_t cur_row = -1;
+    for (uint64_t s = lo; s < hi; ++s) {
+        int64_t i = c->rows[s];
+        if (i != cur_row) {
+            for (int64_t k = 0; k < K; ++k) xf[k] = ptxo_bf16_to_f32(c->x[i * K + k]);
+            for (int64_t b = 0; b < K / 32; ++b) {
+                uint8_t code = ptxo_mxfp8_block(xf + b * 32, q32);
+                double scale = (double)ptxo_ue8m0_to_f32(code);
+                for (int j = 0; j < 32; ++j) xv[b * 32 + j] = (double)ptxo_e4m3_to_f32(q32[j]) * scale;
+            }
+            cur_row = i;
+        }
+        const uint8_t* w = c->W + c->cols[s] * (K / 2);
+        const uint8_t* sw = c->sfW + c->cols[s] * (K / 16);
+        double acc = 0, mag = 0;
+        for (int64_t k = 0; k < K; ++k) {
+            double t = xv[k] * nvfp4_elem(w, sw, k);
+            acc += t; mag += fabs(t);
+        }
+        c->ref[s] = acc * (double)c->gw; c->mag[s] = mag * fabs((double)c->gw);
+    }
+    free(xf); free(xv);
+}
+
+void ptxo_gemm_decode_ref(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float gw,
+                          int64_t M, int64_t N, int64_t K, const int64_t* rows,
+                          const int64_t* cols, int64_t n_samples, double* ref, double* mag,
+                          int threads) {
+    gemm_ctx c; memset(&c, 0, sizeof c);
+    c.x = x; c.W = W; c.sfW = sfW; c.gw = gw; c.M = M; c.N = N; c.K = K;
+    c.rows = rows; c.cols = cols; c.ref = ref; c.mag = mag;
+    parallel_for((uint64_t)n_samples, threads, decode_samples, &c);
+}
+
+/* Cache-blocked C = A * B^T in f32 for the timed CPU baseline. Rows of C are split across
+ * threads; within a thread, blocks of 64 columns x 256 K keep B's panel in cache and 4 rows of A
+ * are processed per pass. */
+typedef struct { const float *A, *B; float* C; int64_t M, N, K; } sg_ctx;
+
+static void sgemm_rows(void* p, uint64_t lo, uint64_t hi) {
+    sg_ctx* c = (sg_ctx*)p;
+    const int64_t NB = 64, KB = 256;
+    for (uint64_t i = lo; i < hi; ++i)
+        for (int64_t j = 0; j < c->N; ++j) c->C[i * c->N + j] = 0.0f;
+    for (int64_t j0 = 0; j0 < c->N; j0 += NB) {
+        int64_t j1 = j0 + NB < c->N ? j0 + NB : c->N;
+        for (int64_t k0 = 0; k0 < c->K; k0 += KB) {
+            int64_t k1 = k0 + KB < c->K ? k0 + KB : c->K;
+            for (uint64_t i = lo; i < hi; ++i) {
+                const float* a = c->A + i * c->K;
+                for (int64_t j = j0; j < j1; ++j) {
+                    const float* b = c->B + j * c->K;
+                    float acc = 0.0f;
+                    for (int64_t k = k0; k < k1; ++k) acc += a[k] * b[k];
+                    c->C[i * c->N + j] += acc;
+                }
+            }
+        }
+    }
+}
+
+void ptxo_sgemm_nt(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                   int threads) {
+    sg_ctx c = {A, B, C, M, N, K};
+    parallel_for((uint64_t)M, threads, sgemm_rows, &c);
+}
+
+/* ------------------------------------------------------------------------------------------ */
+/* tcgen05 descriptors (src/tcgen05/descriptor.rs)                                            */
+/* ------------------------------------------------------------------------------------------ */
+
+/* encode_n: N a multiple of 8 in [8, 256], at bits 17..23 as N >> 3 (descriptor.rs:450-457). */
+static int enc_n(uint32_t n, uint32_t* f) {
+    if (n % 8 || n < 8 || n > 256) return -1;
+    *f = (n >> 3) << 17; return 0;
+}
+/* encode_m: M a multiple of 16 in [16, 256], at bits 24..29 as M >> 4 (descriptor.rs:460-467). */
+static int enc_m(uint32_t m, uint32_t* f) {
+    if (m % 16 || m < 16 || m > 256) return -1;
+    *f = (m >> 4) << 24; return 0;
+}
+/* encode_m_block_scaled: M 128 or 256, at bits 27..29 as M >> 7 (descriptor.rs:470-476). */
+static int enc_m_bs(uint32_t m, uint32_t* f) {
+    if (m != 128 && m != 256) return -1;
+    *f = (m >> 7) << 27; return 0;
+}
+
+/* F16 / F8f6f4: d << 4 | a << 7 | b << 10 | N | M (descriptor.rs:520-527, :555-564). */
+int ptxo_idesc_f16(int a, int b, int d, uint32_t m, uint32_t n, uint32_t* out) {
+    uint32_t fm, fn;
+    if (enc_m(m, &fm) || enc_n(n, &fn)) return -1;
+    *out = ((uint32_t)d << 4) | ((uint32_t)a << 7) | ((uint32_t)b << 10) | fn | fm;
+    return 0;
+}
+int ptxo_idesc_f8f6f4(int a, int b, int d, uint32_t m, uint32_t n, uint32_t* out) {
+    return ptxo_idesc_f16(a, b, d, m, n, out);
+}
+/* Tf32: D f32 (1 << 4), A and B tf32 (2 << 7, 2 << 10) (descriptor.rs:537-541). */
+int ptxo_idesc_tf32(uint32_t m, uint32_t n, uint32_t* out) {
+    return ptxo_idesc_f16(2, 2, 1, m, n, out);
+}
+/* I8: D s32 (2 << 4) (descriptor.rs:575-578). */
+int ptxo_idesc_i8(int a, int b, uint32_t m, uint32_t n, uint32_t* out) {
+    return ptxo_idesc_f16(a, b, 2, m, n, out);
+}
+/* Mxf8f6f4: a << 7 | b << 10 | ue8m0 scales (1 << 23) | N | M>>7<<27 (descriptor.rs:601-611). */
+int ptxo_idesc_mxf8f6f4(int a, int b, uint32_t m, uint32_t n, uint32_t* out) {
+    uint32_t fm, fn;
+    if (enc_m_bs(m, &fm) || enc_n(n, &fn)) return -1;
+    *out = ((uint32_t)a << 7) | ((uint32_t)b << 10) | (1u << 23) | fn | fm;
+    return 0;
+}
+/* Mxf4: e2m1 A and B (1 << 7, 1 << 10), ue8m0 scales (1 << 23) (descriptor.rs:625-628). */
+int ptxo_idesc_mxf4(uint32_t m, uint32_t n, uint32_t* out) {
+    return ptxo_idesc_mxf8f6f4(1, 1, m, n, out);
+}
+/* Mxf4nvf4: e2m1 A and B, scale type << 23 (ue4m3 0, ue8m0 1, ue5m3 2) (descriptor.rs:644-653). */
+int ptxo_idesc_mxf4nvf4(int scale_type, uint32_t m, uint32_t n, uint32_t* out) {
+    uint32_t fm, fn;
+    if (scale_type < 0 || scale_type > 2) return -1;
+    if (enc_m_bs(m, &fm) || enc_n(n, &fn)) return -1;
+    *out = (1u << 7) | (1u << 10) | ((uint32_t)scale_type << 23) | fn | fm;
+    return 0;
+}
+/* with_field (descriptor.rs:494-498): the value must fit in the field. */
+int ptxo_idesc_with_field(uint32_t desc, uint32_t shift, uint32_t width, uint32_t value,
+                          uint32_t* out) {
+    if (width == 0 || width > 31 || shift + width > 32) return -1;
+    if (value >= (1u << width)) return -1;
+    uint32_t mask = ((1u << width) - 1) << shift;
+    *out = (desc & ~mask) | (value << shift);
+    return 0;
+}
+
+/* encode_smem_offset: multiple of 16, at most 0x3FFFF, stored >> 4 (descriptor.rs:100-108). */
+static int enc_off(uint32_t bytes, uint64_t* f) {
+    if (bytes % 16 || bytes > 0x3FFFF) return -1;
+    *f = bytes >> 4; return 0;
+}
+
+/* from_shared_address (descriptor.rs:152-162): start bits 4..17 at 0, LBO >> 4 at 16, SBO >> 4
+ * at 32, the constant 0b001 at 46, swizzle code at 61 (Swizzle codes 0, 1, 2, 4, 6). */
+int ptxo_smem_desc(uint32_t start, uint32_t lbo, uint32_t sbo, int swizzle, uint64_t* out) {
+    uint64_t l, s;
+    if (!(swizzle == 0 || swizzle == 1 || swizzle == 2 || swizzle == 4 || swizzle == 6)) return -1;
+    if (enc_off(lbo, &l) || enc_off(sbo, &s)) return -1;
+    uint64_t st = (uint64_t)((start & 0x3FFFFu) >> 4);
+    *out = st | (l << 16) | (s << 32) | (1ull << 46) | ((uint64_t)swizzle << 61);
+    return 0;
+}
+/* with_base_offset (descriptor.rs:176-183): 3 bits at 49; not with the absolute LBO mode. */
+int ptxo_smem_desc_with_base_offset(uint64_t desc, uint32_t base_offset, uint64_t* out) {
+    if (base_offset >= 8) return -1;
+    if (base_offset != 0 && (desc & (1ull << 52))) return -1;
+    *out = (desc & ~(7ull << 49)) | ((uint64_t)base_offset << 49);
+    return 0;
+}
+/* add_start_bytes (descriptor.rs:231-237): a 64-bit add of bytes >> 4. */
+int ptxo_smem_desc_add_start_bytes(uint64_t desc, uint32_t bytes, uint64_t* out) {
+    if (bytes % 16) return -1;
+    *out = desc + (uint64_t)(bytes >> 4);
+    return 0;
+}
+
+/* ZeroColumnMask::new (descriptor.rs:870-883): enable bit 39, zeroed-1 at 40, used-1 at 48. */
+int ptxo_zero_mask_new(uint32_t zeroed, uint32_t used, uint64_t* out) {
+    if (zeroed < 1 || zeroed > 256 || used < 1 || used > 256) return -1;
+    *out = (1ull << 39) | ((uint64_t)(zeroed - 1) << 40) | ((uint64_t)(used - 1) << 48);
+    return 0;
+}
+/* with_sub_mask_start (descriptor.rs:891-909): count at 8*sub, first span at 32+sub. */
+int ptxo_zero_mask_with_sub_mask_start(uint64_t mask, uint32_t sub, int first_span,
+                                       uint32_t start_count, uint64_t* out) {
+    if (sub >= 4 || start_count >= 256 || (first_span != 0 && first_span != 1)) return -1;
+    uint32_t cs = 8 * sub, ss = 32 + sub;
+    *out = (mask & ~((0xFFull << cs) | (1ull << ss))) | ((uint64_t)start_count << cs) |
+           ((uint64_t)first_span << ss);
+    return 0;
+}
+/* with_column_shift (descriptor.rs:917-921): 6 bits at 56, at most 32. */
+int ptxo_zero_mask_with_column_shift(uint64_t mask, uint32_t shift, uint64_t* out) {
+    if (shift > 32) return -1;
+    *out = (mask & ~(0x3Full << 56)) | ((uint64_t)shift << 56);
+    return 0;
+}

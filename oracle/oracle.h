@@ -1,0 +1,154 @@
+/*
+ * CPU ORACLE — test infrastructure only.
+ *
+ * A plain-C restatement of caelunshun/ptx-std's narrow-float semantics, of the block-scale
+ * recipes built on them, of its tcgen05 descriptor encodings, and an f64 GEMM over decoded
+ * values. Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may load it, and
+ * only as the checker (or as the timed CPU baseline). Nothing in the product links it.
+ *
+ * Parity pins:
+ *   - descriptor encoders: the reference's compile-time known answers
+ *     (examples/tcgen05_ptxas/descriptor.rs:22-234), extracted to tests/golden/;
+ *   - decode: the reference's named bit-pattern constants (src/data_types/float8.rs:22-41,
+ *     :80-103, :153-162; src/data_types/float4.rs:26-42);
+ *   - encode: the reference's encoders are the hardware `cvt` instructions (the core::arch::nvptx
+ *     intrinsics of the rustc fork `nvptx-ext`, src/data_types/narrow.rs:156-182, :600-646), so
+ *     they are pinned by running those same instructions over all 2^32 f32 inputs on a B200 and
+ *     committing per-chunk digests of the outputs (tests/golden/cvt_sweep_digests.json).
+ */
+#ifndef PTXSTD_ORACLE_H
+#define PTXSTD_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- formats ------------------------------------------------------------------------------ */
+enum ptxo_format {
+    PTXO_E4M3 = 0, /* FP8 E4M3, NaN-only specials, max 448 (src/data_types/float8.rs:13-42) */
+    PTXO_E5M2 = 1, /* FP8 E5M2, IEEE specials, max 57344 (src/data_types/float8.rs:70-133) */
+    PTXO_E2M1 = 2, /* FP4 E2M1, no specials, max 6 (src/data_types/float4.rs:14-43) */
+};
+
+/* Exact soft decode (src/data_types/vector.rs:61-95). specials: 0 none, 1 IEEE, 2 NaN-only. */
+float ptxo_minifloat_to_f32(uint8_t bits, uint32_t exp_bits, uint32_t man_bits, int32_t bias,
+                            int specials);
+float ptxo_e4m3_to_f32(uint8_t bits);
+float ptxo_e5m2_to_f32(uint8_t bits);
+float ptxo_e2m1_to_f32(uint8_t nibble);
+/* UE8M0 decode, 2^(b-127), 0xff NaN (src/data_types/float8.rs:148-152). */
+float ptxo_ue8m0_to_f32(uint8_t bits);
+
+/* Decode as the device `to_f32` does it: through f16 (or bf16 for ue8m0), then widened
+ * (src/data_types/narrow.rs:292-299, :683-690). Differs from the soft decode only in NaN bits. */
+float ptxo_to_f32_via_half(int format, uint8_t bits);
+float ptxo_ue8m0_to_f32_via_bf16(uint8_t bits);
+
+/* Round-to-nearest-even, .satfinite, optional .relu encode of one f32
+ * (src/data_types/narrow.rs:125-130 for the semantics). */
+uint8_t ptxo_f32_to_e4m3(float x, int relu);
+uint8_t ptxo_f32_to_e5m2(float x, int relu);
+uint8_t ptxo_f32_to_e2m1(float x, int relu); /* returns a nibble */
+uint8_t ptxo_f32_to_narrow(int format, float x, int relu);
+/* UE8M0 encode, rounding toward zero (rnd_up = 0) or toward +inf (rnd_up = 1), with or without
+ * .satfinite (src/data_types/narrow.rs:585-593, :600-617). */
+uint8_t ptxo_f32_to_ue8m0(float x, int rnd_up, int satfinite);
+
+/* bf16 helpers (src/data_types/bfloat16.rs:76-86): RNE f32 -> bf16 and the exact widening. */
+uint16_t ptxo_f32_to_bf16(float x);
+float ptxo_bf16_to_f32(uint16_t h);
+
+/* ---- bulk conversions (multithreaded; threads <= 0 means all hardware threads) ------------- */
+/* Element i of x -> out[i] (one code per byte for FP8; packed 2 per byte, element 0 in the low
+ * nibble, for E2M1 when format == PTXO_E2M1 and n is even). */
+void ptxo_encode_array(int format, const float* x, uint8_t* out, size_t n, int relu, int threads);
+void ptxo_decode_array(int format, const uint8_t* codes, float* out, size_t n, int threads);
+void ptxo_ue8m0_encode_array(const float* x, uint8_t* out, size_t n, int rnd_up, int satfinite,
+                             int threads);
+
+/* Sweep of the f32 bit patterns [base, base + n): encodes every pattern (variant selects
+ * format/relu or the ue8m0 rounding) and compares with `device_out`, the device's codes for the
+ * same inputs (one byte per input; E2M1 nibbles unpacked). Returns the number of mismatches and
+ * stores up to max_report of them as (input bits, device code, oracle code) triples. */
+enum ptxo_variant {
+    PTXO_V_E4M3 = 0, PTXO_V_E5M2 = 1, PTXO_V_E2M1 = 2,
+    PTXO_V_E4M3_RELU = 3, PTXO_V_E5M2_RELU = 4, PTXO_V_E2M1_RELU = 5,
+    PTXO_V_UE8M0_RZ = 6, PTXO_V_UE8M0_RP = 7,
+};
+uint8_t ptxo_encode_variant(int variant, float x);
+uint64_t ptxo_sweep_compare(int variant, uint64_t base, uint64_t n, const uint8_t* device_out,
+                            uint32_t* report, uint64_t max_report, int threads);
+/* FNV-1a 64 digest of the oracle's codes for inputs [base, base + n) of a variant (one byte per
+ * input, in input order). Used to check the oracle against digests of the hardware's codes. */
+uint64_t ptxo_sweep_digest(int variant, uint64_t base, uint64_t n, int threads);
+uint64_t ptxo_fnv1a64(const uint8_t* data, size_t n, uint64_t seed);
+/* The same digest scheme over given bytes (n a multiple of 2^16). */
+uint64_t ptxo_digest_bytes(const uint8_t* data, uint64_t n, int threads);
+
+/* ---- block-scale recipes ------------------------------------------------------------------ */
+/* MXFP8: bf16 [rows, cols] row-major, cols % 32 == 0 -> E4M3 [rows, cols] and one UE8M0 scale
+ * per 32 contiguous elements [rows, cols / 32]. Scale = floor-pow2 of the block amax minus E4M3's
+ * emax (8), from the reference's f8e8m0::from_f32::<TowardZero, SaturateFinite>; elements are
+ * x * 2^-(scale - 127) encoded RN .satfinite. */
+void ptxo_quantize_mxfp8(const uint16_t* x, int64_t rows, int64_t cols, uint8_t* q, uint8_t* sf,
+                         int threads);
+/* NVFP4: bf16 [rows, cols], cols % 16 == 0, decode global scale g -> E2M1 [rows, cols / 2]
+ * (element 0 in the low nibble) and one E4M3 scale per 16 contiguous elements [rows, cols / 16]:
+ * sf = e4m3(amax / (6 g)), elements e2m1(x * (1 / (sf * g))). Returns -1 on a bad g. */
+int ptxo_quantize_nvfp4(const uint16_t* x, int64_t rows, int64_t cols, float g, uint8_t* q,
+                        uint8_t* sf, int threads);
+/* One MXFP8 block / one NVFP4 block (used by the decode GEMM reference). */
+uint8_t ptxo_mxfp8_block(const float* x32, uint8_t* q32);
+uint8_t ptxo_nvfp4_block(const float* x16, float g, uint8_t* q16 /* one nibble per byte */);
+
+/* ---- GEMM references (f64 over decoded values) at sampled outputs ------------------------- */
+/* FP8: C[i,j] = sa * sb * sum_k A[i,k] B[j,k]; A [M,K], B [N,K] E4M3 (K contiguous). For each
+ * sample s: ref[s] = exact-ish f64 value, mag[s] = sa*sb*sum_k |A B|. */
+void ptxo_gemm_fp8_ref(const uint8_t* A, const uint8_t* B, int64_t M, int64_t N, int64_t K,
+                       float sa, float sb, const int64_t* rows, const int64_t* cols,
+                       int64_t n_samples, double* ref, double* mag, int threads);
+/* NVFP4: A [M,K/2], sfA [M,K/16] E4M3, ga; B [N,K/2], sfB [N,K/16], gb. */
+void ptxo_gemm_nvfp4_ref(const uint8_t* A, const uint8_t* sfA, float ga, const uint8_t* B,
+                         const uint8_t* sfB, float gb, int64_t M, int64_t N, int64_t K,
+                         const int64_t* rows, const int64_t* cols, int64_t n_samples, double* ref,
+                         double* mag, int threads);
+/* Decode: x bf16 [M,K] is MXFP8-quantised (32-blocks) by the recipe above, W NVFP4 [N,K/2] with
+ * sfW [N,K/16] and gw; C[i,j] = sum_k xq[i,k] 2^(sx-127) * w[j,k] sfW gw. */
+void ptxo_gemm_decode_ref(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float gw,
+                          int64_t M, int64_t N, int64_t K, const int64_t* rows,
+                          const int64_t* cols, int64_t n_samples, double* ref, double* mag,
+                          int threads);
+/* Timed CPU baseline: C[M,N] (f32) = sum_k A[i,k] B[j,k] over f32 matrices, cache-blocked and
+ * multithreaded (B given K-contiguous, like the device operands). */
+void ptxo_sgemm_nt(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                   int threads);
+
+/* ---- tcgen05 descriptor encodings (src/tcgen05/descriptor.rs) ----------------------------- */
+/* All return 0 and write *out on success, -1 where the reference asserts. */
+int ptxo_idesc_f16(int a, int b, int d, uint32_t m, uint32_t n, uint32_t* out);
+int ptxo_idesc_tf32(uint32_t m, uint32_t n, uint32_t* out);
+int ptxo_idesc_f8f6f4(int a, int b, int d, uint32_t m, uint32_t n, uint32_t* out);
+int ptxo_idesc_i8(int a, int b, uint32_t m, uint32_t n, uint32_t* out);
+int ptxo_idesc_mxf8f6f4(int a, int b, uint32_t m, uint32_t n, uint32_t* out);
+int ptxo_idesc_mxf4(uint32_t m, uint32_t n, uint32_t* out);
+int ptxo_idesc_mxf4nvf4(int scale_type, uint32_t m, uint32_t n, uint32_t* out);
+/* Generic field setter: replaces the width-bit field at shift (descriptor.rs:494-498). */
+int ptxo_idesc_with_field(uint32_t desc, uint32_t shift, uint32_t width, uint32_t value,
+                          uint32_t* out);
+int ptxo_smem_desc(uint32_t start, uint32_t lbo, uint32_t sbo, int swizzle, uint64_t* out);
+int ptxo_smem_desc_with_base_offset(uint64_t desc, uint32_t base_offset, uint64_t* out);
+int ptxo_smem_desc_add_start_bytes(uint64_t desc, uint32_t bytes, uint64_t* out);
+int ptxo_zero_mask_new(uint32_t zeroed, uint32_t used, uint64_t* out);
+int ptxo_zero_mask_with_sub_mask_start(uint64_t mask, uint32_t sub, int first_span,
+                                       uint32_t start_count, uint64_t* out);
+int ptxo_zero_mask_with_column_shift(uint64_t mask, uint32_t shift, uint64_t* out);
+
+int ptxo_hardware_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,231 @@
+"""ctypes loader for the CPU oracle (test infrastructure only).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg import this module, and
+only to check results or to time the CPU baseline. It builds ``oracle/_build/liboracle.so`` from
+``oracle/oracle.c`` with ``make`` when the library is missing.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+
+E4M3, E5M2, E2M1 = 0, 1, 2
+(V_E4M3, V_E5M2, V_E2M1, V_E4M3_RELU, V_E5M2_RELU, V_E2M1_RELU, V_UE8M0_RZ,
+ V_UE8M0_RP) = range(8)
+VARIANT_NAMES = ["e4m3", "e5m2", "e2m1", "e4m3_relu", "e5m2_relu", "e2m1_relu", "ue8m0_rz",
+                 "ue8m0_rp"]
+
+_lib = None
+
+
+def build() -> str:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        _lib = C.CDLL(LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+def _declare(L: C.CDLL) -> None:
+    u8, u16, u32, u64, i32, i64, f32 = (C.c_uint8, C.c_uint16, C.c_uint32, C.c_uint64, C.c_int,
+                                        C.c_int64, C.c_float)
+    p = C.c_void_p
+    sigs = {
+        "ptxo_minifloat_to_f32": (f32, [u8, u32, u32, C.c_int32, i32]),
+        "ptxo_e4m3_to_f32": (f32, [u8]),
+        "ptxo_e5m2_to_f32": (f32, [u8]),
+        "ptxo_e2m1_to_f32": (f32, [u8]),
+        "ptxo_ue8m0_to_f32": (f32, [u8]),
+        "ptxo_to_f32_via_half": (f32, [i32, u8]),
+        "ptxo_ue8m0_to_f32_via_bf16": (f32, [u8]),
+        "ptxo_f32_to_e4m3": (u8, [f32, i32]),
+        "ptxo_f32_to_e5m2": (u8, [f32, i32]),
+        "ptxo_f32_to_e2m1": (u8, [f32, i32]),
+        "ptxo_f32_to_narrow": (u8, [i32, f32, i32]),
+        "ptxo_f32_to_ue8m0": (u8, [f32, i32, i32]),
+        "ptxo_f32_to_bf16": (u16, [f32]),
+        "ptxo_bf16_to_f32": (f32, [u16]),
+        "ptxo_encode_array": (None, [i32, p, p, C.c_size_t, i32, i32]),
+        "ptxo_decode_array": (None, [i32, p, p, C.c_size_t, i32]),
+        "ptxo_ue8m0_encode_array": (None, [p, p, C.c_size_t, i32, i32, i32]),
+        "ptxo_encode_variant": (u8, [i32, f32]),
+        "ptxo_sweep_compare": (u64, [i32, u64, u64, p, p, u64, i32]),
+        "ptxo_sweep_digest": (u64, [i32, u64, u64, i32]),
+        "ptxo_fnv1a64": (u64, [p, C.c_size_t, u64]),
+        "ptxo_digest_bytes": (u64, [p, u64, i32]),
+        "ptxo_quantize_mxfp8": (None, [p, i64, i64, p, p, i32]),
+        "ptxo_quantize_nvfp4": (i32, [p, i64, i64, f32, p, p, i32]),
+        "ptxo_gemm_fp8_ref": (None, [p, p, i64, i64, i64, f32, f32, p, p, i64, p, p, i32]),
+        "ptxo_gemm_nvfp4_ref": (None, [p, p, f32, p, p, f32, i64, i64, i64, p, p, i64, p, p,
+                                       i32]),
+        "ptxo_gemm_decode_ref": (None, [p, p, p, f32, i64, i64, i64, p, p, i64, p, p, i32]),
+        "ptxo_sgemm_nt": (None, [p, p, p, i64, i64, i64, i32]),
+        "ptxo_idesc_f16": (i32, [i32, i32, i32, u32, u32, C.POINTER(u32)]),
+        "ptxo_idesc_tf32": (i32, [u32, u32, C.POINTER(u32)]),
+        "ptxo_idesc_f8f6f4": (i32, [i32, i32, i32, u32, u32, C.POINTER(u32)]),
+        "ptxo_idesc_i8": (i32, [i32, i32, u32, u32, C.POINTER(u32)]),
+        "ptxo_idesc_mxf8f6f4": (i32, [i32, i32, u32, u32, C.POINTER(u32)]),
+        "ptxo_idesc_mxf4": (i32, [u32, u32, C.POINTER(u32)]),
+        "ptxo_idesc_mxf4nvf4": (i32, [i32, u32, u32, C.POINTER(u32)]),
+        "ptxo_idesc_with_field": (i32, [u32, u32, u32, u32, C.POINTER(u32)]),
+        "ptxo_smem_desc": (i32, [u32, u32, u32, i32, C.POINTER(u64)]),
+        "ptxo_smem_desc_with_base_offset": (i32, [u64, u32, C.POINTER(u64)]),
+        "ptxo_smem_desc_add_start_bytes": (i32, [u64, u32, C.POINTER(u64)]),
+        "ptxo_zero_mask_new": (i32, [u32, u32, C.POINTER(u64)]),
+        "ptxo_zero_mask_with_sub_mask_start": (i32, [u64, u32, i32, u32, C.POINTER(u64)]),
+        "ptxo_zero_mask_with_column_shift": (i32, [u64, u32, C.POINTER(u64)]),
+        "ptxo_hardware_threads": (i32, []),
+    }
+    for name, (res, args) in sigs.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+def _ptr(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+# ---- numpy conveniences ------------------------------------------------------------------------
+
+def encode(fmt: int, x: np.ndarray, relu: bool = False, threads: int = 0) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n = x.size
+    out = np.empty(n // 2 if fmt == E2M1 else n, dtype=np.uint8)
+    lib().ptxo_encode_array(fmt, _ptr(x), _ptr(out), n, int(relu), threads)
+    return out
+
+
+def decode(fmt: int, codes: np.ndarray, threads: int = 0) -> np.ndarray:
+    codes = np.ascontiguousarray(codes, dtype=np.uint8)
+    n = codes.size * 2 if fmt == E2M1 else codes.size
+    out = np.empty(n, dtype=np.float32)
+    lib().ptxo_decode_array(fmt, _ptr(codes), _ptr(out), n, threads)
+    return out
+
+
+def ue8m0_encode(x: np.ndarray, rnd_up: bool = False, satfinite: bool = True,
+                 threads: int = 0) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.size, dtype=np.uint8)
+    lib().ptxo_ue8m0_encode_array(_ptr(x), _ptr(out), x.size, int(rnd_up), int(satfinite),
+                                  threads)
+    return out
+
+
+def quantize_mxfp8(x_bf16: np.ndarray, threads: int = 0):
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    rows, cols = x.shape
+    q = np.empty((rows, cols), dtype=np.uint8)
+    sf = np.empty((rows, cols // 32), dtype=np.uint8)
+    lib().ptxo_quantize_mxfp8(_ptr(x), rows, cols, _ptr(q), _ptr(sf), threads)
+    return q, sf
+
+
+def quantize_nvfp4(x_bf16: np.ndarray, g: float, threads: int = 0):
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    rows, cols = x.shape
+    q = np.empty((rows, cols // 2), dtype=np.uint8)
+    sf = np.empty((rows, cols // 16), dtype=np.uint8)
+    rc = lib().ptxo_quantize_nvfp4(_ptr(x), rows, cols, float(g), _ptr(q), _ptr(sf), threads)
+    if rc != 0:
+        raise ValueError("bad global scale")
+    return q, sf
+
+
+def _samples(rows, cols):
+    r = np.ascontiguousarray(rows, dtype=np.int64)
+    c = np.ascontiguousarray(cols, dtype=np.int64)
+    return r, c, np.empty(r.size), np.empty(r.size)
+
+
+def gemm_fp8_ref(A, B, sa, sb, rows, cols, threads=0):
+    A = np.ascontiguousarray(A, dtype=np.uint8)
+    B = np.ascontiguousarray(B, dtype=np.uint8)
+    (M, K), N = A.shape, B.shape[0]
+    r, c, ref, mag = _samples(rows, cols)
+    lib().ptxo_gemm_fp8_ref(_ptr(A), _ptr(B), M, N, K, sa, sb, _ptr(r), _ptr(c), r.size,
+                            _ptr(ref), _ptr(mag), threads)
+    return ref, mag
+
+
+def gemm_nvfp4_ref(A, sfA, ga, B, sfB, gb, rows, cols, threads=0):
+    A, sfA, B, sfB = (np.ascontiguousarray(t, dtype=np.uint8) for t in (A, sfA, B, sfB))
+    M, K = A.shape[0], A.shape[1] * 2
+    N = B.shape[0]
+    r, c, ref, mag = _samples(rows, cols)
+    lib().ptxo_gemm_nvfp4_ref(_ptr(A), _ptr(sfA), ga, _ptr(B), _ptr(sfB), gb, M, N, K, _ptr(r),
+                              _ptr(c), r.size, _ptr(ref), _ptr(mag), threads)
+    return ref, mag
+
+
+def gemm_decode_ref(x_bf16, W, sfW, gw, rows, cols, threads=0):
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    W, sfW = (np.ascontiguousarray(t, dtype=np.uint8) for t in (W, sfW))
+    M, K = x.shape
+    N = W.shape[0]
+    r, c, ref, mag = _samples(rows, cols)
+    lib().ptxo_gemm_decode_ref(_ptr(x), _ptr(W), _ptr(sfW), gw, M, N, K, _ptr(r), _ptr(c),
+                               r.size, _ptr(ref), _ptr(mag), threads)
+    return ref, mag
+
+
+def sgemm_nt(A, B, threads=0):
+    A = np.ascontiguousarray(A, dtype=np.float32)
+    B = np.ascontiguousarray(B, dtype=np.float32)
+    M, K = A.shape
+    N = B.shape[0]
+    Cm = np.empty((M, N), dtype=np.float32)
+    lib().ptxo_sgemm_nt(_ptr(A), _ptr(B), _ptr(Cm), M, N, K, threads)
+    return Cm
+
+
+def sweep_compare(variant: int, base: int, dev_codes: np.ndarray, max_report: int = 64,
+                  threads: int = 0):
+    dev = np.ascontiguousarray(dev_codes, dtype=np.uint8)
+    rep = np.zeros((max_report, 3), dtype=np.uint32)
+    n = lib().ptxo_sweep_compare(variant, base, dev.size, _ptr(dev), _ptr(rep), max_report,
+                                 threads)
+    return int(n), rep[: min(int(n), max_report)]
+
+
+def sweep_digest(variant: int, base: int, n: int, threads: int = 0) -> int:
+    return int(lib().ptxo_sweep_digest(variant, base, n, threads))
+
+
+def digest_bytes(data: np.ndarray, threads: int = 0) -> int:
+    d = np.ascontiguousarray(data, dtype=np.uint8)
+    return int(lib().ptxo_digest_bytes(_ptr(d), d.size, threads))
+
+
+def fnv1a64(data: np.ndarray, seed: int = 0) -> int:
+    d = np.ascontiguousarray(data, dtype=np.uint8)
+    return int(lib().ptxo_fnv1a64(_ptr(d), d.size, seed))
+
+
+def bf16_from_f32(x: np.ndarray) -> np.ndarray:
+    """RNE f32 -> bf16 bit patterns (vectorised numpy restatement of ptxo_f32_to_bf16)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r = np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), r)
+    return r
+
+
+def bf16_to_f32(h: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)

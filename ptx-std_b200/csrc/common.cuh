@@ -1,0 +1,182 @@
+// Device-side foundation shared by every kernel of libptxstd: status/error word, bounded mbarrier
+// waits, fences, elect, TMA copies. Each wrapper is one PTX instruction (or a short bounded loop
+// around one) with the semantics of the ptx-std API named beside it.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/ptxstd.h"
+
+namespace ptxstd {
+
+// ---- error word ----------------------------------------------------------------------------
+// Each device holds one error word pair {status, detail}. Kernels record the first failure with
+// a CAS so that the earliest cause is kept; the host reads it with ptxstd_last_device_error.
+__device__ __forceinline__ void record_error(uint32_t* err, uint32_t status, uint32_t detail) {
+    if (err != nullptr && atomicCAS(err, 0u, status) == 0u) atomicExch(err + 1, detail);
+}
+
+// Host side: the address of this device's error word (set up once per device).
+uint32_t* device_error_word();
+
+// ---- time -----------------------------------------------------------------------------------
+// %globaltimer in ns (ptx-std src/time.rs:40).
+__device__ __forceinline__ uint64_t global_timer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Every device-side wait gives up after this long and reports PTXSTD_ETIMEOUT.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// ---- addresses --------------------------------------------------------------------------------
+// memory::to_shared_address (src/memory.rs:482): generic -> .shared::cta address.
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- warp collectives ---------------------------------------------------------------------------
+// warp_collectives::elect (src/warp_collectives.rs:900): true on exactly one lane of the warp.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
+__device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
+__device__ __forceinline__ uint32_t warp_id() {
+    return __shfl_sync(0xffffffffu, threadIdx.x >> 5, 0);
+}
+
+// ---- mbarrier (src/mbarrier.rs) --------------------------------------------------------------
+// MBarrier::init (:311).
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+// MBarrier::fence_init (:345): makes the initialisation visible to the async proxy / cluster.
+__device__ __forceinline__ void fence_mbarrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// MBarrier::arrive_expect_tx (:533).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+// MBarrier::arrive.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// MBarrier::try_wait (:928) on a phase parity.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// The reference's MBarrier::wait spins forever (:1011-1016); this one is bounded by
+// kWaitLimitNs on %globaltimer and returns false when it gives up (try_wait_timed, :965).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const uint64_t t0 = global_timer();
+    while (!mbar_try_wait(a, parity)) {
+        if (global_timer() - t0 > kWaitLimitNs) return false;
+    }
+    return true;
+}
+
+// ---- fences (src/fence.rs) -------------------------------------------------------------------
+// fence_proxy::<AsyncSharedCta> (:107): generic-proxy smem writes -> async proxy (TMA, tcgen05).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- TMA (src/tma/tensor.rs) -----------------------------------------------------------------
+// tma_load_tile::<2> (:214-236): 2-D tile global -> this CTA's smem, completing on `bar`.
+// Coordinates are in elements, innermost first. No multicast anywhere in this library.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t c0, int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+// The same with an L2 cache policy (memory::CachePolicy, src/memory.rs:66-240).
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                 int32_t c0, int32_t c1, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
+        : "memory");
+}
+// tma_store_tile::<2> (:746): smem -> global, tracked by the bulk async-group.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t c0,
+                                             int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1)
+        : "memory");
+}
+// bulk_commit_group / bulk_wait_group::<N> read variant (src/tma/mod.rs:204, :220).
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// prefetch_tensormap (src/tma/mod.rs:239).
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// createpolicy.fractional L2::evict_first / evict_last (memory::CachePolicy).
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// ---- streaming global memory ------------------------------------------------------------------
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+}  // namespace ptxstd
+
+// ---- host-side helpers ----------------------------------------------------------------------
+namespace ptxstd {
+// Maps a CUDA error to a status, remembering nothing (callers check cudaGetLastError()).
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? PTXSTD_OK : PTXSTD_ECUDA; }
+// Launch-side check of the last launch.
+inline int launch_status() { return cuda_status(cudaGetLastError()); }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+// Streaming-multiprocessor count of the current device (cached per device).
+int sm_count();
+}  // namespace ptxstd

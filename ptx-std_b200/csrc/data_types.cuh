@@ -1,0 +1,149 @@
+// Device conversions of the narrow formats: the B200 form of ptx-std's data_types module
+// (src/data_types/narrow.rs, float8.rs, float4.rs). Each pair function is the one `cvt`
+// instruction the reference's pair_* method wraps; element 0 of a pair always lands in the least
+// significant bits, so the PTX operands are swapped (`cvt` puts operand a in the upper half,
+// src/data_types/narrow.rs:18-21).
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace ptxstd::data_types {
+
+// ---- f32 -> narrow, RN .satfinite [.relu] ---------------------------------------------------
+// f8e4m3x2::pair_from_f32 (narrow.rs:156-162): cvt.rn.satfinite{.relu}.e4m3x2.f32.
+template <bool RELU = false>
+__device__ __forceinline__ uint16_t e4m3x2_from_f32(float x0, float x1) {
+    uint16_t r;
+    if constexpr (RELU)
+        asm("cvt.rn.satfinite.relu.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    else
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    return r;
+}
+// f8e5m2x2::pair_from_f32: cvt.rn.satfinite{.relu}.e5m2x2.f32.
+template <bool RELU = false>
+__device__ __forceinline__ uint16_t e5m2x2_from_f32(float x0, float x1) {
+    uint16_t r;
+    if constexpr (RELU)
+        asm("cvt.rn.satfinite.relu.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    else
+        asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    return r;
+}
+// f4e2m1x2::pair_from_f32: cvt.rn.satfinite{.relu}.e2m1x2.f32 (one byte, x0 in the low nibble).
+template <bool RELU = false>
+__device__ __forceinline__ uint32_t e2m1x2_from_f32(float x0, float x1) {
+    uint32_t r;
+    if constexpr (RELU)
+        asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.relu.e2m1x2.f32 t, %1, %2;\n\t"
+            "cvt.u32.u8 %0, t;\n\t}"
+            : "=r"(r)
+            : "f"(x1), "f"(x0));
+    else
+        asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\t"
+            "cvt.u32.u8 %0, t;\n\t}"
+            : "=r"(r)
+            : "f"(x1), "f"(x0));
+    return r;
+}
+// Four E2M1 values packed in 16 bits (element 0 in bits 0..3).
+__device__ __forceinline__ uint32_t e2m1x4_from_f32(float x0, float x1, float x2, float x3) {
+    return e2m1x2_from_f32(x0, x1) | (e2m1x2_from_f32(x2, x3) << 8);
+}
+
+// f8e8m0x2::pair_from_f32::<RND, OVERFLOW> (narrow.rs:600-617): RZ or RP, optional .satfinite.
+template <bool ROUND_UP, bool SATFINITE>
+__device__ __forceinline__ uint16_t ue8m0x2_from_f32(float x0, float x1) {
+    uint16_t r;
+    if constexpr (ROUND_UP && SATFINITE)
+        asm("cvt.rp.satfinite.ue8m0x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    else if constexpr (ROUND_UP)
+        asm("cvt.rp.ue8m0x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    else if constexpr (SATFINITE)
+        asm("cvt.rz.satfinite.ue8m0x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    else
+        asm("cvt.rz.ue8m0x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    return r;
+}
+// Scalar form: the pair instruction with a zero lane (narrow.rs:243-247, :660-664).
+template <bool ROUND_UP, bool SATFINITE>
+__device__ __forceinline__ uint32_t ue8m0_from_f32(float x) {
+    return ue8m0x2_from_f32<ROUND_UP, SATFINITE>(x, 0.0f) & 0xFFu;
+}
+
+// ---- narrow -> f32 (exact) ---------------------------------------------------------------------
+// to_f32 = to_f16 then the exact widening (narrow.rs:292-299).
+__device__ __forceinline__ float2 half2_bits_to_float2(uint32_t h2) {
+    __half2 h = *reinterpret_cast<__half2*>(&h2);
+    return __half22float2(h);
+}
+__device__ __forceinline__ float2 e4m3x2_to_f32(uint16_t codes) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(codes));
+    return half2_bits_to_float2(h2);
+}
+__device__ __forceinline__ float2 e5m2x2_to_f32(uint16_t codes) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(h2) : "h"(codes));
+    return half2_bits_to_float2(h2);
+}
+__device__ __forceinline__ float2 e2m1x2_to_f32(uint32_t byte) {
+    uint32_t h2;
+    asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+        : "=r"(h2)
+        : "r"(byte));
+    return half2_bits_to_float2(h2);
+}
+// ue8m0 to_f32 = to_bf16 then widening (narrow.rs:683-690): cvt.rn.bf16x2.ue8m0x2.
+__device__ __forceinline__ float2 ue8m0x2_to_f32(uint16_t codes) {
+    uint32_t b2;
+    asm("cvt.rn.bf16x2.ue8m0x2 %0, %1;" : "=r"(b2) : "h"(codes));
+    return make_float2(__uint_as_float(b2 << 16), __uint_as_float(b2 & 0xFFFF0000u));
+}
+// One E4M3 code -> f32, exact.
+__device__ __forceinline__ float e4m3_to_f32(uint32_t code) {
+    return e4m3x2_to_f32(static_cast<uint16_t>(code & 0xFFu)).x;
+}
+
+// ---- bf16 ------------------------------------------------------------------------------------
+// bf16::to_f32 (src/data_types/bfloat16.rs:84-86): exact widening of the two halves of a word.
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// bf16x2 from two f32, RN (bfloat16.rs:104-118): cvt.rn.bf16x2.f32, x0 in the low half.
+__device__ __forceinline__ uint32_t bf16x2_from_f32(float x0, float x1) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
+    return r;
+}
+
+// ---- block-scale helpers -------------------------------------------------------------------
+// NaN-propagating amax of the |bf16| values in a word pair: for non-negative bf16 patterns the
+// integer order is the float order, and every NaN pattern sorts above infinity, so an unsigned
+// 16-bit max of the magnitudes is reduce_f32::<Max, Absolute> with NaN propagation
+// (src/warp_collectives.rs:679-700) computed on the raw bits.
+__device__ __forceinline__ uint32_t bf16x2_absmax_bits(uint32_t a, uint32_t b) {
+    return __vmaxu2(a & 0x7FFF7FFFu, b & 0x7FFF7FFFu);
+}
+__device__ __forceinline__ uint32_t bf16x2_fold(uint32_t m2) {
+    return max(m2 & 0xFFFFu, m2 >> 16);
+}
+
+// 2^-(code-127) as f32 for a UE8M0 scale code (2^127 .. 2^-127, the last an f32 subnormal);
+// NaN for the NaN code 0xff.
+__device__ __forceinline__ float ue8m0_inverse(uint32_t code) {
+    if (code == 0xFFu) return __uint_as_float(0x7FFFFFFFu);
+    const int e = 127 - static_cast<int>(code);
+    return e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23)
+                     : __uint_as_float(0x00400000u);
+}
+
+// MXFP8 scale code of a block from its amax: from_f32::<TowardZero, SaturateFinite>(amax) minus
+// E4M3's emax (8), clamped at 0; NaN stays NaN.
+__device__ __forceinline__ uint32_t mxfp8_scale_code(float amax) {
+    const uint32_t u = ue8m0_from_f32<false, true>(amax);
+    return u == 0xFFu ? 0xFFu : (u > 8u ? u - 8u : 0u);
+}
+
+}  // namespace ptxstd::data_types

@@ -1,0 +1,78 @@
+"""Narrow-float conversions over CUDA tensors (ptx-std src/data_types/).
+
+Each function mirrors a reference conversion applied element-wise, computed by libptxstd's
+kernels with the same `cvt` instructions the reference's pair methods wrap:
+
+- ``from_f32(fmt, x, relu)``: Vector<fmt, N>::from_f32::<RELU> (src/data_types/narrow.rs:354-361),
+  RN .satfinite; one code per byte for FP8, two per byte (element 0 low nibble) for E2M1.
+- ``to_f32(fmt, codes)``: exact decode through f16 (narrow.rs:292-299).
+- ``ue8m0_from_f32(x, round_up, satfinite)``: f8e8m0::from_f32::<RND, OVERFLOW>
+  (narrow.rs:600-617); ``ue8m0_to_f32``: through bf16 (narrow.rs:683-690).
+"""
+
+from __future__ import annotations
+
+from . import _dev, _stream, _torch, check, lib
+
+E4M3, E5M2, E2M1 = "e4m3", "e5m2", "e2m1"
+
+_ENC = {E4M3: "ptxstd_cvt_f32_to_e4m3", E5M2: "ptxstd_cvt_f32_to_e5m2",
+        E2M1: "ptxstd_cvt_f32_to_e2m1x2"}
+_DEC = {E4M3: "ptxstd_cvt_e4m3_to_f32", E5M2: "ptxstd_cvt_e5m2_to_f32",
+        E2M1: "ptxstd_cvt_e2m1x2_to_f32"}
+
+
+def from_f32(fmt: str, x, relu: bool = False, stream=None):
+    torch = _torch()
+    if x.dtype != torch.float32:
+        raise TypeError("expected float32")
+    x = x.contiguous()
+    n = x.numel()
+    out = torch.empty(n // 2 if fmt == E2M1 else n, dtype=torch.uint8, device=x.device)
+    check(getattr(lib(), _ENC[fmt])(_dev(x), _dev(out), n, int(relu), _stream(stream)),
+          f"from_f32({fmt})")
+    return out
+
+
+def from_bf16(fmt: str, x, relu: bool = False, stream=None):
+    """Vector<fmt, N>::from_bf16 (narrow.rs:363-395): bf16 widens to f32 exactly, so the RN
+    conversion of the widened value is the same rounding of the same real number."""
+    torch = _torch()
+    return from_f32(fmt, x.to(torch.float32), relu, stream)
+
+
+def to_f32(fmt: str, codes, stream=None):
+    torch = _torch()
+    codes = codes.contiguous()
+    n = codes.numel()
+    out = torch.empty(2 * n if fmt == E2M1 else n, dtype=torch.float32, device=codes.device)
+    check(getattr(lib(), _DEC[fmt])(_dev(codes), _dev(out), n, _stream(stream)),
+          f"to_f32({fmt})")
+    return out
+
+
+def ue8m0_from_f32(x, round_up: bool = False, satfinite: bool = True, stream=None):
+    torch = _torch()
+    x = x.contiguous()
+    out = torch.empty(x.numel(), dtype=torch.uint8, device=x.device)
+    check(lib().ptxstd_cvt_f32_to_ue8m0(_dev(x), _dev(out), x.numel(), int(round_up),
+                                        int(satfinite), _stream(stream)), "ue8m0_from_f32")
+    return out
+
+
+def ue8m0_to_f32(codes, stream=None):
+    torch = _torch()
+    codes = codes.contiguous()
+    out = torch.empty(codes.numel(), dtype=torch.float32, device=codes.device)
+    check(lib().ptxstd_cvt_ue8m0_to_f32(_dev(codes), _dev(out), codes.numel(), _stream(stream)),
+          "ue8m0_to_f32")
+    return out
+
+
+def sweep(variant: int, base: int, n: int, out=None, stream=None):
+    """Codes of the f32 bit patterns base .. base+n-1 (see ptxstd_cvt_sweep)."""
+    torch = _torch()
+    if out is None:
+        out = torch.empty(n, dtype=torch.uint8, device="cuda")
+    check(lib().ptxstd_cvt_sweep(variant, base, n, _dev(out), _stream(stream)), "sweep")
+    return out

@@ -1,0 +1,59 @@
+"""The C ABI library loads without a GPU and exports every function include/*.h declares."""
+
+import ctypes as C
+import glob
+import os
+import re
+import subprocess
+
+from conftest import ROOT
+
+
+def _declared():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        names |= set(re.findall(r"PTXSTD_API\s+[\w\s\*]*?\b(ptxstd_\w+)\s*\(", src))
+    return names
+
+
+def test_exports_every_declared_symbol(ptxstd_lib):
+    lib_path = ptxstd_lib.LIB_PATH
+    out = subprocess.run(["nm", "-D", "--defined-only", lib_path], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (ptxstd_\w+)", out))
+    declared = _declared()
+    assert len(declared) >= 30
+    missing = declared - exported
+    assert not missing, sorted(missing)
+    L = C.CDLL(lib_path)
+    for name in declared:
+        assert getattr(L, name) is not None
+
+
+def test_no_undeclared_exports(ptxstd_lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", ptxstd_lib.LIB_PATH],
+                         capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (\w+)", out))
+    assert exported - _declared() == set() or all(not n.startswith("ptxstd_")
+                                                  for n in exported - _declared())
+
+
+def test_status_strings_and_version(ptxstd_lib):
+    L = ptxstd_lib.lib()
+    assert ptxstd_lib.status_string(0) == "ok"
+    assert ptxstd_lib.status_string(ptxstd_lib.ETIMEOUT) == "device-side wait timed out"
+    assert L.ptxstd_version() >= 100
+
+
+def test_host_validation_without_gpu(ptxstd_lib):
+    """Argument checks happen before any CUDA call, so they answer EINVAL on a CPU-only host."""
+    L = ptxstd_lib.lib()
+    EINVAL = ptxstd_lib.EINVAL
+    assert L.ptxstd_quantize_mxfp8(None, 128, 96 + 1, None, None, None) == EINVAL
+    assert L.ptxstd_quantize_mxfp8(None, 0, 64, None, None, None) == EINVAL
+    assert L.ptxstd_quantize_nvfp4(None, 128, 64, 0.0, None, None, None) == EINVAL
+    assert L.ptxstd_quantize_nvfp4_layout(16, 128, 64, 1.0, 16, 16, 2, None) == EINVAL
+    assert L.ptxstd_cvt_f32_to_e2m1x2(16, 16, 3, 0, None) == EINVAL
+    assert L.ptxstd_cvt_sweep(9, 0, 16, 16, None) == EINVAL
+    assert L.ptxstd_cvt_sweep(0, (1 << 32) - 8, 16, 16, None) == EINVAL
