@@ -109,6 +109,15 @@ PTXSTD_API int ptxstd_quantize_nvfp4_layout(const uint16_t* d_x, int64_t rows, i
                                  float global_scale, uint8_t* d_q, uint8_t* d_sf, int sf_layout,
                                  ptxstd_stream stream);
 
+/* ---- block-scaled / narrow GEMMs on tcgen05 --------------------------------------------------- */
+/* FP8 GEMM: C[M,N] bf16 row-major = sa * sb * A[M,K] * B[N,K]^T with E4M3 A and B (K contiguous),
+ * fp32 accumulation, bf16 RN output. The tcgen05.mma.kind::f8f6f4 + TMA + mbarrier pipeline of
+ * src/tcgen05/mod.rs:105-162 (mma :434-453 of src/tcgen05/mma.rs; InstrDescriptor::<F8f6f4>::new,
+ * src/tcgen05/descriptor.rs:555-564). M % 128 == 0, N % 256 == 0, K % 128 == 0. */
+PTXSTD_API int ptxstd_gemm_fp8(const uint8_t* d_a, const uint8_t* d_b, float sa, float sb,
+                               uint16_t* d_c, int64_t M, int64_t N, int64_t K,
+                               ptxstd_stream stream);
+
 /* ---- tcgen05 descriptors (src/tcgen05/descriptor.rs) ---------------------------------------- */
 /* InstrDescriptor::<KIND>::new for each kind. Element types use the reference's discriminants:
  * F16ElementType F16 0 / Bf16 1; FloatAccumulator F16 0 / F32 1; F8f6f4ElementType E4m3 0,

@@ -98,9 +98,10 @@ float ptxo_ue8m0_to_f32(uint8_t b) {
     return u2f((uint32_t)b << 23);
 }
 
-/* The device's `to_f32` goes through f16 (`cvt.rn.f16x2.<fmt>x2`, then the exact widening;
- * src/data_types/narrow.rs:292-299). Finite values are exact either way; a NaN code becomes the
- * f16 canonical NaN 0x7fff, widened to f32 0x7fffe000 (the sign of the NaN is not kept). */
+/* The device's `to_f32` is to_f16 (`cvt.rn.f16x2.<fmt>x2`) followed by f16::to_f32, which is
+ * `self.prim() as f32` (src/data_types/narrow.rs:292-299, src/data_types/float16.rs:90-92), the
+ * hardware cvt.f32.f16: finite values are exact, and every NaN becomes the canonical f32 NaN
+ * 0x7fffffff whatever its sign or payload (observed on B200 for codes 0x7f and 0xff). */
 float ptxo_to_f32_via_half(int format, uint8_t bits) {
     float v;
     switch (format) {
@@ -108,7 +109,7 @@ float ptxo_to_f32_via_half(int format, uint8_t bits) {
     case PTXO_E5M2: v = ptxo_e5m2_to_f32(bits); break;
     default: v = ptxo_e2m1_to_f32(bits); break;
     }
-    if (v != v) return u2f(0x7FFFE000u);
+    if (v != v) return u2f(0x7FFFFFFFu);
     return v;
 }
 

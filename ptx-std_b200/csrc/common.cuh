@@ -179,4 +179,6 @@ inline int launch_status() { return cuda_status(cudaGetLastError()); }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 // Streaming-multiprocessor count of the current device (cached per device).
 int sm_count();
+// Raises a kernel's dynamic shared memory limit once per device; returns a ptxstd_status.
+int set_max_dynamic_smem(const void* kernel, int bytes);
 }  // namespace ptxstd

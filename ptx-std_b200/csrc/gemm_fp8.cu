@@ -1,0 +1,269 @@
+// FP8 E4M3 x E4M3 GEMM on the 5th-generation tensor cores:
+//   C[M, N] (bf16, row-major) = sa * sb * A[M, K] * B[N, K]^T, fp32 accumulation,
+// A and B K-contiguous E4M3 codes. This is the tcgen05 + TMA + mbarrier pipeline that ptx-std
+// documents as its canonical pattern (src/tcgen05/mod.rs:105-162), assembled into a persistent,
+// warp-specialised kernel:
+//   warp 0        TMA producer: one elected lane streams 128x128-byte A tiles and 256x128-byte B
+//                 tiles (128-byte swizzle) into a STAGES-deep ring, arming `full[s]` with the
+//                 byte count (tma_load_tile, src/tma/tensor.rs:214-236; arrive_expect_tx,
+//                 src/mbarrier.rs:533);
+//   warp 1        TMEM owner and MMA issuer: one lane issues tcgen05.mma.kind::f8f6f4 (M=128,
+//                 N=256, K=32) four times per stage and commits each stage back to `empty[s]`
+//                 (src/tcgen05/mma.rs:434-453, sync.rs:70-80);
+//   warps 2..5    epilogue: tcgen05.ld.32x32b of their TMEM lane quarter, scale, RN to bf16,
+//                 16-byte stores (src/tcgen05/ld_st.rs:252-300).
+// Two 128x256 fp32 accumulators (all 512 TMEM columns) let the epilogue of tile i overlap the
+// main loop of tile i+1. Tiles are visited in groups of 8 M-blocks so that concurrently running
+// CTAs share B tiles in L2. Every wait is bounded (kWaitLimitNs); a timeout records
+// PTXSTD_ETIMEOUT in the device error word, drains outstanding copies and MMAs, frees TMEM and
+// returns.
+#include "common.cuh"
+#include "data_types.cuh"
+#include "tcgen05.cuh"
+#include "tma_host.h"
+
+namespace {
+
+namespace t5 = ptxstd::tcgen05;
+namespace dt = ptxstd::data_types;
+using ptxstd::mbar_wait;
+
+constexpr uint32_t BM = 128, BN = 256, BK = 128;  // BK in bytes = E4M3 elements
+constexpr uint32_t STAGES = 4;
+constexpr uint32_t kThreads = 192;
+constexpr uint32_t kABytes = BM * BK;
+constexpr uint32_t kBBytes = BN * BK;
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kAccCols = BN;
+constexpr uint32_t kTmemCols = 2 * kAccCols;
+constexpr uint32_t kGroupM = 8;
+constexpr uint32_t kMmaK = 32;  // K of one kind::f8f6f4 MMA
+
+struct alignas(1024) Smem {
+    uint8_t a[STAGES][kABytes];
+    uint8_t b[STAGES][kBBytes];
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t tfull[2];
+    uint64_t tempty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    uint32_t abort;
+};
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+
+// Error-word detail codes: which wait gave up.
+enum : uint32_t { kDetailProducer = 0x100, kDetailMma = 0x200, kDetailEpilogue = 0x300 };
+
+__device__ __forceinline__ void tile_coords(uint32_t t, uint32_t num_m, uint32_t num_n,
+                                            uint32_t& mb, uint32_t& nb) {
+    const uint32_t group_tiles = kGroupM * num_n;
+    const uint32_t g = t / group_tiles;
+    const uint32_t first_m = g * kGroupM;
+    const uint32_t gm = min(num_m - first_m, kGroupM);
+    const uint32_t local = t - g * group_tiles;
+    mb = first_m + local % gm;
+    nb = local / gm;
+}
+
+__device__ __forceinline__ void fail(Smem& s, uint32_t* err, uint32_t detail) {
+    ptxstd::record_error(err, PTXSTD_ETIMEOUT, detail);
+    *reinterpret_cast<volatile uint32_t*>(&s.abort) = 1u;
+}
+__device__ __forceinline__ bool aborted(Smem& s) {
+    return *reinterpret_cast<volatile uint32_t*>(&s.abort) != 0u;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    uint16_t* __restrict__ C, uint32_t M, uint32_t N, uint32_t K, float alpha,
+                    uint32_t* err) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                       ~static_cast<uintptr_t>(1023));
+    const uint32_t warp = ptxstd::warp_id();
+    const uint32_t lane = ptxstd::lane_id();
+    const uint32_t num_m = M / BM, num_n = N / BN, num_tiles = num_m * num_n, num_k = K / BK;
+
+    if (warp == 0 && lane == 0) {
+        ptxstd::prefetch_tensormap(&tmA);
+        ptxstd::prefetch_tensormap(&tmB);
+        for (uint32_t i = 0; i < STAGES; ++i) {
+            ptxstd::mbar_init(&s.full[i], 1);
+            ptxstd::mbar_init(&s.empty[i], 1);
+        }
+        for (uint32_t i = 0; i < 2; ++i) {
+            ptxstd::mbar_init(&s.tfull[i], 1);
+            ptxstd::mbar_init(&s.tempty[i], 4);
+        }
+        ptxstd::mbar_init(&s.drain, 1);
+        s.abort = 0;
+        ptxstd::fence_mbarrier_init();
+    }
+    if (warp == 1) {
+        t5::tmem_alloc(&s.tmem_base, kTmemCols);
+        t5::tmem_relinquish();
+    }
+    t5::fence_before_thread_sync();
+    __syncthreads();
+    t5::fence_after_thread_sync();
+    const uint32_t tmem = s.tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (ptxstd::elect_one()) {
+            uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
+            for (uint32_t t = blockIdx.x; t < num_tiles && !aborted(s); t += gridDim.x) {
+                uint32_t mb, nb;
+                tile_coords(t, num_m, num_n, mb, nb);
+                for (uint32_t kb = 0; kb < num_k; ++kb) {
+                    if (!mbar_wait(&s.empty[stage], phase ^ 1u)) {
+                        fail(s, err, kDetailProducer | stage);
+                        break;
+                    }
+                    if (aborted(s)) break;
+                    ptxstd::mbar_arrive_expect_tx(&s.full[stage], kStageBytes);
+                    ptxstd::tma_load_2d(s.a[stage], &tmA, &s.full[stage],
+                                        static_cast<int32_t>(kb * BK), static_cast<int32_t>(mb * BM));
+                    ptxstd::tma_load_2d(s.b[stage], &tmB, &s.full[stage],
+                                        static_cast<int32_t>(kb * BK), static_cast<int32_t>(nb * BN));
+                    issued |= 1u << stage;
+                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (aborted(s)) {
+                // Wait (bounded) for this thread's copies still in flight before the CTA exits.
+                for (uint32_t i = 0; i < STAGES; ++i)
+                    if (issued & (1u << i)) mbar_wait(&s.full[i], (issued_parity >> i) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (ptxstd::elect_one()) {
+            uint32_t idesc = 0;
+            t5::idesc_dense(/*E4m3*/ 0, /*E4m3*/ 0, /*F32*/ 1, BM, BN, idesc);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            for (uint32_t t = blockIdx.x; t < num_tiles && !aborted(s); t += gridDim.x) {
+                if (!mbar_wait(&s.tempty[acc], acc_phase ^ 1u)) {
+                    fail(s, err, kDetailMma | 0x10 | acc);
+                    break;
+                }
+                t5::fence_after_thread_sync();
+                const uint32_t d = tmem + acc * kAccCols;
+                bool ok = true;
+                for (uint32_t kb = 0; kb < num_k; ++kb) {
+                    if (!mbar_wait(&s.full[stage], phase)) {
+                        fail(s, err, kDetailMma | stage);
+                        ok = false;
+                        break;
+                    }
+                    t5::fence_after_thread_sync();
+                    const uint64_t ad = t5::smem_desc_k128(ptxstd::smem_u32(s.a[stage]));
+                    const uint64_t bd = t5::smem_desc_k128(ptxstd::smem_u32(s.b[stage]));
+#pragma unroll
+                    for (uint32_t k = 0; k < BK / kMmaK; ++k) {
+                        // +32 bytes along K inside the 128-byte swizzle atom (descriptor units
+                        // of 16 bytes, SmemDescriptor::add_start_bytes).
+                        t5::mma_f8f6f4(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0u);
+                    }
+                    t5::commit(&s.empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                t5::commit(&s.tfull[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            // All MMAs of this thread complete before TMEM is released.
+            t5::commit(&s.drain);
+            mbar_wait(&s.drain, 0);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const uint32_t q = warp & 3u;  // TMEM lane quarter this warp may access
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+            bool ok = !aborted(s) && mbar_wait(&s.tfull[acc], acc_phase);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                if (lane == 0 && !aborted(s)) fail(s, err, kDetailEpilogue | acc);
+                break;
+            }
+            t5::fence_after_thread_sync();
+            uint32_t mb, nb;
+            tile_coords(t, num_m, num_n, mb, nb);
+            const uint32_t row = mb * BM + 32 * q + lane;
+            uint16_t* crow = C + static_cast<size_t>(row) * N + nb * BN;
+            const uint32_t tbase = tmem + ((32 * q) << 16) + acc * kAccCols;
+#pragma unroll 1
+            for (uint32_t c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                t5::ld_32x32b_x32(tbase + 32 * c, r);
+                t5::wait_ld();
+                uint32_t p[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    p[j] = dt::bf16x2_from_f32(__uint_as_float(r[2 * j]) * alpha,
+                                               __uint_as_float(r[2 * j + 1]) * alpha);
+                uint4* dst = reinterpret_cast<uint4*>(crow + 32 * c);
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                    dst[v] = make_uint4(p[4 * v], p[4 * v + 1], p[4 * v + 2], p[4 * v + 3]);
+            }
+            t5::fence_before_thread_sync();
+            __syncwarp();
+            if (lane == 0) ptxstd::mbar_arrive(&s.tempty[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    t5::fence_before_thread_sync();
+    __syncthreads();
+    t5::fence_after_thread_sync();
+    if (warp == 1) t5::tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace
+
+extern "C" int ptxstd_gemm_fp8(const uint8_t* d_a, const uint8_t* d_b, float sa, float sb,
+                               uint16_t* d_c, int64_t M, int64_t N, int64_t K,
+                               ptxstd_stream stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || M % BM || N % BN || K % BK) return PTXSTD_EINVAL;
+    if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) return PTXSTD_EINVAL;
+    if (!d_a || !d_b || !d_c || !ptxstd::aligned16(d_a) || !ptxstd::aligned16(d_b) ||
+        !ptxstd::aligned16(d_c))
+        return PTXSTD_EINVAL;
+    CUtensorMap ta, tb;
+    int st = ptxstd::make_tmap_2d(&ta, d_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, K, BK, BM,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = ptxstd::make_tmap_2d(&tb, d_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, K, BK, BN,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(gemm_fp8_kernel),
+                                      static_cast<int>(kSmemBytes));
+    if (st) return st;
+    const uint32_t tiles = static_cast<uint32_t>((M / BM) * (N / BN));
+    const uint32_t grid = tiles < static_cast<uint32_t>(ptxstd::sm_count())
+                              ? tiles
+                              : static_cast<uint32_t>(ptxstd::sm_count());
+    uint32_t* err = ptxstd::device_error_word();
+    if (!err) return PTXSTD_ECUDA;
+    const float alpha = sa * sb;
+    gemm_fp8_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
+        ta, tb, d_c, static_cast<uint32_t>(M), static_cast<uint32_t>(N),
+        static_cast<uint32_t>(K), alpha, err);
+    return ptxstd::launch_status();
+}

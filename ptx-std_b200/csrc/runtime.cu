@@ -1,6 +1,8 @@
 // Library-level entry points: status strings, version, device check, and the per-device error
 // word that every bounded device-side wait reports into.
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 
@@ -49,6 +51,26 @@ int sm_count() {
         g_sm_count[d] = n;
     }
     return g_sm_count[d];
+}
+
+int set_max_dynamic_smem(const void* kernel, int bytes) {
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return PTXSTD_ECUDA;
+    static std::mutex mu;
+    static std::vector<std::pair<const void*, uint64_t>> done;  // (kernel, device mask)
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto& e : done)
+        if (e.first == kernel && (e.second >> d) & 1u) return PTXSTD_OK;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+        cudaSuccess)
+        return PTXSTD_ECUDA;
+    for (auto& e : done)
+        if (e.first == kernel) {
+            e.second |= 1ull << d;
+            return PTXSTD_OK;
+        }
+    done.emplace_back(kernel, 1ull << d);
+    return PTXSTD_OK;
 }
 
 }  // namespace ptxstd

@@ -26,6 +26,21 @@ def quantize_mxfp8(x, sf_layout: int = SF_ROWMAJOR, out=None, stream=None):
     return q, sf
 
 
+def gemm_fp8(a, b, sa: float = 1.0, sb: float = 1.0, out=None, stream=None):
+    """E4M3 codes a [M, K], b [N, K] (uint8, K contiguous) -> bf16 C [M, N] = sa*sb * a @ b^T."""
+    torch = _torch()
+    if a.dtype != torch.uint8 or b.dtype != torch.uint8 or a.dim() != 2 or b.dim() != 2:
+        raise TypeError("expected 2-D uint8 E4M3 code tensors")
+    M, K = a.shape
+    N = b.shape[0]
+    if b.shape[1] != K:
+        raise ValueError("K mismatch")
+    c = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    check(lib().ptxstd_gemm_fp8(_dev(a), _dev(b), float(sa), float(sb), _dev(c), M, N, K,
+                                _stream(stream)), "gemm_fp8")
+    return c
+
+
 def quantize_nvfp4(x, global_scale: float, sf_layout: int = SF_ROWMAJOR, out=None,
                    stream=None):
     """bf16 [rows, cols] -> (E2M1x2 [rows, cols/2] uint8, E4M3 scales per 16 uint8)."""

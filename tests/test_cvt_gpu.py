@@ -29,6 +29,7 @@ def test_decode_every_code(cuda, oracle):
     got = _to_np(dt.to_f32(dt.E2M1, codes)).view(np.uint32)
     want = oracle.decode(2, np.arange(256, dtype=np.uint8)).view(np.uint32)
     assert np.array_equal(got, want)
+    # ue8m0 widens through bf16 with a bit shift (bf16::to_f32, src/data_types/bfloat16.rs:84-86)
     got = _to_np(dt.ue8m0_to_f32(codes)).view(np.uint32)
     want = np.array([oracle.lib().ptxo_ue8m0_to_f32_via_bf16(c) for c in range(256)],
                     dtype=np.float32).view(np.uint32)
