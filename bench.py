@@ -157,7 +157,7 @@ class MxFp8Quantize:
     rows = cols = 8192
     kernel = "quantize_mxfp8_kernel"
 
-    def __init__(self):
+    def __init__(self, world: int = 1):
         self.in_bytes = self.rows * self.cols * 2
         self.out_bytes = self.rows * self.cols + self.rows * self.cols // 32
         self.bytes = self.in_bytes + self.out_bytes  # algorithmic bytes per step
@@ -232,7 +232,7 @@ class Fp8Gemm:
     peak_ratio_to_bf16 = 2.0
     peak_note = "dense FP8 = 2x bf16"
 
-    def __init__(self):
+    def __init__(self, world: int = 1):
         self.flops = 2 * self.M * self.N * self.K
         self.in_bytes = (self.M + self.N) * self.K
         self.out_bytes = self.M * self.N * 2
@@ -291,7 +291,89 @@ class Fp8Gemm:
         return 2 * rows * self.N * self.K / el / 1e12, "256x8192x8192 row block, f32 blocked GEMM"
 
 
-WORKLOADS = {"mxfp8_quantize": MxFp8Quantize, "fp8_gemm": Fp8Gemm}
+class Nvfp4Gemm:
+    """NVFP4 MLP up-projection: A [8192, 8192] x B [28672, 8192] (E2M1 + E4M3/16 + f32 global)
+    -> bf16 [8192, 28672]; B is sharded along N across ranks (no communication)."""
+
+    name = "nvfp4_gemm"
+    unit = "TFLOP/s"
+    dtype = "e2m1 x e2m1 (e4m3/16 scales) -> f32 acc -> bf16"
+    M, N, K = 8192, 28672, 8192
+    kernel = "gemm_nvfp4_kernel"
+    bound = "tensor"
+    peak_ratio_to_bf16 = 4.0
+    peak_note = "dense NVFP4 = 4x bf16"
+    scaling = "strong"
+    parallelism = "n-shard"
+
+    def __init__(self, world: int = 1):
+        self.world = world
+        self.n_local = self.N // world
+        self.flops = 2 * self.M * self.n_local * self.K
+        self.in_bytes = (self.M + self.n_local) * self.K // 2 + (self.M + self.n_local) * self.K // 16
+        self.out_bytes = self.M * self.n_local * 2
+        self.bytes = self.in_bytes + self.out_bytes
+        self.config = {"workload": "nvfp4_gemm 8192x28672x8192 (MLP up-projection) -> bf16",
+                       "M": self.M, "N": self.N, "K": self.K, "n_per_gpu": self.n_local,
+                       "sharding": "B along N, no communication",
+                       "l2": "operands 127 MiB + output 448 MiB per step (> L2)"}
+
+    def host_input(self):
+        return None
+
+    def setup(self, torch, _):
+        import ptxstd
+        rank = int(os.environ.get("RANK", "0"))
+        g = torch.Generator(device="cuda")
+        g.manual_seed(1234)
+        xa = torch.randn((self.M, self.K), generator=g, device="cuda").to(torch.bfloat16)
+        g.manual_seed(5678 + rank)
+        xb = torch.randn((self.n_local, self.K), generator=g, device="cuda").to(torch.bfloat16)
+        self.ga = float(xa.float().abs().max()) / (448.0 * 6.0)
+        self.gb = float(xb.float().abs().max()) / (448.0 * 6.0)
+        self.a, self.sfa = ptxstd.quantize_nvfp4(xa, self.ga, sf_layout=1)
+        self.b, self.sfb = ptxstd.quantize_nvfp4(xb, self.gb, sf_layout=1)
+        del xa, xb
+        self.c = torch.empty((self.M, self.n_local), dtype=torch.bfloat16, device="cuda")
+        self.host = [t.cpu().pin_memory() for t in (self.a, self.sfa, self.b, self.sfb)]
+        self.c_host = torch.empty((self.M, self.n_local), dtype=torch.bfloat16, pin_memory=True)
+
+    def step(self, i):
+        import ptxstd
+        ptxstd.gemm_nvfp4(self.a, self.sfa, self.ga, self.b, self.sfb, self.gb, out=self.c)
+        return 1
+
+    def e2e_step(self, i):
+        import ptxstd
+        for d, h in zip((self.a, self.sfa, self.b, self.sfb), self.host):
+            d.copy_(h, non_blocking=True)
+        ptxstd.gemm_nvfp4(self.a, self.sfa, self.ga, self.b, self.sfb, self.gb, out=self.c)
+        self.c_host.copy_(self.c, non_blocking=True)
+        return 1
+
+    def value(self, seconds_per_step: float) -> float:
+        return self.flops / seconds_per_step / 1e12
+
+    def cpu_sample(self, threads: int, budget_s: float):
+        """Blocked f32 GEMM over decoded values on a 128 x N x K row block."""
+        import numpy as np
+
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        rows = 128
+        rng = np.random.default_rng(7)
+        if getattr(self, "_dec", None) is None:
+            self._dec = (rng.standard_normal((rows, self.K), dtype=np.float32),
+                         rng.standard_normal((self.n_local, self.K), dtype=np.float32))
+        da, db = self._dec
+        t0 = time.perf_counter()
+        O.sgemm_nt(da, db, threads)
+        el = time.perf_counter() - t0
+        return (2 * rows * self.n_local * self.K / el / 1e12,
+                f"{rows}x{self.n_local}x{self.K} row block, f32 blocked GEMM on decoded values")
+
+
+WORKLOADS = {"mxfp8_quantize": MxFp8Quantize, "fp8_gemm": Fp8Gemm, "nvfp4_gemm": Nvfp4Gemm}
 
 
 # ---- arms -----------------------------------------------------------------------------------
@@ -372,8 +454,9 @@ def run_ours(args, wl) -> dict | None:
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
-        "data": "synthetic (seeded numpy)", "config": dict(wl.config, parallelism=f"replicas{world}"),
+        "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"), "vs_baseline": None,
+        "dtype": wl.dtype, "data": "synthetic (seeded)",
+        "config": dict(wl.config, parallelism=getattr(wl, "parallelism", "replicas") + str(world)),
         "roofline": roofline,
         "e2e": {"value": round(wl.value(e2e_max / 1e3 / args.steps) * world, 2),
                 "unit": wl.unit, "h2d_bytes_per_step": wl.in_bytes,
@@ -426,7 +509,7 @@ def main() -> int:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    wl = WORKLOADS[args.workload]()
+    wl = WORKLOADS[args.workload](int(os.environ.get("WORLD_SIZE", "1")))
     res = run_reference(args, wl) if args.impl == "reference" else run_ours(args, wl)
     if res is not None:
         print(json.dumps(res), flush=True)

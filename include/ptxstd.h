@@ -117,6 +117,17 @@ PTXSTD_API int ptxstd_quantize_nvfp4_layout(const uint16_t* d_x, int64_t rows, i
 PTXSTD_API int ptxstd_gemm_fp8(const uint8_t* d_a, const uint8_t* d_b, float sa, float sb,
                                uint16_t* d_c, int64_t M, int64_t N, int64_t K,
                                ptxstd_stream stream);
+/* NVFP4 GEMM: C[M,N] bf16 = ga * gb * sum_k (A[m,k] sfA[m,k/16]) (B[n,k] sfB[n,k/16]).
+ * A [M,K/2], B [N,K/2]: E2M1 two per byte, element 0 in the low nibble, K contiguous.
+ * sfA, sfB: E4M3 scales per 16 K elements in the blocked layout of
+ * ptxstd_quantize_nvfp4_layout(sf_layout = 1). tcgen05.mma.kind::mxf4nvf4.block_scale.block16
+ * (mma_block_scaled, src/tcgen05/mma.rs:698-724; InstrDescriptor::<Mxf4nvf4>::new,
+ * src/tcgen05/descriptor.rs:644-653; scale copy, src/tcgen05/copy.rs:76-116).
+ * M % 128 == 0, N % 256 == 0, K % 256 == 0. */
+PTXSTD_API int ptxstd_gemm_nvfp4(const uint8_t* d_a, const uint8_t* d_sfa, float ga,
+                                 const uint8_t* d_b, const uint8_t* d_sfb, float gb,
+                                 uint16_t* d_c, int64_t M, int64_t N, int64_t K,
+                                 ptxstd_stream stream);
 
 /* ---- tcgen05 descriptors (src/tcgen05/descriptor.rs) ---------------------------------------- */
 /* InstrDescriptor::<KIND>::new for each kind. Element types use the reference's discriminants:

@@ -1,0 +1,314 @@
+// NVFP4 block-scaled GEMM on the 5th-generation tensor cores:
+//   C[M, N] (bf16) = ga * gb * sum_k (A[m,k] sfA[m,k/16]) (B[n,k] sfB[n,k/16])
+// with A [M, K/2] and B [N, K/2] E2M1 packed two per byte (element 0 in the low nibble, K
+// contiguous), E4M3 scales per 16 K elements in the blocked 128x4 layout, f32 global scales ga and
+// gb, fp32 accumulation and bf16 RN output. tcgen05.mma.kind::mxf4nvf4.block_scale.block16 (the
+// reference's mma_block_scaled with ScaleVectorSize::Block16, src/tcgen05/mma.rs:698-724;
+// InstrDescriptor::<Mxf4nvf4>::new(Ue4m3, 128, 256), src/tcgen05/descriptor.rs:644-653).
+//
+// Per 256-element K stage the producer issues two TMA tile loads (A 128 rows x 128 bytes, B 256
+// rows x 128 bytes, 128-byte swizzle) and three 1-D bulk copies of scales: in the blocked layout
+// the four 512-byte scale tiles of one 128-row block and one stage are contiguous, so A's scales
+// are one 2 KiB copy and B's two. The MMA thread moves each 512-byte tile to TMEM with
+// tcgen05.cp.32x128b.warpx4 (src/tcgen05/copy.rs:29-30, :76-116) — 32 lanes x 16 bytes
+// replicated to the four lane quarters, which is the scale layout the MMA reads — and issues the
+// four K=64 MMAs of the stage. Scale slots in TMEM are per (stage, MMA), so a slot is rewritten
+// only after the stage's `empty` barrier has observed the completion of the MMAs that read it.
+//
+// TMEM: accumulator 128 lanes x 256 f32 columns, plus 4 stages x 4 MMAs x (4 + 8) scale columns.
+// The accumulator is single-buffered; eight epilogue warps (two per lane quarter, 128 columns
+// each) copy it to registers and release it before converting and storing, so the next tile's
+// MMAs wait only for the TMEM reads.
+#include "common.cuh"
+#include "data_types.cuh"
+#include "tcgen05.cuh"
+#include "tma_host.h"
+
+namespace {
+
+namespace t5 = ptxstd::tcgen05;
+namespace dt = ptxstd::data_types;
+using ptxstd::mbar_wait;
+
+constexpr uint32_t BM = 128, BN = 256;
+constexpr uint32_t BKB = 128;          // K bytes per stage
+constexpr uint32_t BK = 2 * BKB;       // K elements per stage (256)
+constexpr uint32_t kMmaK = 64;         // K elements of one mxf4nvf4 MMA
+constexpr uint32_t kMmas = BK / kMmaK; // 4 per stage
+constexpr uint32_t STAGES = 4;
+constexpr uint32_t kEpiWarps = 8;
+constexpr uint32_t kThreads = 64 + 32 * kEpiWarps;
+constexpr uint32_t kABytes = BM * BKB;
+constexpr uint32_t kBBytes = BN * BKB;
+constexpr uint32_t kSfaBytes = (BM / 128) * kMmas * 512;  // 2048
+constexpr uint32_t kSfbBytes = (BN / 128) * kMmas * 512;  // 4096
+constexpr uint32_t kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+constexpr uint32_t kAccCols = BN;
+constexpr uint32_t kSfaCols = 4 * (BM / 128);  // per MMA
+constexpr uint32_t kSfbCols = 4 * (BN / 128);  // per MMA
+constexpr uint32_t kSfSlotCols = kSfaCols + kSfbCols;
+constexpr uint32_t kSfBase = kAccCols;
+constexpr uint32_t kTmemCols = 512;
+static_assert(kSfBase + STAGES * kMmas * kSfSlotCols <= kTmemCols, "TMEM budget");
+constexpr uint32_t kGroupM = 8;
+
+struct alignas(1024) Smem {
+    uint8_t a[STAGES][kABytes];
+    uint8_t b[STAGES][kBBytes];
+    uint8_t sfa[STAGES][kSfaBytes];
+    uint8_t sfb[STAGES][kSfbBytes];
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t tfull;
+    uint64_t tempty;
+    uint64_t drain;
+    uint32_t tmem_base;
+    uint32_t abort;
+};
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+enum : uint32_t { kDetailProducer = 0x1100, kDetailMma = 0x1200, kDetailEpilogue = 0x1300 };
+
+__device__ __forceinline__ void tile_coords(uint32_t t, uint32_t num_m, uint32_t num_n,
+                                            uint32_t& mb, uint32_t& nb) {
+    const uint32_t group_tiles = kGroupM * num_n;
+    const uint32_t g = t / group_tiles;
+    const uint32_t first_m = g * kGroupM;
+    const uint32_t gm = min(num_m - first_m, kGroupM);
+    const uint32_t local = t - g * group_tiles;
+    mb = first_m + local % gm;
+    nb = local / gm;
+}
+
+__device__ __forceinline__ void fail(Smem& s, uint32_t* err, uint32_t detail) {
+    ptxstd::record_error(err, PTXSTD_ETIMEOUT, detail);
+    *reinterpret_cast<volatile uint32_t*>(&s.abort) = 1u;
+}
+__device__ __forceinline__ bool aborted(Smem& s) {
+    return *reinterpret_cast<volatile uint32_t*>(&s.abort) != 0u;
+}
+
+// cp.async.bulk global -> this CTA's smem, completing on `bar` (tma::bulk_load, src/tma/bulk.rs:60).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(ptxstd::smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(ptxstd::smem_u32(bar))
+        : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB, const uint8_t* __restrict__ sfA,
+                      const uint8_t* __restrict__ sfB, uint16_t* __restrict__ C, uint32_t M,
+                      uint32_t N, uint32_t K, float alpha, uint32_t* err) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                       ~static_cast<uintptr_t>(1023));
+    const uint32_t warp = ptxstd::warp_id();
+    const uint32_t lane = ptxstd::lane_id();
+    const uint32_t num_m = M / BM, num_n = N / BN, num_tiles = num_m * num_n, num_k = K / BK;
+    const uint32_t sf_tiles_per_row = K / 64;  // 512-byte scale tiles per 128-row block
+
+    if (warp == 0 && lane == 0) {
+        ptxstd::prefetch_tensormap(&tmA);
+        ptxstd::prefetch_tensormap(&tmB);
+        for (uint32_t i = 0; i < STAGES; ++i) {
+            ptxstd::mbar_init(&s.full[i], 1);
+            ptxstd::mbar_init(&s.empty[i], 1);
+        }
+        ptxstd::mbar_init(&s.tfull, 1);
+        ptxstd::mbar_init(&s.tempty, kEpiWarps);
+        ptxstd::mbar_init(&s.drain, 1);
+        s.abort = 0;
+        ptxstd::fence_mbarrier_init();
+    }
+    if (warp == 1) {
+        t5::tmem_alloc(&s.tmem_base, kTmemCols);
+        t5::tmem_relinquish();
+    }
+    t5::fence_before_thread_sync();
+    __syncthreads();
+    t5::fence_after_thread_sync();
+    const uint32_t tmem = s.tmem_base;
+
+    if (warp == 0) {
+        // ---------------- producer: TMA tiles + bulk scale copies ----------------
+        if (ptxstd::elect_one()) {
+            uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
+            for (uint32_t t = blockIdx.x; t < num_tiles && !aborted(s); t += gridDim.x) {
+                uint32_t mb, nb;
+                tile_coords(t, num_m, num_n, mb, nb);
+                for (uint32_t kb = 0; kb < num_k; ++kb) {
+                    if (!mbar_wait(&s.empty[stage], phase ^ 1u)) {
+                        fail(s, err, kDetailProducer | stage);
+                        break;
+                    }
+                    if (aborted(s)) break;
+                    ptxstd::mbar_arrive_expect_tx(&s.full[stage], kStageBytes);
+                    ptxstd::tma_load_2d(s.a[stage], &tmA, &s.full[stage],
+                                        static_cast<int32_t>(kb * BKB), static_cast<int32_t>(mb * BM));
+                    ptxstd::tma_load_2d(s.b[stage], &tmB, &s.full[stage],
+                                        static_cast<int32_t>(kb * BKB), static_cast<int32_t>(nb * BN));
+                    const size_t ktile = static_cast<size_t>(kb) * kMmas;
+                    bulk_load(s.sfa[stage], sfA + (static_cast<size_t>(mb) * sf_tiles_per_row + ktile) * 512,
+                              kSfaBytes, &s.full[stage]);
+#pragma unroll
+                    for (uint32_t j = 0; j < BN / 128; ++j) {
+                        const size_t rt = static_cast<size_t>(nb) * (BN / 128) + j;
+                        bulk_load(s.sfb[stage] + j * (kMmas * 512),
+                                  sfB + (rt * sf_tiles_per_row + ktile) * 512, kMmas * 512,
+                                  &s.full[stage]);
+                    }
+                    issued |= 1u << stage;
+                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (aborted(s)) {
+                for (uint32_t i = 0; i < STAGES; ++i)
+                    if (issued & (1u << i)) mbar_wait(&s.full[i], (issued_parity >> i) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (ptxstd::elect_one()) {
+            uint32_t idesc = 0;
+            t5::idesc_mxf4nvf4(/*Ue4m3*/ 0, BM, BN, idesc);
+            uint32_t stage = 0, phase = 0, acc_phase = 0;
+            for (uint32_t t = blockIdx.x; t < num_tiles && !aborted(s); t += gridDim.x) {
+                if (!mbar_wait(&s.tempty, acc_phase ^ 1u)) {
+                    fail(s, err, kDetailMma | 0x10);
+                    break;
+                }
+                t5::fence_after_thread_sync();
+                bool ok = true;
+                for (uint32_t kb = 0; kb < num_k; ++kb) {
+                    if (!mbar_wait(&s.full[stage], phase)) {
+                        fail(s, err, kDetailMma | stage);
+                        ok = false;
+                        break;
+                    }
+                    t5::fence_after_thread_sync();
+                    const uint64_t ad = t5::smem_desc_k128(ptxstd::smem_u32(s.a[stage]));
+                    const uint64_t bd = t5::smem_desc_k128(ptxstd::smem_u32(s.b[stage]));
+#pragma unroll
+                    for (uint32_t j = 0; j < kMmas; ++j) {
+                        const uint32_t slot = tmem + kSfBase + (stage * kMmas + j) * kSfSlotCols;
+                        const uint32_t sfa_t = slot;
+                        const uint32_t sfb_t = slot + kSfaCols;
+                        t5::cp_32x128b_warpx4(
+                            sfa_t, t5::smem_desc_nosw(ptxstd::smem_u32(s.sfa[stage] + 512 * j), 0, 128));
+#pragma unroll
+                        for (uint32_t h = 0; h < BN / 128; ++h)
+                            t5::cp_32x128b_warpx4(
+                                sfb_t + 4 * h,
+                                t5::smem_desc_nosw(
+                                    ptxstd::smem_u32(s.sfb[stage] + h * (kMmas * 512) + 512 * j), 0,
+                                    128));
+                        t5::mma_mxf4nvf4_block16(tmem, ad + 2 * j, bd + 2 * j, idesc, sfa_t, sfb_t,
+                                                 (kb | j) != 0u);
+                    }
+                    t5::commit(&s.empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                t5::commit(&s.tfull);
+                acc_phase ^= 1u;
+            }
+            t5::commit(&s.drain);
+            mbar_wait(&s.drain, 0);
+        }
+    } else {
+        // ---------------- epilogue: warps 2..9 ----------------
+        const uint32_t q = warp & 3u;              // TMEM lane quarter
+        const uint32_t half = (warp - 2u) >> 2;    // which 128 columns
+        uint32_t acc_phase = 0;
+        for (uint32_t t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+            bool ok = !aborted(s) && mbar_wait(&s.tfull, acc_phase);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                if (lane == 0 && !aborted(s)) fail(s, err, kDetailEpilogue);
+                break;
+            }
+            t5::fence_after_thread_sync();
+            uint32_t r[128];
+            const uint32_t tbase = tmem + ((32 * q) << 16) + half * 128;
+            {
+                uint32_t(&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
+                uint32_t(&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
+                uint32_t(&r2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[64]);
+                uint32_t(&r3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[96]);
+                t5::ld_32x32b_x32(tbase, r0);
+                t5::ld_32x32b_x32(tbase + 32, r1);
+                t5::ld_32x32b_x32(tbase + 64, r2);
+                t5::ld_32x32b_x32(tbase + 96, r3);
+                t5::wait_ld();
+            }
+            t5::fence_before_thread_sync();
+            __syncwarp();
+            if (lane == 0) ptxstd::mbar_arrive(&s.tempty);
+            acc_phase ^= 1u;
+
+            uint32_t mb, nb;
+            tile_coords(t, num_m, num_n, mb, nb);
+            const uint32_t row = mb * BM + 32 * q + lane;
+            uint16_t* crow = C + static_cast<size_t>(row) * N + nb * BN + half * 128;
+#pragma unroll
+            for (uint32_t c = 0; c < 16; ++c) {
+                uint32_t p[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    p[j] = dt::bf16x2_from_f32(__uint_as_float(r[8 * c + 2 * j]) * alpha,
+                                               __uint_as_float(r[8 * c + 2 * j + 1]) * alpha);
+                reinterpret_cast<uint4*>(crow)[c] = make_uint4(p[0], p[1], p[2], p[3]);
+            }
+        }
+    }
+
+    t5::fence_before_thread_sync();
+    __syncthreads();
+    t5::fence_after_thread_sync();
+    if (warp == 1) t5::tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace
+
+extern "C" int ptxstd_gemm_nvfp4(const uint8_t* d_a, const uint8_t* d_sfa, float ga,
+                                 const uint8_t* d_b, const uint8_t* d_sfb, float gb,
+                                 uint16_t* d_c, int64_t M, int64_t N, int64_t K,
+                                 ptxstd_stream stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || M % BM || N % BN || K % BK) return PTXSTD_EINVAL;
+    if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) return PTXSTD_EINVAL;
+    if (!d_a || !d_b || !d_c || !d_sfa || !d_sfb || !ptxstd::aligned16(d_a) ||
+        !ptxstd::aligned16(d_b) || !ptxstd::aligned16(d_c) || !ptxstd::aligned16(d_sfa) ||
+        !ptxstd::aligned16(d_sfb))
+        return PTXSTD_EINVAL;
+    CUtensorMap ta, tb;
+    int st = ptxstd::make_tmap_2d(&ta, d_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, M, K / 2, BKB,
+                                  BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = ptxstd::make_tmap_2d(&tb, d_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, BKB, BN,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(gemm_nvfp4_kernel),
+                                      static_cast<int>(kSmemBytes));
+    if (st) return st;
+    const uint32_t tiles = static_cast<uint32_t>((M / BM) * (N / BN));
+    const uint32_t sms = static_cast<uint32_t>(ptxstd::sm_count());
+    const uint32_t grid = tiles < sms ? tiles : sms;
+    uint32_t* err = ptxstd::device_error_word();
+    if (!err) return PTXSTD_ECUDA;
+    gemm_nvfp4_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
+        ta, tb, d_sfa, d_sfb, d_c, static_cast<uint32_t>(M), static_cast<uint32_t>(N),
+        static_cast<uint32_t>(K), ga * gb, err);
+    return ptxstd::launch_status();
+}

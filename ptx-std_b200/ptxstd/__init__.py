@@ -57,6 +57,9 @@ _SIGS = {
                                                C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
     "ptxstd_gemm_fp8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_float, C.c_float, C.c_void_p,
                                   C.c_int64, C.c_int64, C.c_int64, C.c_void_p]),
+    "ptxstd_gemm_nvfp4": (C.c_int, [C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p,
+                                    C.c_float, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
+                                    C.c_void_p]),
     "ptxstd_idesc_f16": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_uint32, C.c_uint32,
                                    C.POINTER(C.c_uint32)]),
     "ptxstd_idesc_tf32": (C.c_int, [C.c_uint32, C.c_uint32, C.POINTER(C.c_uint32)]),
@@ -139,7 +142,7 @@ def last_device_error(clear: bool = True, stream=None) -> tuple[int, int]:
 
 
 from . import data_types, tcgen05  # noqa: E402
-from .kernels import gemm_fp8, quantize_mxfp8, quantize_nvfp4  # noqa: E402
+from .kernels import gemm_fp8, gemm_nvfp4, quantize_mxfp8, quantize_nvfp4  # noqa: E402
 
 __all__ = ["lib", "check", "PtxStdError", "status_string", "last_device_error", "data_types",
-           "tcgen05", "quantize_mxfp8", "quantize_nvfp4", "gemm_fp8"]
+           "tcgen05", "quantize_mxfp8", "quantize_nvfp4", "gemm_fp8", "gemm_nvfp4"]

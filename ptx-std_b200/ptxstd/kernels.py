@@ -41,6 +41,22 @@ def gemm_fp8(a, b, sa: float = 1.0, sb: float = 1.0, out=None, stream=None):
     return c
 
 
+def gemm_nvfp4(a, sfa, ga: float, b, sfb, gb: float, out=None, stream=None):
+    """NVFP4 a [M, K/2], b [N, K/2] (uint8, E2M1x2) with blocked E4M3 scales -> bf16 [M, N]."""
+    torch = _torch()
+    M, Kh = a.shape
+    N = b.shape[0]
+    if b.shape[1] != Kh:
+        raise ValueError("K mismatch")
+    K = 2 * Kh
+    if sfa.numel() != M * K // 16 or sfb.numel() != N * K // 16:
+        raise ValueError("scale tensors must hold one E4M3 per 16 elements")
+    c = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    check(lib().ptxstd_gemm_nvfp4(_dev(a), _dev(sfa), float(ga), _dev(b), _dev(sfb), float(gb),
+                                  _dev(c), M, N, K, _stream(stream)), "gemm_nvfp4")
+    return c
+
+
 def quantize_nvfp4(x, global_scale: float, sf_layout: int = SF_ROWMAJOR, out=None,
                    stream=None):
     """bf16 [rows, cols] -> (E2M1x2 [rows, cols/2] uint8, E4M3 scales per 16 uint8)."""
