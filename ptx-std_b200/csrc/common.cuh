@@ -122,6 +122,16 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* m
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
         : "memory");
 }
+// bulk_load (src/tma/bulk.rs:60): `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// global -> this CTA's smem, completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
 // tma_store_tile::<2> (:746): smem -> global, tracked by the bulk async-group.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t c0,
                                              int32_t c1) {

@@ -89,15 +89,7 @@ __device__ __forceinline__ bool aborted(Smem& s) {
     return *reinterpret_cast<volatile uint32_t*>(&s.abort) != 0u;
 }
 
-// cp.async.bulk global -> this CTA's smem, completing on `bar` (tma::bulk_load, src/tma/bulk.rs:60).
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-            "r"(ptxstd::smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(ptxstd::smem_u32(bar))
-        : "memory");
-}
+using ptxstd::bulk_load;
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA,

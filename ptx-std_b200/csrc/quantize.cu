@@ -1,18 +1,46 @@
 // Quantise/pack kernels: bf16 activations -> MXFP8 (E4M3 + UE8M0 per 32) and NVFP4 (E2M1 + E4M3
-// per 16, f32 global scale). HBM-bound: each thread streams 16-byte vectors (8 bf16) with
-// non-allocating loads, four vectors in flight per thread; the lanes holding one block combine
-// their amax with shuffle-xor, and every element pair is packed by one `cvt` instruction
-// (ptx-std src/data_types/narrow.rs:156-162). Outputs are written as whole 8-byte (MXFP8) or
-// 4-byte (NVFP4) words per lane, so each warp store covers a contiguous 256 / 128 bytes.
+// per 16, f32 global scale). HBM-bound, so the kernel is built around bytes in flight:
+//
+//   - a persistent grid of one CTA per SM walks 16 KiB chunks of the flat input (8192 bf16);
+//   - one producer lane streams each chunk into an 8-stage shared-memory ring with a 1-D bulk
+//     async copy (cp.async.bulk, ptx-std src/tma/bulk.rs:60) that completes on the stage's
+//     mbarrier (arrive_expect_tx, src/mbarrier.rs:533) — up to 128 KiB in flight per SM with no
+//     register cost;
+//   - eight consumer warps read the stage with 16-byte shared loads, lane l of warp w taking
+//     vector (w * 32 + l) of each 256-vector row so that every warp load is one contiguous,
+//     conflict-free 512-byte row; the lanes holding one block (4 for MXFP8, 2 for NVFP4) combine
+//     their amax with shuffle-xor; each element pair is packed by one `cvt` instruction
+//     (src/data_types/narrow.rs:156-162); payload words go straight to global memory as 8-byte
+//     (MXFP8) or 4-byte (NVFP4) stores, so a warp store covers 256 / 128 contiguous bytes;
+//   - consumers release a stage with one arrive per warp on its `empty` barrier.
+//
+// Every wait is bounded; a timeout records PTXSTD_ETIMEOUT, and the producer drains its copies
+// before the CTA exits.
 #include "common.cuh"
 #include "data_types.cuh"
 
 namespace dt = ptxstd::data_types;
+using ptxstd::mbar_wait;
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kUnroll = 4;  // 16-byte vectors in flight per thread
+constexpr uint32_t kChunkElems = 8192;              // bf16 per stage (16 KiB)
+constexpr uint32_t kChunkBytes = kChunkElems * 2;
+constexpr uint32_t kChunkVecs = kChunkElems / 8;     // 16-byte vectors per stage
+constexpr uint32_t kStages = 8;
+constexpr uint32_t kConsumerWarps = 8;
+constexpr uint32_t kThreads = 32 * (kConsumerWarps + 1);
+constexpr uint32_t kVecsPerLane = kChunkVecs / (32 * kConsumerWarps);  // 4
+
+struct alignas(128) Smem {
+    uint8_t buf[kStages][kChunkBytes];
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    uint32_t abort;
+};
+constexpr size_t kSmemBytes = sizeof(Smem) + 128;
+
+enum : uint32_t { kDetailProducer = 0x2100, kDetailConsumer = 0x2200 };
 
 // Offset of scale (r, s) in the blocked "128x4" layout consumed by the block-scaled GEMMs: tiles
 // of 128 rows x 4 scale columns stored as 512 contiguous bytes, row-tile major; inside a tile the
@@ -23,112 +51,169 @@ __device__ __forceinline__ size_t blocked_sf_offset(size_t r, size_t s, size_t s
     return tile * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (s & 3);
 }
 
-// One MXFP8 block is 32 bf16 = 4 vectors = 4 consecutive lanes. Vector v of the flat tensor
-// covers elements 8v .. 8v+7; block b = v / 4.
 template <bool BLOCKED>
-__global__ void __launch_bounds__(kThreads) quantize_mxfp8_kernel(
-    const uint4* __restrict__ x, size_t n_vec, uint2* __restrict__ q, uint8_t* __restrict__ sf,
-    size_t sf_cols) {
-    const uint32_t lane = threadIdx.x & 31u;
-    const size_t warp = (static_cast<size_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-    const size_t n_warps = (static_cast<size_t>(gridDim.x) * kThreads) >> 5;
-    const size_t chunk = 32 * kUnroll;  // vectors per warp step
-    for (size_t base = warp * chunk; base < n_vec; base += n_warps * chunk) {
-        uint4 v[kUnroll];
+__device__ __forceinline__ void store_scale(uint8_t* sf, size_t b, size_t sf_cols, uint32_t code) {
+    if constexpr (BLOCKED)
+        sf[blocked_sf_offset(b / sf_cols, b % sf_cols, sf_cols)] = static_cast<uint8_t>(code);
+    else
+        sf[b] = static_cast<uint8_t>(code);
+}
+
+// Per-vector work of the two formats. `w` holds 8 bf16; `gv` is the vector's flat index.
+template <bool BLOCKED>
+struct Mxfp8 {
+    static constexpr uint32_t kLanesPerBlock = 4;  // 32 elements
+    float six_g;  // unused
+    __device__ __forceinline__ void operator()(const uint4 v, bool valid, size_t gv, uint32_t lane,
+                                               uint8_t* q, uint8_t* sf, size_t sf_cols) const {
+        uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                              dt::bf16x2_absmax_bits(v.z, v.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        const uint32_t code = dt::mxfp8_scale_code(__uint_as_float(m << 16));
+        const float inv = dt::ue8m0_inverse(code);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t p[4];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const size_t i = base + 32 * u + lane;
-            v[u] = i < n_vec ? ptxstd::ld_stream_v4(x + i) : make_uint4(0, 0, 0, 0);
+        for (int k = 0; k < 4; ++k)
+            p[k] = dt::e4m3x2_from_f32<false>(__fmul_rn(dt::bf16_lo(w[k]), inv),
+                                              __fmul_rn(dt::bf16_hi(w[k]), inv));
+        if (valid) {
+            reinterpret_cast<uint2*>(q)[gv] = make_uint2(p[0] | (p[1] << 16), p[2] | (p[3] << 16));
+            if ((lane & 3u) == 0) store_scale<BLOCKED>(sf, gv >> 2, sf_cols, code);
         }
+    }
+};
+
+template <bool BLOCKED>
+struct Nvfp4 {
+    static constexpr uint32_t kLanesPerBlock = 2;  // 16 elements
+    float g, six_g;
+    __device__ __forceinline__ void operator()(const uint4 v, bool valid, size_t gv, uint32_t lane,
+                                               uint8_t* q, uint8_t* sf, size_t sf_cols) const {
+        uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                              dt::bf16x2_absmax_bits(v.z, v.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        // sf = e4m3(amax / (6 g)); r = 1 / (sf * g), or 0 when that product is 0.
+        const float s = __fdiv_rn(__uint_as_float(m << 16), six_g);
+        const uint32_t code = dt::e4m3x2_from_f32<false>(s, 0.0f) & 0xFFu;
+        const float t = __fmul_rn(dt::e4m3_to_f32(code), g);
+        const float r = (t == 0.0f) ? 0.0f : __frcp_rn(t);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t packed = 0;
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const size_t i = base + 32 * u + lane;
-            uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v[u].x, v[u].y),
-                                                  dt::bf16x2_absmax_bits(v[u].z, v[u].w)));
-            m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
-            m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
-            const float amax = __uint_as_float(m << 16);
-            const uint32_t code = dt::mxfp8_scale_code(amax);
-            const float inv = dt::ue8m0_inverse(code);
-            const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-            uint32_t p[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                p[k] = dt::e4m3x2_from_f32<false>(__fmul_rn(dt::bf16_lo(w[k]), inv),
-                                                  __fmul_rn(dt::bf16_hi(w[k]), inv));
-            if (i < n_vec) {
-                q[i] = make_uint2(p[0] | (p[1] << 16), p[2] | (p[3] << 16));
-                if ((lane & 3u) == 0) {
-                    const size_t b = i >> 2;
-                    if constexpr (BLOCKED) {
-                        sf[blocked_sf_offset(b / sf_cols, b % sf_cols, sf_cols)] =
-                            static_cast<uint8_t>(code);
-                    } else {
-                        sf[b] = static_cast<uint8_t>(code);
-                    }
+        for (int k = 0; k < 4; ++k)
+            packed |= dt::e2m1x2_from_f32<false>(__fmul_rn(dt::bf16_lo(w[k]), r),
+                                                 __fmul_rn(dt::bf16_hi(w[k]), r))
+                      << (8 * k);
+        if (valid) {
+            reinterpret_cast<uint32_t*>(q)[gv] = packed;
+            if ((lane & 1u) == 0) store_scale<BLOCKED>(sf, gv >> 1, sf_cols, code);
+        }
+    }
+};
+
+template <class Op>
+__global__ void __launch_bounds__(kThreads, 1)
+    quantize_kernel(const uint16_t* __restrict__ x, size_t n_elems, Op op, uint8_t* __restrict__ q,
+                    uint8_t* __restrict__ sf, size_t sf_cols, uint32_t* err) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                       ~static_cast<uintptr_t>(127));
+    const uint32_t warp = ptxstd::warp_id();
+    const uint32_t lane = ptxstd::lane_id();
+    const size_t n_chunks = (n_elems + kChunkElems - 1) / kChunkElems;
+    const size_t n_vec = n_elems / 8;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t i = 0; i < kStages; ++i) {
+            ptxstd::mbar_init(&s.full[i], 1);
+            ptxstd::mbar_init(&s.empty[i], kConsumerWarps);
+        }
+        s.abort = 0;
+        ptxstd::fence_mbarrier_init();
+    }
+    __syncthreads();
+    volatile uint32_t* abort_flag = &s.abort;
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
+            for (size_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+                if (!mbar_wait(&s.empty[stage], phase ^ 1u)) {
+                    ptxstd::record_error(err, PTXSTD_ETIMEOUT, kDetailProducer | stage);
+                    *abort_flag = 1u;
+                    break;
                 }
+                if (*abort_flag) break;
+                const size_t e0 = c * kChunkElems;
+                const uint32_t bytes =
+                    static_cast<uint32_t>(min(static_cast<size_t>(kChunkElems), n_elems - e0) * 2);
+                ptxstd::mbar_arrive_expect_tx(&s.full[stage], bytes);
+                ptxstd::bulk_load(s.buf[stage], x + e0, bytes, &s.full[stage]);
+                issued |= 1u << stage;
+                issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (*abort_flag) {
+                for (uint32_t i = 0; i < kStages; ++i)
+                    if (issued & (1u << i)) mbar_wait(&s.full[i], (issued_parity >> i) & 1u);
+            }
+        }
+    } else {
+        // ---------------- consumers ----------------
+        uint32_t stage = 0, phase = 0;
+        for (size_t c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+            bool ok = !*abort_flag && mbar_wait(&s.full[stage], phase);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                if (lane == 0 && !*abort_flag) {
+                    ptxstd::record_error(err, PTXSTD_ETIMEOUT, kDetailConsumer | stage);
+                    *abort_flag = 1u;
+                }
+                break;
+            }
+            const uint4* buf = reinterpret_cast<const uint4*>(s.buf[stage]);
+            const size_t v0 = c * kChunkVecs;
+            uint4 v[kVecsPerLane];
+#pragma unroll
+            for (uint32_t j = 0; j < kVecsPerLane; ++j) {
+                const uint32_t lv = (j * kConsumerWarps + warp) * 32 + lane;
+                v[j] = (v0 + lv < n_vec) ? buf[lv] : make_uint4(0, 0, 0, 0);
+            }
+            __syncwarp();
+            if (lane == 0) ptxstd::mbar_arrive(&s.empty[stage]);
+#pragma unroll
+            for (uint32_t j = 0; j < kVecsPerLane; ++j) {
+                const uint32_t lv = (j * kConsumerWarps + warp) * 32 + lane;
+                op(v[j], v0 + lv < n_vec, v0 + lv, lane, q, sf, sf_cols);
+            }
+            if (++stage == kStages) {
+                stage = 0;
+                phase ^= 1u;
             }
         }
     }
 }
 
-// One NVFP4 block is 16 bf16 = 2 vectors = 2 consecutive lanes.
-template <bool BLOCKED>
-__global__ void __launch_bounds__(kThreads) quantize_nvfp4_kernel(
-    const uint4* __restrict__ x, size_t n_vec, float g, uint32_t* __restrict__ q,
-    uint8_t* __restrict__ sf, size_t sf_cols) {
-    const uint32_t lane = threadIdx.x & 31u;
-    const size_t warp = (static_cast<size_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-    const size_t n_warps = (static_cast<size_t>(gridDim.x) * kThreads) >> 5;
-    const size_t chunk = 32 * kUnroll;
-    const float six_g = __fmul_rn(6.0f, g);
-    for (size_t base = warp * chunk; base < n_vec; base += n_warps * chunk) {
-        uint4 v[kUnroll];
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const size_t i = base + 32 * u + lane;
-            v[u] = i < n_vec ? ptxstd::ld_stream_v4(x + i) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const size_t i = base + 32 * u + lane;
-            uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v[u].x, v[u].y),
-                                                  dt::bf16x2_absmax_bits(v[u].z, v[u].w)));
-            m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
-            const float amax = __uint_as_float(m << 16);
-            // sf = e4m3(amax / (6 g)); r = 1 / (sf * g), or 0 when that product is 0.
-            const float s = __fdiv_rn(amax, six_g);
-            const uint32_t code = dt::e4m3x2_from_f32<false>(s, 0.0f) & 0xFFu;
-            const float t = __fmul_rn(dt::e4m3_to_f32(code), g);
-            const float r = (t == 0.0f) ? 0.0f : __frcp_rn(t);
-            const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-            uint32_t packed = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                packed |= dt::e2m1x2_from_f32<false>(__fmul_rn(dt::bf16_lo(w[k]), r),
-                                                     __fmul_rn(dt::bf16_hi(w[k]), r))
-                          << (8 * k);
-            if (i < n_vec) {
-                q[i] = packed;
-                if ((lane & 1u) == 0) {
-                    const size_t b = i >> 1;
-                    if constexpr (BLOCKED) {
-                        sf[blocked_sf_offset(b / sf_cols, b % sf_cols, sf_cols)] =
-                            static_cast<uint8_t>(code);
-                    } else {
-                        sf[b] = static_cast<uint8_t>(code);
-                    }
-                }
-            }
-        }
-    }
-}
-
-int grid_for(size_t n_vec) {
-    const size_t per_block = static_cast<size_t>(kThreads) * kUnroll;
-    const size_t need = (n_vec + per_block - 1) / per_block;
-    const size_t cap = static_cast<size_t>(ptxstd::sm_count()) * (2048 / kThreads);
-    return static_cast<int>(need == 0 ? 1 : (need < cap ? need : cap));
+template <class Op>
+int launch(const uint16_t* x, size_t n_elems, Op op, uint8_t* q, uint8_t* sf, size_t sf_cols,
+           cudaStream_t stream) {
+    int st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(quantize_kernel<Op>),
+                                          static_cast<int>(kSmemBytes));
+    if (st) return st;
+    uint32_t* err = ptxstd::device_error_word();
+    if (!err) return PTXSTD_ECUDA;
+    const size_t chunks = (n_elems + kChunkElems - 1) / kChunkElems;
+    const size_t sms = static_cast<size_t>(ptxstd::sm_count());
+    const int grid = static_cast<int>(chunks < sms ? chunks : sms);
+    quantize_kernel<Op><<<grid, kThreads, kSmemBytes, stream>>>(x, n_elems, op, q, sf, sf_cols,
+                                                                err);
+    return ptxstd::launch_status();
 }
 
 }  // namespace
@@ -142,19 +227,11 @@ int ptxstd_quantize_mxfp8_layout(const uint16_t* d_x, int64_t rows, int64_t cols
         return PTXSTD_EINVAL;
     if (sf_layout != 0 && sf_layout != 1) return PTXSTD_EINVAL;
     if (sf_layout == 1 && (rows % 128 != 0 || cols % 128 != 0)) return PTXSTD_EINVAL;
-    const size_t n_vec = static_cast<size_t>(rows) * static_cast<size_t>(cols) / 8;
+    const size_t n = static_cast<size_t>(rows) * static_cast<size_t>(cols);
     const size_t sf_cols = static_cast<size_t>(cols) / 32;
     auto s = static_cast<cudaStream_t>(stream);
-    const int g = grid_for(n_vec);
-    if (sf_layout == 1)
-        quantize_mxfp8_kernel<true><<<g, kThreads, 0, s>>>(reinterpret_cast<const uint4*>(d_x),
-                                                          n_vec, reinterpret_cast<uint2*>(d_q),
-                                                          d_sf, sf_cols);
-    else
-        quantize_mxfp8_kernel<false><<<g, kThreads, 0, s>>>(reinterpret_cast<const uint4*>(d_x),
-                                                           n_vec, reinterpret_cast<uint2*>(d_q),
-                                                           d_sf, sf_cols);
-    return ptxstd::launch_status();
+    if (sf_layout == 1) return launch(d_x, n, Mxfp8<true>{0.0f}, d_q, d_sf, sf_cols, s);
+    return launch(d_x, n, Mxfp8<false>{0.0f}, d_q, d_sf, sf_cols, s);
 }
 
 int ptxstd_quantize_mxfp8(const uint16_t* d_x, int64_t rows, int64_t cols, uint8_t* d_q,
@@ -171,19 +248,14 @@ int ptxstd_quantize_nvfp4_layout(const uint16_t* d_x, int64_t rows, int64_t cols
         return PTXSTD_EINVAL;
     if (sf_layout != 0 && sf_layout != 1) return PTXSTD_EINVAL;
     if (sf_layout == 1 && (rows % 128 != 0 || cols % 64 != 0)) return PTXSTD_EINVAL;
-    const size_t n_vec = static_cast<size_t>(rows) * static_cast<size_t>(cols) / 8;
+    const size_t n = static_cast<size_t>(rows) * static_cast<size_t>(cols);
     const size_t sf_cols = static_cast<size_t>(cols) / 16;
     auto s = static_cast<cudaStream_t>(stream);
-    const int g = grid_for(n_vec);
+    // six_g = 6 * g as one IEEE rounding, as in the recipe.
+    const float six_g = 6.0f * global_scale;
     if (sf_layout == 1)
-        quantize_nvfp4_kernel<true><<<g, kThreads, 0, s>>>(
-            reinterpret_cast<const uint4*>(d_x), n_vec, global_scale,
-            reinterpret_cast<uint32_t*>(d_q), d_sf, sf_cols);
-    else
-        quantize_nvfp4_kernel<false><<<g, kThreads, 0, s>>>(
-            reinterpret_cast<const uint4*>(d_x), n_vec, global_scale,
-            reinterpret_cast<uint32_t*>(d_q), d_sf, sf_cols);
-    return ptxstd::launch_status();
+        return launch(d_x, n, Nvfp4<true>{global_scale, six_g}, d_q, d_sf, sf_cols, s);
+    return launch(d_x, n, Nvfp4<false>{global_scale, six_g}, d_q, d_sf, sf_cols, s);
 }
 
 int ptxstd_quantize_nvfp4(const uint16_t* d_x, int64_t rows, int64_t cols, float global_scale,
