@@ -373,7 +373,104 @@ class Nvfp4Gemm:
                 f"{rows}x{self.n_local}x{self.K} row block, f32 blocked GEMM on decoded values")
 
 
-WORKLOADS = {"mxfp8_quantize": MxFp8Quantize, "fp8_gemm": Fp8Gemm, "nvfp4_gemm": Nvfp4Gemm}
+class DecodeGemm:
+    """Decode step: x bf16 [16, 8192] (MXFP8 in the call) x NVFP4 W [57344, 8192] -> bf16
+    [16, 57344]; W is sharded along N across ranks and the output columns are all-gathered."""
+
+    name = "decode_gemm"
+    unit = "GB/s"
+    dtype = "mxfp8(x) x nvfp4(W) -> f16 tensor cores, f32 acc -> bf16"
+    M, N, K = 16, 57344, 8192
+    kernel = "gemm_decode_kernel"
+    scaling = "strong"
+    parallelism = "n-shard"
+
+    def __init__(self, world: int = 1):
+        self.world = world
+        self.n_local = self.N // world
+        w_bytes = self.n_local * self.K // 2 + self.n_local * self.K // 16
+        self.bytes = w_bytes + self.M * self.K * 2 + self.M * self.n_local * 2
+        self.in_bytes = self.M * self.K * 2            # per step from host: the activations
+        self.out_bytes = self.M * self.N * 2           # per step to host: the gathered output
+        self.config = {"workload": "decode_gemm x[16,8192] bf16 -> mxfp8, W nvfp4 [57344,8192]",
+                       "M": self.M, "N": self.N, "K": self.K, "n_per_gpu": self.n_local,
+                       "sharding": "W along N, NCCL all-gather of output columns",
+                       "l2": "weights 252 MiB per step (> L2), 2 rotating weight copies"}
+
+    def host_input(self):
+        return None
+
+    def setup(self, torch, _):
+        import ptxstd
+        rank = int(os.environ.get("RANK", "0"))
+        g = torch.Generator(device="cuda")
+        g.manual_seed(4321)
+        self.x = torch.randn((self.M, self.K), generator=g, device="cuda").to(torch.bfloat16)
+        self.sets = []
+        for copy in range(2):
+            g.manual_seed(8765 + 17 * rank + copy)
+            wb = (torch.randn((self.n_local, self.K), generator=g, device="cuda") * 0.02).to(
+                torch.bfloat16)
+            gw = float(wb.float().abs().max()) / (448.0 * 6.0)
+            w, sfw = ptxstd.quantize_nvfp4(wb, gw, sf_layout=1)
+            del wb
+            self.sets.append((w, sfw, gw))
+        self.y = torch.empty((self.M, self.n_local), dtype=torch.bfloat16, device="cuda")
+        self.x_host = self.x.cpu().pin_memory()
+        self.y_full = torch.empty((self.world, self.M, self.n_local), dtype=torch.bfloat16,
+                                  device="cuda")
+        self.y_host = torch.empty((self.world, self.M, self.n_local), dtype=torch.bfloat16,
+                                  pin_memory=True)
+        self.launches_per_step = 2
+
+    def _gather(self):
+        if self.world > 1:
+            import torch.distributed as td
+            td.all_gather_into_tensor(self.y_full.view(-1), self.y.view(-1))
+
+    def step(self, i):
+        import ptxstd
+        w, sfw, gw = self.sets[i % 2]
+        ptxstd.gemm_decode(self.x, w, sfw, gw, out=self.y)
+        self._gather()
+        return 2
+
+    def e2e_step(self, i):
+        import ptxstd
+        w, sfw, gw = self.sets[i % 2]
+        self.x.copy_(self.x_host, non_blocking=True)
+        ptxstd.gemm_decode(self.x, w, sfw, gw, out=self.y)
+        self._gather()
+        if self.world > 1:
+            self.y_host.copy_(self.y_full, non_blocking=True)
+        else:
+            self.y_host[0].copy_(self.y, non_blocking=True)
+        return 2
+
+    def value(self, seconds_per_step: float) -> float:
+        return self.bytes / seconds_per_step / 1e9
+
+    def cpu_sample(self, threads: int, budget_s: float):
+        """f32 GEMV-shaped blocked GEMM (16 x 8192 x 8192 block of the weights)."""
+        import numpy as np
+
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        rng = np.random.default_rng(3)
+        if getattr(self, "_dec", None) is None:
+            self._dec = (rng.standard_normal((self.M, self.K), dtype=np.float32),
+                         rng.standard_normal((8192, self.K), dtype=np.float32))
+        a, b = self._dec
+        t0 = time.perf_counter()
+        O.sgemm_nt(a, b, threads)
+        el = time.perf_counter() - t0
+        # bytes of the NVFP4 weight block this sample covers, per second
+        wbytes = 8192 * self.K // 2 + 8192 * self.K // 16
+        return wbytes / el / 1e9, "16x8192x8192 block, f32 blocked GEMM on decoded weights"
+
+
+WORKLOADS = {"mxfp8_quantize": MxFp8Quantize, "fp8_gemm": Fp8Gemm, "nvfp4_gemm": Nvfp4Gemm,
+             "decode_gemm": DecodeGemm}
 
 
 # ---- arms -----------------------------------------------------------------------------------

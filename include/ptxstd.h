@@ -129,6 +129,22 @@ PTXSTD_API int ptxstd_gemm_nvfp4(const uint8_t* d_a, const uint8_t* d_sfa, float
                                  uint16_t* d_c, int64_t M, int64_t N, int64_t K,
                                  ptxstd_stream stream);
 
+/* Decode-shape GEMM: y[M,N] bf16 = MXFP8(x)[M,K] * NVFP4(W)[N,K]^T * gw, M <= 16 tokens.
+ * x: bf16 [M,K] row-major, quantised inside the call with the recipe of ptxstd_quantize_mxfp8
+ * (f8e8m0::from_f32::<TowardZero, SaturateFinite>, src/data_types/narrow.rs:600-617; f8e4m3
+ * ::from_f32, :156-162). W: [N,K/2] E2M1x2 with E4M3 scales per 16 in the blocked layout
+ * (ptxstd_quantize_nvfp4_layout, sf_layout 1) and f32 global scale gw. Both operands are brought
+ * to f16 exactly and multiplied with tcgen05.mma.kind::f16 with the A operand in TMEM
+ * (src/tcgen05/mma.rs:434-453), fp32 accumulation. N % 128 == 0, K % 256 == 0.
+ * workspace: device scratch of ptxstd_gemm_decode_workspace_bytes(M, N, K) bytes, 1024-byte
+ * aligned, owned by the caller; the call initialises it itself (no zeroing needed). Calls that
+ * share a workspace must be stream-ordered. */
+PTXSTD_API size_t ptxstd_gemm_decode_workspace_bytes(int64_t M, int64_t N, int64_t K);
+PTXSTD_API int ptxstd_gemm_decode(const uint16_t* d_x, const uint8_t* d_w, const uint8_t* d_sfw,
+                                  float gw, uint16_t* d_y, int64_t M, int64_t N, int64_t K,
+                                  void* d_workspace, size_t workspace_bytes,
+                                  ptxstd_stream stream);
+
 /* ---- tcgen05 descriptors (src/tcgen05/descriptor.rs) ---------------------------------------- */
 /* InstrDescriptor::<KIND>::new for each kind. Element types use the reference's discriminants:
  * F16ElementType F16 0 / Bf16 1; FloatAccumulator F16 0 / F32 1; F8f6f4ElementType E4m3 0,

@@ -1,0 +1,604 @@
+// Decode-shape GEMM: y[M, N] (bf16, M <= 16 tokens) = MXFP8(x)[M, K] * NVFP4(W)[N, K]^T * gw.
+//
+// x is bf16 and is quantised on the fly to MXFP8 (E4M3 + UE8M0 per 32, the recipe of
+// ptxstd_quantize_mxfp8); W is E2M1 packed two per byte with E4M3 scales per 16 (blocked 128x4
+// layout) and an f32 global scale. No block-scaled tcgen05 kind takes one UE8M0/32 operand and one
+// E4M3/16 operand (kind::mxf8f6f4 wants UE8M0 on both, kind::mxf4nvf4 wants E2M1 on both;
+// src/tcgen05/descriptor.rs:589-653), so both operands are brought to f16 exactly and multiplied
+// with tcgen05.mma.kind::f16 (fp32 accumulation):
+//   - W: e2m1 x e4m3 has at most 6 significant bits and lies in [2^-10, 2688], so
+//     cvt.rn.f16x2.e2m1x2 followed by one f16x2 multiply by the scale is exact;
+//   - x: q * 2^(code - 127) is rewritten per token row as f16 q * 2^(code - maxcode_row), exact
+//     for blocks within 15 binades of the row's largest block; the factor 2^(maxcode_row - 127) is
+//     applied to the fp32 result.
+// The op is weight-streaming (HBM-bound): each W byte is read once.
+//
+// Kernel 1, decode_prep (one CTA per token row plus CTAs that clear the split-K scratch):
+//   MXFP8-quantises x and writes the f16 B operand pre-swizzled (K-major, 128-byte swizzle, 8 KiB
+//   per 256-K stage) so that the main kernel fetches it with one 1-D bulk copy per stage.
+// Kernel 2, gemm_decode (persistent, one CTA per SM, launched with programmatic dependent launch so
+//   its setup and first weight loads overlap kernel 1):
+//   work = (128-row W block, 256-K stage) units split evenly over the CTAs ("stream-K");
+//   warp 0: TMA producer (W tile 128 x 128 bytes, W scales 2 KiB, x image 8 KiB per stage);
+//   warp 1: TMEM owner + MMA issuer: 16 MMAs of M=128 (W rows), N=16 (tokens), K=16 per stage with
+//           the A operand in TMEM;
+//   warps 2..9: dequantise W rows into TMEM (tcgen05.st; two warps per lane quarter, 128 K each)
+//           and, at the end of each W-block segment, reduce the 128 x 16 fp32 partial into the
+//           scratch with red.global.add.v4.f32. A per-block counter of finished K stages elects the
+//           CTA that completes a block; it converts the block to bf16 and writes y (transposed).
+#include "common.cuh"
+#include "data_types.cuh"
+#include "tcgen05.cuh"
+#include "tma_host.h"
+
+namespace {
+
+namespace t5 = ptxstd::tcgen05;
+namespace dt = ptxstd::data_types;
+using ptxstd::mbar_wait;
+
+constexpr uint32_t BM = 128;            // W rows per block (MMA M)
+constexpr uint32_t BKS = 256;           // K elements per stage
+constexpr uint32_t kWStageBytes = BM * BKS / 2;   // 16 KiB packed E2M1
+constexpr uint32_t kSfStageBytes = BM * BKS / 16; // 2 KiB E4M3
+constexpr uint32_t kTok = 16;           // MMA N (tokens, padded)
+constexpr uint32_t kXStageBytes = kTok * BKS * 2; // 8 KiB f16
+constexpr uint32_t kStageBytes = kWStageBytes + kSfStageBytes + kXStageBytes;
+constexpr uint32_t STAGES = 6;
+constexpr uint32_t kDqWarps = 8;
+constexpr uint32_t kThreads = 64 + 32 * kDqWarps;
+constexpr uint32_t kACols = BKS / 2;    // f16 pairs per row per stage = 128 TMEM columns
+constexpr uint32_t kDCol = 2 * kACols;  // accumulator columns start after two A buffers
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kPrepThreads = 256;
+
+struct alignas(1024) Smem {
+    uint8_t w[STAGES][kWStageBytes];
+    uint8_t x[STAGES][kXStageBytes];
+    uint8_t sf[STAGES][kSfStageBytes];
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t afull[2];
+    uint64_t aempty[2];
+    uint64_t dfull;
+    uint64_t dempty;
+    uint64_t segA;
+    uint64_t segB;
+    uint64_t drain;
+    uint32_t tmem_base;
+    uint32_t abort;
+    uint32_t finalize;
+    float factor[kTok];
+};
+constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+enum : uint32_t { kDetailProducer = 0x3100, kDetailMma = 0x3200, kDetailDq = 0x3300 };
+
+// Workspace layout (bytes): y32 [N][16] f32 | counters [N/128] u32 (16 B aligned) |
+// x image [K/256][8 KiB] | factors [16] f32.
+struct Workspace {
+    float* y32;
+    uint32_t* counters;
+    uint8_t* ximg;
+    float* factors;
+};
+__host__ __device__ inline size_t ws_counters_off(size_t N) { return N * kTok * 4; }
+__host__ __device__ inline size_t ws_ximg_off(size_t N) {
+    return ws_counters_off(N) + (((N / BM) * 4 + 1023) & ~static_cast<size_t>(1023));
+}
+__host__ __device__ inline size_t ws_factors_off(size_t N, size_t K) {
+    return ws_ximg_off(N) + K * kTok * 2;
+}
+__host__ __device__ inline size_t ws_bytes(size_t N, size_t K) { return ws_factors_off(N, K) + 64; }
+
+// Byte offset of f16 element (row r < 16, k) in the x image: per 256-K stage 8 KiB made of four
+// 64-element K atoms of 16 rows x 128 bytes, 16-byte chunks XOR-swizzled by row % 8.
+__device__ __forceinline__ uint32_t ximg_offset(uint32_t r, uint32_t k) {
+    const uint32_t stage = k / BKS, kk = k % BKS;
+    const uint32_t atom = kk / 64, byte = (kk % 64) * 2;
+    return stage * kXStageBytes + atom * (kTok * 128) + r * 128 +
+           (((byte >> 4) ^ (r & 7)) << 4) + (byte & 15);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Kernel 1: x -> MXFP8 -> f16 B-operand image, per-row factors; clears y32 and the counters.
+// Blocks 0..15 handle token rows (rows >= M write zeros); the rest clear the scratch.
+__global__ void __launch_bounds__(kPrepThreads)
+    decode_prep_kernel(const uint16_t* __restrict__ x, uint32_t M, uint32_t K, uint8_t* ws,
+                       uint32_t N) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    Workspace w{reinterpret_cast<float*>(ws),
+                reinterpret_cast<uint32_t*>(ws + ws_counters_off(N)), ws + ws_ximg_off(N),
+                reinterpret_cast<float*>(ws + ws_factors_off(N, K))};
+    if (blockIdx.x >= kTok) {
+        // clear y32 (N*16 floats) and counters with 16-byte stores
+        const size_t n4 = static_cast<size_t>(N) * kTok / 4;
+        const size_t nthr = static_cast<size_t>(gridDim.x - kTok) * blockDim.x;
+        const size_t tid = static_cast<size_t>(blockIdx.x - kTok) * blockDim.x + threadIdx.x;
+        for (size_t i = tid; i < n4; i += nthr)
+            reinterpret_cast<float4*>(w.y32)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (size_t i = tid; i < N / BM; i += nthr) w.counters[i] = 0;
+        return;
+    }
+    const uint32_t r = blockIdx.x;
+    __shared__ uint32_t red[kPrepThreads / 32];
+    const uint32_t nblk = K / 32;
+    // pass 1: block scale codes and the row's largest code
+    uint32_t maxcode = 0;
+    if (r < M) {
+        for (uint32_t b = threadIdx.x; b < nblk; b += blockDim.x) {
+            const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * K + b * 32);
+            uint32_t m = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint4 v = p[i];
+                m = max(m, dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                                    dt::bf16x2_absmax_bits(v.z, v.w))));
+            }
+            const uint32_t code = dt::mxfp8_scale_code(__uint_as_float(m << 16));
+            if (code != 0xFFu) maxcode = max(maxcode, code);
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) maxcode = max(maxcode, __shfl_xor_sync(0xffffffffu, maxcode, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = maxcode;
+    __syncthreads();
+    maxcode = 0;
+    for (uint32_t i = 0; i < kPrepThreads / 32; ++i) maxcode = max(maxcode, red[i]);
+    if (threadIdx.x == 0) {
+        // 2^(maxcode - 127) in f32 (maxcode <= 254; 0 for padding rows)
+        w.factors[r] = r < M ? (maxcode >= 1 ? __uint_as_float(maxcode << 23)
+                                             : __uint_as_float(0x00400000u))
+                             : 0.0f;
+    }
+    // pass 2: elements as f16 q * 2^(code - maxcode)
+    for (uint32_t b = threadIdx.x; b < nblk; b += blockDim.x) {
+        uint32_t h[16];
+        if (r < M) {
+            const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * K + b * 32);
+            uint4 v[4];
+            uint32_t m = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                v[i] = p[i];
+                m = max(m, dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v[i].x, v[i].y),
+                                                    dt::bf16x2_absmax_bits(v[i].z, v[i].w))));
+            }
+            const uint32_t code = dt::mxfp8_scale_code(__uint_as_float(m << 16));
+            const float inv = dt::ue8m0_inverse(code);
+            // factor 2^(code - maxcode) in f32 (>= 2^-254 is not representable: flush below 2^-149)
+            const int d = static_cast<int>(code) - static_cast<int>(maxcode);
+            const float rel = code == 0xFFu ? __uint_as_float(0x7FFFFFFFu)
+                              : d >= -126   ? __uint_as_float(static_cast<uint32_t>(d + 127) << 23)
+                              : d >= -149   ? __uint_as_float(1u << (d + 149))
+                                            : 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t ww[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint16_t qq = dt::e4m3x2_from_f32<false>(
+                        __fmul_rn(dt::bf16_lo(ww[k]), inv), __fmul_rn(dt::bf16_hi(ww[k]), inv));
+                    const float2 qf = dt::e4m3x2_to_f32(qq);
+                    uint32_t hh;
+                    asm("cvt.rn.f16x2.f32 %0, %1, %2;"
+                        : "=r"(hh)
+                        : "f"(__fmul_rn(qf.y, rel)), "f"(__fmul_rn(qf.x, rel)));
+                    h[i * 4 + k] = hh;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) h[i] = 0;
+        }
+        // 32 f16 = 64 bytes = four 16-byte chunks of the image
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(w.ximg + ximg_offset(r, b * 32 + c * 8)) =
+                make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Kernel 2.
+__device__ __forceinline__ void fail(Smem& s, uint32_t* err, uint32_t detail) {
+    ptxstd::record_error(err, PTXSTD_ETIMEOUT, detail);
+    *reinterpret_cast<volatile uint32_t*>(&s.abort) = 1u;
+}
+__device__ __forceinline__ bool aborted(Smem& s) {
+    return *reinterpret_cast<volatile uint32_t*>(&s.abort) != 0u;
+}
+
+// tcgen05.st.32x32b.x64: 64 consecutive columns of this warp's lane quarter.
+__device__ __forceinline__ void tmem_st_x64(uint32_t taddr, const uint32_t (&v)[64]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+        "%29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, "
+        "%47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, "
+        "%64};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+        "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+        "r"(v[29]), "r"(v[30]), "r"(v[31]), "r"(v[32]), "r"(v[33]), "r"(v[34]), "r"(v[35]),
+        "r"(v[36]), "r"(v[37]), "r"(v[38]), "r"(v[39]), "r"(v[40]), "r"(v[41]), "r"(v[42]),
+        "r"(v[43]), "r"(v[44]), "r"(v[45]), "r"(v[46]), "r"(v[47]), "r"(v[48]), "r"(v[49]),
+        "r"(v[50]), "r"(v[51]), "r"(v[52]), "r"(v[53]), "r"(v[54]), "r"(v[55]), "r"(v[56]),
+        "r"(v[57]), "r"(v[58]), "r"(v[59]), "r"(v[60]), "r"(v[61]), "r"(v[62]), "r"(v[63])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// A from TMEM: tcgen05.mma.cta_group::1.kind::f16 [d], [a], b_desc, idesc.
+__device__ __forceinline__ void mma_f16_tmem_a(uint32_t d, uint32_t a, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b),
+                 "f"(c), "f"(d)
+                 : "memory");
+}
+
+// Unit u of U = nblocks * S is (block u / S, stage u % S); CTA c owns [c U / G, (c+1) U / G).
+__device__ __forceinline__ void unit_range(uint64_t U, uint32_t& u0, uint32_t& u1) {
+    u0 = static_cast<uint32_t>(U * blockIdx.x / gridDim.x);
+    u1 = static_cast<uint32_t>(U * (blockIdx.x + 1) / gridDim.x);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_decode_kernel(const __grid_constant__ CUtensorMap tmW, const uint8_t* __restrict__ sfW,
+                       uint8_t* ws, uint16_t* __restrict__ y, uint32_t M, uint32_t N, uint32_t K,
+                       float gw, uint32_t* err) {
+    extern __shared__ uint8_t smem_raw[];
+    Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                       ~static_cast<uintptr_t>(1023));
+    const uint32_t warp = ptxstd::warp_id();
+    const uint32_t lane = ptxstd::lane_id();
+    const uint32_t S = K / BKS;
+    const uint64_t U = static_cast<uint64_t>(N / BM) * S;
+    uint32_t u0, u1;
+    unit_range(U, u0, u1);
+    Workspace wsp{reinterpret_cast<float*>(ws),
+                  reinterpret_cast<uint32_t*>(ws + ws_counters_off(N)), ws + ws_ximg_off(N),
+                  reinterpret_cast<float*>(ws + ws_factors_off(N, K))};
+
+    if (warp == 0 && lane == 0) {
+        ptxstd::prefetch_tensormap(&tmW);
+        for (uint32_t i = 0; i < STAGES; ++i) {
+            ptxstd::mbar_init(&s.full[i], 1);
+            ptxstd::mbar_init(&s.empty[i], kDqWarps + 1);
+        }
+        for (uint32_t i = 0; i < 2; ++i) {
+            ptxstd::mbar_init(&s.afull[i], kDqWarps);
+            ptxstd::mbar_init(&s.aempty[i], 1);
+        }
+        ptxstd::mbar_init(&s.dfull, 1);
+        ptxstd::mbar_init(&s.dempty, kDqWarps);
+        ptxstd::mbar_init(&s.segA, kDqWarps);
+        ptxstd::mbar_init(&s.segB, 1);
+        ptxstd::mbar_init(&s.drain, 1);
+        s.abort = 0;
+        s.finalize = 0;
+        ptxstd::fence_mbarrier_init();
+    }
+    if (warp == 1) {
+        t5::tmem_alloc(&s.tmem_base, kTmemCols);
+        t5::tmem_relinquish();
+    }
+    t5::fence_before_thread_sync();
+    __syncthreads();
+    t5::fence_after_thread_sync();
+    const uint32_t tmem = s.tmem_base;
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (ptxstd::elect_one()) {
+            uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
+            bool waited = false;
+            const uint32_t sf_tiles_per_row = K / 64;
+            for (uint32_t u = u0; u < u1; ++u) {
+                const uint32_t nb = u / S, ks = u % S;
+                if (!mbar_wait(&s.empty[stage], phase ^ 1u)) {
+                    fail(s, err, kDetailProducer | stage);
+                    break;
+                }
+                if (aborted(s)) break;
+                ptxstd::mbar_arrive_expect_tx(&s.full[stage], kStageBytes);
+                ptxstd::tma_load_2d(s.w[stage], &tmW, &s.full[stage],
+                                    static_cast<int32_t>(ks * (BKS / 2)),
+                                    static_cast<int32_t>(nb * BM));
+                ptxstd::bulk_load(s.sf[stage],
+                                  sfW + (static_cast<size_t>(nb) * sf_tiles_per_row + ks * 4) * 512,
+                                  kSfStageBytes, &s.full[stage]);
+                if (!waited) {
+                    // x image and the cleared scratch come from decode_prep.
+                    asm volatile("griddepcontrol.wait;" ::: "memory");
+                    waited = true;
+                }
+                ptxstd::bulk_load(s.x[stage], wsp.ximg + static_cast<size_t>(ks) * kXStageBytes,
+                                  kXStageBytes, &s.full[stage]);
+                issued |= 1u << stage;
+                issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (aborted(s)) {
+                for (uint32_t i = 0; i < STAGES; ++i)
+                    if (issued & (1u << i)) mbar_wait(&s.full[i], (issued_parity >> i) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (ptxstd::elect_one()) {
+            uint32_t idesc = 0;
+            t5::idesc_dense(/*F16*/ 0, /*F16*/ 0, /*F32*/ 1, BM, kTok, idesc);
+            uint32_t stage = 0, phase = 0, abuf = 0, aphase = 0, dphase = 0;
+            const uint32_t d = tmem + kDCol;
+            for (uint32_t u = u0; u < u1 && !aborted(s); ++u) {
+                const uint32_t ks = u % S;
+                const bool first = (u == u0) || ks == 0;
+                const bool last = (u + 1 == u1) || ks == S - 1;
+                if (first) {
+                    if (!mbar_wait(&s.dempty, dphase ^ 1u)) {
+                        fail(s, err, kDetailMma | 0x30);
+                        break;
+                    }
+                }
+                if (!mbar_wait(&s.afull[abuf], aphase) || !mbar_wait(&s.full[stage], phase)) {
+                    fail(s, err, kDetailMma | stage);
+                    break;
+                }
+                t5::fence_after_thread_sync();
+                const uint32_t xs = ptxstd::smem_u32(s.x[stage]);
+                const uint32_t a = tmem + abuf * kACols;
+#pragma unroll
+                for (uint32_t j = 0; j < BKS / 16; ++j) {
+                    // B: K atom j / 4 (2 KiB apart), +32 bytes per K=16 step inside the atom.
+                    const uint64_t bd = t5::smem_desc_k128(xs + (j / 4) * (kTok * 128) + (j % 4) * 32);
+                    mma_f16_tmem_a(d, a + 8 * j, bd, idesc, (!first || j != 0) ? 1u : 0u);
+                }
+                t5::commit(&s.aempty[abuf]);
+                t5::commit(&s.empty[stage]);
+                if (last) {
+                    t5::commit(&s.dfull);
+                    dphase ^= 1u;
+                }
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+                if (++abuf == 2) {
+                    abuf = 0;
+                    aphase ^= 1u;
+                }
+            }
+            t5::commit(&s.drain);
+            mbar_wait(&s.drain, 0);
+        }
+    } else {
+        // ---------------- dequant + epilogue (warps 2..9) ----------------
+        const uint32_t q = warp & 3u;             // lane quarter = W rows 32q .. 32q+31
+        const uint32_t h = (warp - 2u) >> 2;      // K half of the stage
+        const uint32_t row = 32 * q + lane;       // W row within the block
+        uint32_t stage = 0, phase = 0, abuf = 0, aphase = 0, dphase = 0, sphase = 0;
+        uint32_t seg_len = 0;
+        for (uint32_t u = u0; u < u1; ++u) {
+            const uint32_t nb = u / S, ks = u % S;
+            const bool last = (u + 1 == u1) || ks == S - 1;
+            bool ok = !aborted(s) && mbar_wait(&s.full[stage], phase);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                if (lane == 0 && !aborted(s)) fail(s, err, kDetailDq | stage);
+                break;
+            }
+            // packed W: 64 bytes of this row (4 swizzled 16-byte chunks), scales: 2 x 4 bytes
+            const uint8_t* wrow = s.w[stage] + row * 128;
+            uint4 pk[4];
+#pragma unroll
+            for (uint32_t i = 0; i < 4; ++i) {
+                const uint32_t c = h * 4 + i;
+                pk[i] = *reinterpret_cast<const uint4*>(wrow + ((c ^ (row & 7)) << 4));
+            }
+            uint32_t sc[2];
+#pragma unroll
+            for (uint32_t t = 0; t < 2; ++t)
+                sc[t] = *reinterpret_cast<const uint32_t*>(s.sf[stage] + (h * 2 + t) * 512 +
+                                                           (row & 31) * 16 + (row >> 5) * 4);
+            __syncwarp();
+            if (lane == 0) ptxstd::mbar_arrive(&s.empty[stage]);
+            // dequantise 128 elements into 64 f16x2 words
+            uint32_t out[64];
+#pragma unroll
+            for (uint32_t i = 0; i < 4; ++i) {
+                // chunk i covers K elements 32 i .. 32 i + 31 of this half: scales 2i, 2i+1
+                const uint32_t sbytes = (sc[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+                uint32_t s2;
+                asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(s2) : "h"(static_cast<uint16_t>(sbytes)));
+                const uint32_t slo = __byte_perm(s2, 0, 0x1010);  // scale of the first 16
+                const uint32_t shi = __byte_perm(s2, 0, 0x3232);  // scale of the next 16
+                const uint32_t wv[4] = {pk[i].x, pk[i].y, pk[i].z, pk[i].w};
+#pragma unroll
+                for (uint32_t j = 0; j < 4; ++j) {
+                    const uint32_t sx = j < 2 ? slo : shi;
+#pragma unroll
+                    for (uint32_t b = 0; b < 4; ++b) {
+                        uint32_t hf;
+                        asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+                            : "=r"(hf)
+                            : "r"(wv[j] >> (8 * b)));
+                        uint32_t prod;
+                        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(prod) : "r"(hf), "r"(sx));
+                        out[i * 16 + j * 4 + b] = prod;
+                    }
+                }
+            }
+            bool okA = mbar_wait(&s.aempty[abuf], aphase ^ 1u);
+            okA = __all_sync(0xffffffffu, okA);
+            if (!okA) {
+                if (lane == 0) fail(s, err, kDetailDq | 0x40);
+                break;
+            }
+            t5::fence_after_thread_sync();
+            tmem_st_x64(tmem + ((32 * q) << 16) + abuf * kACols + h * 64, out);
+            tmem_wait_st();
+            t5::fence_before_thread_sync();
+            __syncwarp();
+            if (lane == 0) ptxstd::mbar_arrive(&s.afull[abuf]);
+            if (++abuf == 2) {
+                abuf = 0;
+                aphase ^= 1u;
+            }
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+            ++seg_len;
+            if (!last) continue;
+
+            // ---- end of a W-block segment: reduce the 128 x 16 partial into y32 ----
+            bool okD = mbar_wait(&s.dfull, dphase);
+            okD = __all_sync(0xffffffffu, okD);
+            if (!okD) {
+                if (lane == 0) fail(s, err, kDetailDq | 0x50);
+                break;
+            }
+            dphase ^= 1u;
+            t5::fence_after_thread_sync();
+            uint32_t acc[16];
+            t5::ld_32x32b_x16(tmem + ((32 * q) << 16) + kDCol, acc);
+            t5::wait_ld();
+            t5::fence_before_thread_sync();
+            __syncwarp();
+            if (lane == 0) ptxstd::mbar_arrive(&s.dempty);
+            // this warp reduces tokens 8h .. 8h+7 of its row
+            float* dst = wsp.y32 + (static_cast<size_t>(nb) * BM + row) * kTok + 8 * h;
+            const float* fac = wsp.factors + 8 * h;
+            float v[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+                v[t] = __uint_as_float(h ? acc[8 + t] : acc[t]) * (__ldcg(fac + t) * gw);
+            red_add_v4(dst, v[0], v[1], v[2], v[3]);
+            red_add_v4(dst + 4, v[4], v[5], v[6], v[7]);
+            __threadfence();
+            // All 8 warps have reduced (segA, one arrive per warp), then warp 2 publishes the
+            // finished stages and tells the others whether this CTA completes the block (segB).
+            // mbarriers rather than bar.sync so that every wait stays bounded.
+            __syncwarp();
+            if (lane == 0) ptxstd::mbar_arrive(&s.segA);
+            bool okS = mbar_wait(&s.segA, sphase);
+            okS = __all_sync(0xffffffffu, okS);
+            if (!okS) {
+                if (lane == 0) fail(s, err, kDetailDq | 0x60);
+                break;
+            }
+            if (warp == 2 && lane == 0) {
+                const uint32_t before = atomicAdd(wsp.counters + nb, seg_len);
+                *reinterpret_cast<volatile uint32_t*>(&s.finalize) =
+                    (before + seg_len == S) ? 1u : 0u;
+                ptxstd::mbar_arrive(&s.segB);
+            }
+            okS = mbar_wait(&s.segB, sphase);
+            okS = __all_sync(0xffffffffu, okS);
+            if (!okS) {
+                if (lane == 0) fail(s, err, kDetailDq | 0x70);
+                break;
+            }
+            sphase ^= 1u;
+            seg_len = 0;
+            if (*reinterpret_cast<volatile uint32_t*>(&s.finalize)) {
+                __threadfence();
+                // 256 threads: token t = tid / 16, 8 consecutive columns (tid % 16) * 8
+                const uint32_t tid = (warp - 2) * 32 + lane;
+                const uint32_t t = tid / 16, c0 = (tid % 16) * 8;
+                if (t < M) {
+                    uint32_t o[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float a0 = __ldcg(wsp.y32 + (static_cast<size_t>(nb) * BM + c0 + 2 * j) * kTok + t);
+                        const float a1 = __ldcg(wsp.y32 + (static_cast<size_t>(nb) * BM + c0 + 2 * j + 1) * kTok + t);
+                        o[j] = dt::bf16x2_from_f32(a0, a1);
+                    }
+                    *reinterpret_cast<uint4*>(y + static_cast<size_t>(t) * N + nb * BM + c0) =
+                        make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+        }
+    }
+
+    t5::fence_before_thread_sync();
+    __syncthreads();
+    t5::fence_after_thread_sync();
+    if (warp == 1) t5::tmem_dealloc(tmem, kTmemCols);
+}
+
+int launch_decode(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float gw, uint16_t* y,
+                  int64_t M, int64_t N, int64_t K, uint8_t* ws, cudaStream_t stream) {
+    CUtensorMap tw;
+    int st = ptxstd::make_tmap_2d(&tw, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2,
+                                  BKS / 2, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(gemm_decode_kernel),
+                                      static_cast<int>(kSmemBytes));
+    if (st) return st;
+    uint32_t* err = ptxstd::device_error_word();
+    if (!err) return PTXSTD_ECUDA;
+    const int sms = ptxstd::sm_count();
+    decode_prep_kernel<<<sms, kPrepThreads, 0, stream>>>(x, static_cast<uint32_t>(M),
+                                                         static_cast<uint32_t>(K), ws,
+                                                         static_cast<uint32_t>(N));
+    st = ptxstd::launch_status();
+    if (st) return st;
+    const uint64_t units = static_cast<uint64_t>(N / BM) * static_cast<uint64_t>(K / BKS);
+    const uint32_t grid = static_cast<uint32_t>(units < static_cast<uint64_t>(sms) ? units : sms);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, gemm_decode_kernel, tw, sfW, ws, y, static_cast<uint32_t>(M),
+                           static_cast<uint32_t>(N), static_cast<uint32_t>(K), gw,
+                           err) != cudaSuccess)
+        return PTXSTD_ECUDA;
+    return ptxstd::launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t ptxstd_gemm_decode_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    return ws_bytes(static_cast<size_t>(N), static_cast<size_t>(K));
+}
+
+int ptxstd_gemm_decode(const uint16_t* d_x, const uint8_t* d_w, const uint8_t* d_sfw, float gw,
+                       uint16_t* d_y, int64_t M, int64_t N, int64_t K, void* d_workspace,
+                       size_t workspace_bytes, ptxstd_stream stream) {
+    if (M <= 0 || M > static_cast<int64_t>(kTok) || N <= 0 || K <= 0 || N % BM || K % BKS)
+        return PTXSTD_EINVAL;
+    if (N >= (1ll << 31) || K >= (1ll << 30)) return PTXSTD_EINVAL;
+    if (!(gw == gw) || !d_x || !d_w || !d_sfw || !d_y || !d_workspace) return PTXSTD_EINVAL;
+    if (!ptxstd::aligned16(d_x) || !ptxstd::aligned16(d_w) || !ptxstd::aligned16(d_sfw) ||
+        !ptxstd::aligned16(d_y) || (reinterpret_cast<uintptr_t>(d_workspace) & 1023u))
+        return PTXSTD_EINVAL;
+    if (workspace_bytes < ws_bytes(static_cast<size_t>(N), static_cast<size_t>(K)))
+        return PTXSTD_EINVAL;
+    return launch_decode(d_x, d_w, d_sfw, gw, d_y, M, N, K, static_cast<uint8_t*>(d_workspace),
+                         static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

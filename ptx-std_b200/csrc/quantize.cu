@@ -1,13 +1,13 @@
 // Quantise/pack kernels: bf16 activations -> MXFP8 (E4M3 + UE8M0 per 32) and NVFP4 (E2M1 + E4M3
 // per 16, f32 global scale). HBM-bound, so the kernel is built around bytes in flight:
 //
-//   - a persistent grid of one CTA per SM walks 16 KiB chunks of the flat input (8192 bf16);
-//   - one producer lane streams each chunk into an 8-stage shared-memory ring with a 1-D bulk
+//   - a persistent grid of one CTA per SM walks fixed-size chunks of the flat input;
+//   - one producer lane streams each chunk into a multi-stage shared-memory ring with a 1-D bulk
 //     async copy (cp.async.bulk, ptx-std src/tma/bulk.rs:60) that completes on the stage's
-//     mbarrier (arrive_expect_tx, src/mbarrier.rs:533) — up to 128 KiB in flight per SM with no
-//     register cost;
-//   - eight consumer warps read the stage with 16-byte shared loads, lane l of warp w taking
-//     vector (w * 32 + l) of each 256-vector row so that every warp load is one contiguous,
+//     mbarrier (arrive_expect_tx, src/mbarrier.rs:533) — 128 KiB in flight per SM by default,
+//     with no register cost;
+//   - CW consumer warps read the stage with 16-byte shared loads, lane l of warp w taking
+//     vector (w * 32 + l) of each (32 CW)-vector row so that every warp load is one contiguous,
 //     conflict-free 512-byte row; the lanes holding one block (4 for MXFP8, 2 for NVFP4) combine
 //     their amax with shuffle-xor; each element pair is packed by one `cvt` instruction
 //     (src/data_types/narrow.rs:156-162); payload words go straight to global memory as 8-byte
@@ -24,21 +24,26 @@ using ptxstd::mbar_wait;
 
 namespace {
 
-constexpr uint32_t kChunkElems = 8192;              // bf16 per stage (16 KiB)
-constexpr uint32_t kChunkBytes = kChunkElems * 2;
-constexpr uint32_t kChunkVecs = kChunkElems / 8;     // 16-byte vectors per stage
-constexpr uint32_t kStages = 8;
-constexpr uint32_t kConsumerWarps = 8;
-constexpr uint32_t kThreads = 32 * (kConsumerWarps + 1);
-constexpr uint32_t kVecsPerLane = kChunkVecs / (32 * kConsumerWarps);  // 4
-
-struct alignas(128) Smem {
-    uint8_t buf[kStages][kChunkBytes];
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
-    uint32_t abort;
+// Tiling of the ring: CW consumer warps, VPL 16-byte vectors per lane per stage, ST stages.
+template <uint32_t CW, uint32_t VPL, uint32_t ST>
+struct QCfg {
+    static constexpr uint32_t kConsumerWarps = CW;
+    static constexpr uint32_t kVecsPerLane = VPL;
+    static constexpr uint32_t kStages = ST;
+    static constexpr uint32_t kChunkVecs = 32 * CW * VPL;  // 16-byte vectors per stage
+    static constexpr uint32_t kChunkElems = kChunkVecs * 8;
+    static constexpr uint32_t kChunkBytes = kChunkVecs * 16;
+    static constexpr uint32_t kThreads = 32 * (CW + 1);
+    struct alignas(128) Smem {
+        uint8_t buf[ST][kChunkBytes];
+        uint64_t full[ST];
+        uint64_t empty[ST];
+        uint32_t abort;
+    };
+    static constexpr size_t kSmemBytes = sizeof(Smem) + 128;
 };
-constexpr size_t kSmemBytes = sizeof(Smem) + 128;
+// Default: 16 consumer warps x 2 vectors per lane = 16 KiB stages, 8 stages (128 KiB in flight).
+using DefaultCfg = QCfg<16, 2, 8>;
 
 enum : uint32_t { kDetailProducer = 0x2100, kDetailConsumer = 0x2200 };
 
@@ -113,22 +118,24 @@ struct Nvfp4 {
     }
 };
 
-template <class Op>
-__global__ void __launch_bounds__(kThreads, 1)
+template <class Cfg, class Op>
+__global__ void __launch_bounds__(Cfg::kThreads, 1)
     quantize_kernel(const uint16_t* __restrict__ x, size_t n_elems, Op op, uint8_t* __restrict__ q,
                     uint8_t* __restrict__ sf, size_t sf_cols, uint32_t* err) {
+    using Smem = typename Cfg::Smem;
+    constexpr uint32_t CW = Cfg::kConsumerWarps, VPL = Cfg::kVecsPerLane, ST = Cfg::kStages;
     extern __shared__ uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
                                        ~static_cast<uintptr_t>(127));
     const uint32_t warp = ptxstd::warp_id();
     const uint32_t lane = ptxstd::lane_id();
-    const size_t n_chunks = (n_elems + kChunkElems - 1) / kChunkElems;
+    const size_t n_chunks = (n_elems + Cfg::kChunkElems - 1) / Cfg::kChunkElems;
     const size_t n_vec = n_elems / 8;
 
     if (threadIdx.x == 0) {
-        for (uint32_t i = 0; i < kStages; ++i) {
+        for (uint32_t i = 0; i < ST; ++i) {
             ptxstd::mbar_init(&s.full[i], 1);
-            ptxstd::mbar_init(&s.empty[i], kConsumerWarps);
+            ptxstd::mbar_init(&s.empty[i], CW);
         }
         s.abort = 0;
         ptxstd::fence_mbarrier_init();
@@ -136,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     volatile uint32_t* abort_flag = &s.abort;
 
-    if (warp == kConsumerWarps) {
+    if (warp == CW) {
         // ---------------- producer ----------------
         if (lane == 0) {
             uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
@@ -147,20 +154,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 if (*abort_flag) break;
-                const size_t e0 = c * kChunkElems;
-                const uint32_t bytes =
-                    static_cast<uint32_t>(min(static_cast<size_t>(kChunkElems), n_elems - e0) * 2);
+                const size_t e0 = c * Cfg::kChunkElems;
+                const uint32_t bytes = static_cast<uint32_t>(
+                    min(static_cast<size_t>(Cfg::kChunkElems), n_elems - e0) * 2);
                 ptxstd::mbar_arrive_expect_tx(&s.full[stage], bytes);
                 ptxstd::bulk_load(s.buf[stage], x + e0, bytes, &s.full[stage]);
                 issued |= 1u << stage;
                 issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-                if (++stage == kStages) {
+                if (++stage == ST) {
                     stage = 0;
                     phase ^= 1u;
                 }
             }
             if (*abort_flag) {
-                for (uint32_t i = 0; i < kStages; ++i)
+                for (uint32_t i = 0; i < ST; ++i)
                     if (issued & (1u << i)) mbar_wait(&s.full[i], (issued_parity >> i) & 1u);
             }
         }
@@ -178,21 +185,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             const uint4* buf = reinterpret_cast<const uint4*>(s.buf[stage]);
-            const size_t v0 = c * kChunkVecs;
-            uint4 v[kVecsPerLane];
+            const size_t v0 = c * Cfg::kChunkVecs;
+            // vectors of this chunk that exist (all of them except in the last chunk)
+            const uint32_t live = static_cast<uint32_t>(
+                min(static_cast<size_t>(Cfg::kChunkVecs), n_vec - v0));
+            uint4 v[VPL];
 #pragma unroll
-            for (uint32_t j = 0; j < kVecsPerLane; ++j) {
-                const uint32_t lv = (j * kConsumerWarps + warp) * 32 + lane;
-                v[j] = (v0 + lv < n_vec) ? buf[lv] : make_uint4(0, 0, 0, 0);
+            for (uint32_t j = 0; j < VPL; ++j) {
+                const uint32_t lv = (j * CW + warp) * 32 + lane;
+                v[j] = lv < live ? buf[lv] : make_uint4(0, 0, 0, 0);
             }
             __syncwarp();
             if (lane == 0) ptxstd::mbar_arrive(&s.empty[stage]);
 #pragma unroll
-            for (uint32_t j = 0; j < kVecsPerLane; ++j) {
-                const uint32_t lv = (j * kConsumerWarps + warp) * 32 + lane;
-                op(v[j], v0 + lv < n_vec, v0 + lv, lane, q, sf, sf_cols);
+            for (uint32_t j = 0; j < VPL; ++j) {
+                const uint32_t lv = (j * CW + warp) * 32 + lane;
+                op(v[j], lv < live, v0 + lv, lane, q, sf, sf_cols);
             }
-            if (++stage == kStages) {
+            if (++stage == ST) {
                 stage = 0;
                 phase ^= 1u;
             }
@@ -200,19 +210,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <class Op>
+template <class Cfg, class Op>
 int launch(const uint16_t* x, size_t n_elems, Op op, uint8_t* q, uint8_t* sf, size_t sf_cols,
            cudaStream_t stream) {
-    int st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(quantize_kernel<Op>),
-                                          static_cast<int>(kSmemBytes));
+    int st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(quantize_kernel<Cfg, Op>),
+                                          static_cast<int>(Cfg::kSmemBytes));
     if (st) return st;
     uint32_t* err = ptxstd::device_error_word();
     if (!err) return PTXSTD_ECUDA;
-    const size_t chunks = (n_elems + kChunkElems - 1) / kChunkElems;
+    const size_t chunks = (n_elems + Cfg::kChunkElems - 1) / Cfg::kChunkElems;
     const size_t sms = static_cast<size_t>(ptxstd::sm_count());
     const int grid = static_cast<int>(chunks < sms ? chunks : sms);
-    quantize_kernel<Op><<<grid, kThreads, kSmemBytes, stream>>>(x, n_elems, op, q, sf, sf_cols,
-                                                                err);
+    quantize_kernel<Cfg, Op><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
+        x, n_elems, op, q, sf, sf_cols, err);
     return ptxstd::launch_status();
 }
 
@@ -230,8 +240,8 @@ int ptxstd_quantize_mxfp8_layout(const uint16_t* d_x, int64_t rows, int64_t cols
     const size_t n = static_cast<size_t>(rows) * static_cast<size_t>(cols);
     const size_t sf_cols = static_cast<size_t>(cols) / 32;
     auto s = static_cast<cudaStream_t>(stream);
-    if (sf_layout == 1) return launch(d_x, n, Mxfp8<true>{0.0f}, d_q, d_sf, sf_cols, s);
-    return launch(d_x, n, Mxfp8<false>{0.0f}, d_q, d_sf, sf_cols, s);
+    if (sf_layout == 1) return launch<DefaultCfg>(d_x, n, Mxfp8<true>{0.0f}, d_q, d_sf, sf_cols, s);
+    return launch<DefaultCfg>(d_x, n, Mxfp8<false>{0.0f}, d_q, d_sf, sf_cols, s);
 }
 
 int ptxstd_quantize_mxfp8(const uint16_t* d_x, int64_t rows, int64_t cols, uint8_t* d_q,
@@ -254,8 +264,8 @@ int ptxstd_quantize_nvfp4_layout(const uint16_t* d_x, int64_t rows, int64_t cols
     // six_g = 6 * g as one IEEE rounding, as in the recipe.
     const float six_g = 6.0f * global_scale;
     if (sf_layout == 1)
-        return launch(d_x, n, Nvfp4<true>{global_scale, six_g}, d_q, d_sf, sf_cols, s);
-    return launch(d_x, n, Nvfp4<false>{global_scale, six_g}, d_q, d_sf, sf_cols, s);
+        return launch<DefaultCfg>(d_x, n, Nvfp4<true>{global_scale, six_g}, d_q, d_sf, sf_cols, s);
+    return launch<DefaultCfg>(d_x, n, Nvfp4<false>{global_scale, six_g}, d_q, d_sf, sf_cols, s);
 }
 
 int ptxstd_quantize_nvfp4(const uint16_t* d_x, int64_t rows, int64_t cols, float global_scale,

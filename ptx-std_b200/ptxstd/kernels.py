@@ -57,6 +57,46 @@ def gemm_nvfp4(a, sfa, ga: float, b, sfb, gb: float, out=None, stream=None):
     return c
 
 
+_workspaces: dict = {}
+
+
+def decode_workspace(M: int, N: int, K: int, device=None):
+    """A cached device workspace for gemm_decode (one per device and size)."""
+    torch = _torch()
+    dev = torch.device(device) if device is not None else torch.device(
+        "cuda", torch.cuda.current_device())
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    nbytes = int(lib().ptxstd_gemm_decode_workspace_bytes(M, N, K))
+    key = (dev.index, nbytes)
+    ws = _workspaces.get(key)
+    if ws is None:
+        ws = torch.empty(nbytes + 1024, dtype=torch.uint8, device=dev)
+        _workspaces[key] = ws
+    off = (-ws.data_ptr()) % 1024
+    return ws, ws.data_ptr() + off, nbytes
+
+
+def gemm_decode(x, w, sfw, gw: float, out=None, workspace=None, stream=None):
+    """bf16 x [M <= 16, K] (quantised to MXFP8 in the call) times NVFP4 w [N, K/2] with blocked
+    E4M3 scales and global scale gw -> bf16 [M, N]."""
+    torch = _torch()
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise TypeError("expected a 2-D bfloat16 activation tensor")
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] * 2 != K or sfw.numel() != N * K // 16:
+        raise ValueError("shape mismatch")
+    y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    if workspace is None:
+        _, ptr, nbytes = decode_workspace(M, N, K, x.device)
+    else:
+        ptr, nbytes = workspace
+    check(lib().ptxstd_gemm_decode(_dev(x), _dev(w), _dev(sfw), float(gw), _dev(y), M, N, K,
+                                   ptr, nbytes, _stream(stream)), "gemm_decode")
+    return y
+
+
 def quantize_nvfp4(x, global_scale: float, sf_layout: int = SF_ROWMAJOR, out=None,
                    stream=None):
     """bf16 [rows, cols] -> (E2M1x2 [rows, cols/2] uint8, E4M3 scales per 16 uint8)."""

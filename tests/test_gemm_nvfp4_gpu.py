@@ -81,10 +81,10 @@ def test_k_block_scales(cuda, oracle):
 
 
 def test_col_scales(cuda, oracle):
-    """sfB[n, :] = 2^(n % 16 - 8): C[m, n] = K * sfB(n)."""
+    """sfB[n, :] = 2^(n % 14 - 6) (normal E4M3 powers of two): C[m, n] = K * sfB(n)."""
     M, N, K = 128, 512, 256
     A, B = _ones(M, K), _ones(N, K)
-    e = (np.arange(N) % 16) - 8
+    e = (np.arange(N) % 14) - 6
     sfA = np.full((M, K // 16), 0x38, dtype=np.uint8)
     sfB = np.repeat((0x38 + 8 * e).astype(np.uint8)[:, None], K // 16, axis=1)
     Cg = _run(cuda, A, sfA, 1.0, B, sfB, 1.0)
