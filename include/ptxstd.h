@@ -145,6 +145,26 @@ PTXSTD_API int ptxstd_gemm_decode(const uint16_t* d_x, const uint8_t* d_w, const
                                   void* d_workspace, size_t workspace_bytes,
                                   ptxstd_stream stream);
 
+/* Size of the fixed device scratch array behind ptxstd_gemm_decode_noalloc (4 MiB). */
+#define PTXSTD_DECODE_NOALLOC_SCRATCH_BYTES (4u << 20)
+/* The decode GEMM for callers that cannot allocate device memory; this entry point has no
+ * counterpart in the reference (ptx-std has no host code at all). It computes what
+ * ptxstd_gemm_decode computes, with the same arguments minus the workspace, and allocates
+ * nothing: no cudaMalloc, no cudaFree, no allocating library call. It is meant for callers such
+ * as a serving loop whose device-memory plan is fixed at start-up (cudaMalloc / cudaFree can
+ * synchronise the device and fragment a sized pool, so they are not allowed per request), or a
+ * thin C / Rust binding that owns only its input and output buffers and has no allocator of its
+ * own for a workspace. Its scratch is a file-scope device array of
+ * PTXSTD_DECODE_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until the process
+ * exits; shapes whose scratch (ptxstd_gemm_decode_workspace_bytes) would exceed it are rejected
+ * with PTXSTD_EINVAL (the 16 x 57344 x 8192 decode shape fits). The first call on a device looks up
+ * the array's device address for that device; make that first call before any stream capture.
+ * All calls on a device share the array (each call clears what must start at zero); calls that
+ * overlap on the GPU, e.g. on two streams, race on it and must be serialised by the caller. */
+PTXSTD_API int ptxstd_gemm_decode_noalloc(const uint16_t* d_x, const uint8_t* d_w,
+                                          const uint8_t* d_sfw, float gw, uint16_t* d_y,
+                                          int64_t M, int64_t N, int64_t K, ptxstd_stream stream);
+
 /* ---- tcgen05 descriptors (src/tcgen05/descriptor.rs) ---------------------------------------- */
 /* InstrDescriptor::<KIND>::new for each kind. Element types use the reference's discriminants:
  * F16ElementType F16 0 / Bf16 1; FloatAccumulator F16 0 / F32 1; F8f6f4ElementType E4m3 0,

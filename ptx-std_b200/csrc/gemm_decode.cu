@@ -26,6 +26,8 @@
 //           and, at the end of each W-block segment, reduce the 128 x 16 fp32 partial into the
 //           scratch with red.global.add.v4.f32. A per-block counter of finished K stages elects the
 //           CTA that completes a block; it converts the block to bf16 and writes y (transposed).
+#include <mutex>
+
 #include "common.cuh"
 #include "data_types.cuh"
 #include "tcgen05.cuh"
@@ -602,3 +604,63 @@ int ptxstd_gemm_decode(const uint16_t* d_x, const uint8_t* d_w, const uint8_t* d
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Decode GEMM without allocation.
+//
+// Some callers cannot allocate the workspace that ptxstd_gemm_decode asks for: a serving loop
+// whose device-memory plan is fixed at start-up must not call cudaMalloc / cudaFree per request
+// (both can synchronise the device and fragment a carefully sized pool), and a thin C or Rust
+// binding may own only the input and output buffers, with no allocator of its own to create a
+// workspace. For them the scratch lives in this file-scope device array instead. Every GPU that
+// loads the library reserves it until the process exits.
+//
+// In host code `g_decode_scratch` is only a host-side stand-in for the symbol, not a device
+// address; its device address is fetched with cudaGetSymbolAddress, once per device, with that
+// device current, on the first call on that device. That first call should come before any
+// stream capture. All calls on a device share the one array: decode_prep clears the parts that
+// must start at zero on every call, and calls that overlap on the GPU (e.g. on two streams) race
+// on it.
+static __device__ __align__(256) uint8_t g_decode_scratch[PTXSTD_DECODE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[64] = {};
+
+int decode_scratch_address(void** out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PTXSTD_ECUDA;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (g_scratch_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || p == nullptr)
+            return PTXSTD_ECUDA;
+        g_scratch_ptr[dev] = p;
+    }
+    *out = g_scratch_ptr[dev];
+    return PTXSTD_OK;
+}
+
+}  // namespace
+
+extern "C" int ptxstd_gemm_decode_noalloc(const uint16_t* d_x, const uint8_t* d_w,
+                                          const uint8_t* d_sfw, float gw, uint16_t* d_y,
+                                          int64_t M, int64_t N, int64_t K, ptxstd_stream stream) {
+    if (M <= 0 || M > static_cast<int64_t>(kTok) || N <= 0 || K <= 0 || N % BM || K % BKS)
+        return PTXSTD_EINVAL;
+    if (N >= (1ll << 31) || K >= (1ll << 30)) return PTXSTD_EINVAL;
+    if (!(gw == gw) || !d_x || !d_w || !d_sfw || !d_y) return PTXSTD_EINVAL;
+    if (!ptxstd::aligned16(d_x) || !ptxstd::aligned16(d_w) || !ptxstd::aligned16(d_sfw) ||
+        !ptxstd::aligned16(d_y))
+        return PTXSTD_EINVAL;
+    // The shape's scratch must fit the fixed array.
+    if (ws_bytes(static_cast<size_t>(N), static_cast<size_t>(K)) >
+        static_cast<size_t>(PTXSTD_DECODE_NOALLOC_SCRATCH_BYTES))
+        return PTXSTD_EINVAL;
+    void* scratch = nullptr;
+    const int st = decode_scratch_address(&scratch);
+    if (st) return st;
+    return launch_decode(d_x, d_w, d_sfw, gw, d_y, M, N, K, static_cast<uint8_t*>(scratch),
+                         static_cast<cudaStream_t>(stream));
+}
