@@ -22,7 +22,8 @@
 //   warp 0: TMA producer (W tile 128 x 128 bytes, W scales 2 KiB, x image 8 KiB per stage);
 //   warp 1: TMEM owner + MMA issuer: 16 MMAs of M=128 (W rows), N=16 (tokens), K=16 per stage with
 //           the A operand in TMEM;
-//   warps 2..9: dequantise W rows into TMEM (tcgen05.st; two warps per lane quarter, 128 K each)
+//   warps 2..17: dequantise W rows into TMEM (tcgen05.st; four warps per lane quarter, 64 K each,
+//           three A buffers)
 //           and, at the end of each W-block segment, reduce the 128 x 16 fp32 partial into the
 //           scratch with red.global.add.v4.f32. A per-block counter of finished K stages elects the
 //           CTA that completes a block; it converts the block to bf16 and writes y (transposed).
@@ -47,10 +48,16 @@ constexpr uint32_t kTok = 16;           // MMA N (tokens, padded)
 constexpr uint32_t kXStageBytes = kTok * BKS * 2; // 8 KiB f16
 constexpr uint32_t kStageBytes = kWStageBytes + kSfStageBytes + kXStageBytes;
 constexpr uint32_t STAGES = 6;
-constexpr uint32_t kDqWarps = 8;
+constexpr uint32_t kDqWarps = 16;                 // dequant / epilogue warps
+constexpr uint32_t kDqPerQ = kDqWarps / 4;        // per TMEM lane quarter
+constexpr uint32_t kKPerWarp = BKS / kDqPerQ;     // K elements of a row per warp and stage (64)
+constexpr uint32_t kTokPerWarp = kTok / kDqPerQ;  // tokens reduced per warp (4)
 constexpr uint32_t kThreads = 64 + 32 * kDqWarps;
 constexpr uint32_t kACols = BKS / 2;    // f16 pairs per row per stage = 128 TMEM columns
-constexpr uint32_t kDCol = 2 * kACols;  // accumulator columns start after two A buffers
+constexpr uint32_t kABufs = 3;          // A operand buffers in TMEM
+constexpr uint32_t kDCol = kABufs * kACols;  // accumulator columns after the A buffers
+static_assert(kDCol + kTok <= 512, "TMEM budget");
+static_assert(kKPerWarp == 64 && kTokPerWarp == 4, "dequant layout below assumes 4 warps per quarter");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kPrepThreads = 256;
 
@@ -60,8 +67,8 @@ struct alignas(1024) Smem {
     uint8_t sf[STAGES][kSfStageBytes];
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
-    uint64_t afull[2];
-    uint64_t aempty[2];
+    uint64_t afull[kABufs];
+    uint64_t aempty[kABufs];
     uint64_t dfull;
     uint64_t dempty;
     uint64_t segA;
@@ -211,23 +218,17 @@ __device__ __forceinline__ bool aborted(Smem& s) {
     return *reinterpret_cast<volatile uint32_t*>(&s.abort) != 0u;
 }
 
-// tcgen05.st.32x32b.x64: 64 consecutive columns of this warp's lane quarter.
-__device__ __forceinline__ void tmem_st_x64(uint32_t taddr, const uint32_t (&v)[64]) {
+// tcgen05.st.32x32b.x32: 32 consecutive columns of this warp's lane quarter.
+__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
         "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
-        "%29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, "
-        "%47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, "
-        "%64};" ::"r"(taddr),
+        "%29, %30, %31, %32};" ::"r"(taddr),
         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
         "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
         "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
         "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
-        "r"(v[29]), "r"(v[30]), "r"(v[31]), "r"(v[32]), "r"(v[33]), "r"(v[34]), "r"(v[35]),
-        "r"(v[36]), "r"(v[37]), "r"(v[38]), "r"(v[39]), "r"(v[40]), "r"(v[41]), "r"(v[42]),
-        "r"(v[43]), "r"(v[44]), "r"(v[45]), "r"(v[46]), "r"(v[47]), "r"(v[48]), "r"(v[49]),
-        "r"(v[50]), "r"(v[51]), "r"(v[52]), "r"(v[53]), "r"(v[54]), "r"(v[55]), "r"(v[56]),
-        "r"(v[57]), "r"(v[58]), "r"(v[59]), "r"(v[60]), "r"(v[61]), "r"(v[62]), "r"(v[63])
+        "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() {
@@ -277,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptxstd::mbar_init(&s.full[i], 1);
             ptxstd::mbar_init(&s.empty[i], kDqWarps + 1);
         }
-        for (uint32_t i = 0; i < 2; ++i) {
+        for (uint32_t i = 0; i < kABufs; ++i) {
             ptxstd::mbar_init(&s.afull[i], kDqWarps);
             ptxstd::mbar_init(&s.aempty[i], 1);
         }
@@ -303,10 +304,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- producer ----------------
         if (ptxstd::elect_one()) {
             uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
-            bool waited = false;
             const uint32_t sf_tiles_per_row = K / 64;
+            // The weights do not depend on decode_prep: the first ring of W tiles and scales is
+            // issued before waiting for it; their x-image copies follow the wait.
+            bool waited = false;
+            uint32_t deferred = 0;
+            auto flush_deferred = [&]() {
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+                waited = true;
+                for (uint32_t i = 0; i < deferred; ++i)
+                    ptxstd::bulk_load(s.x[i],
+                                      wsp.ximg + static_cast<size_t>((u0 + i) % S) * kXStageBytes,
+                                      kXStageBytes, &s.full[i]);
+            };
             for (uint32_t u = u0; u < u1; ++u) {
                 const uint32_t nb = u / S, ks = u % S;
+                if (!waited && u == u0 + STAGES) flush_deferred();
                 if (!mbar_wait(&s.empty[stage], phase ^ 1u)) {
                     fail(s, err, kDetailProducer | stage);
                     break;
@@ -319,13 +332,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ptxstd::bulk_load(s.sf[stage],
                                   sfW + (static_cast<size_t>(nb) * sf_tiles_per_row + ks * 4) * 512,
                                   kSfStageBytes, &s.full[stage]);
-                if (!waited) {
-                    // x image and the cleared scratch come from decode_prep.
-                    asm volatile("griddepcontrol.wait;" ::: "memory");
-                    waited = true;
-                }
-                ptxstd::bulk_load(s.x[stage], wsp.ximg + static_cast<size_t>(ks) * kXStageBytes,
-                                  kXStageBytes, &s.full[stage]);
+                if (waited)
+                    ptxstd::bulk_load(s.x[stage], wsp.ximg + static_cast<size_t>(ks) * kXStageBytes,
+                                      kXStageBytes, &s.full[stage]);
+                else
+                    ++deferred;
                 issued |= 1u << stage;
                 issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
                 if (++stage == STAGES) {
@@ -333,6 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     phase ^= 1u;
                 }
             }
+            if (!waited && !aborted(s)) flush_deferred();
             if (aborted(s)) {
                 for (uint32_t i = 0; i < STAGES; ++i)
                     if (issued & (1u << i)) mbar_wait(&s.full[i], (issued_parity >> i) & 1u);
@@ -378,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     stage = 0;
                     phase ^= 1u;
                 }
-                if (++abuf == 2) {
+                if (++abuf == kABufs) {
                     abuf = 0;
                     aphase ^= 1u;
                 }
@@ -387,10 +399,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait(&s.drain, 0);
         }
     } else {
-        // ---------------- dequant + epilogue (warps 2..9) ----------------
-        const uint32_t q = warp & 3u;             // lane quarter = W rows 32q .. 32q+31
-        const uint32_t h = (warp - 2u) >> 2;      // K half of the stage
-        const uint32_t row = 32 * q + lane;       // W row within the block
+        // ---------------- dequant + epilogue (warps 2 .. 2 + kDqWarps) ----------------
+        const uint32_t q = warp & 3u;                  // lane quarter = W rows 32q .. 32q+31
+        const uint32_t h = (warp - 2u) >> 2;           // which 64-element K slice of the stage
+        const uint32_t row = 32 * q + lane;            // W row within the block
         uint32_t stage = 0, phase = 0, abuf = 0, aphase = 0, dphase = 0, sphase = 0;
         uint32_t seg_len = 0;
         for (uint32_t u = u0; u < u1; ++u) {
@@ -402,27 +414,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0 && !aborted(s)) fail(s, err, kDetailDq | stage);
                 break;
             }
-            // packed W: 64 bytes of this row (4 swizzled 16-byte chunks), scales: 2 x 4 bytes
+            // packed W: 32 bytes of this row (2 swizzled 16-byte chunks); scales: one 4-byte
+            // word of the blocked tile that covers these 64 K elements
             const uint8_t* wrow = s.w[stage] + row * 128;
-            uint4 pk[4];
+            uint4 pk[2];
 #pragma unroll
-            for (uint32_t i = 0; i < 4; ++i) {
-                const uint32_t c = h * 4 + i;
+            for (uint32_t i = 0; i < 2; ++i) {
+                const uint32_t c = h * 2 + i;
                 pk[i] = *reinterpret_cast<const uint4*>(wrow + ((c ^ (row & 7)) << 4));
             }
-            uint32_t sc[2];
-#pragma unroll
-            for (uint32_t t = 0; t < 2; ++t)
-                sc[t] = *reinterpret_cast<const uint32_t*>(s.sf[stage] + (h * 2 + t) * 512 +
-                                                           (row & 31) * 16 + (row >> 5) * 4);
+            const uint32_t sc = *reinterpret_cast<const uint32_t*>(
+                s.sf[stage] + h * 512 + (row & 31) * 16 + (row >> 5) * 4);
             __syncwarp();
             if (lane == 0) ptxstd::mbar_arrive(&s.empty[stage]);
-            // dequantise 128 elements into 64 f16x2 words
-            uint32_t out[64];
+            // dequantise 64 elements into 32 f16x2 words (exact: e2m1 x e4m3 fits f16)
+            uint32_t out[32];
 #pragma unroll
-            for (uint32_t i = 0; i < 4; ++i) {
-                // chunk i covers K elements 32 i .. 32 i + 31 of this half: scales 2i, 2i+1
-                const uint32_t sbytes = (sc[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+            for (uint32_t i = 0; i < 2; ++i) {
+                // chunk i covers K elements 32 i .. 32 i + 31 of this slice: scales 2i, 2i+1
+                const uint32_t sbytes = (sc >> (16 * i)) & 0xFFFFu;
                 uint32_t s2;
                 asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(s2) : "h"(static_cast<uint16_t>(sbytes)));
                 const uint32_t slo = __byte_perm(s2, 0, 0x1010);  // scale of the first 16
@@ -450,12 +460,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             t5::fence_after_thread_sync();
-            tmem_st_x64(tmem + ((32 * q) << 16) + abuf * kACols + h * 64, out);
+            tmem_st_x32(tmem + ((32 * q) << 16) + abuf * kACols + h * (kKPerWarp / 2), out);
             tmem_wait_st();
             t5::fence_before_thread_sync();
             __syncwarp();
             if (lane == 0) ptxstd::mbar_arrive(&s.afull[abuf]);
-            if (++abuf == 2) {
+            if (++abuf == kABufs) {
                 abuf = 0;
                 aphase ^= 1u;
             }
@@ -481,17 +491,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             t5::fence_before_thread_sync();
             __syncwarp();
             if (lane == 0) ptxstd::mbar_arrive(&s.dempty);
-            // this warp reduces tokens 8h .. 8h+7 of its row
-            float* dst = wsp.y32 + (static_cast<size_t>(nb) * BM + row) * kTok + 8 * h;
-            const float* fac = wsp.factors + 8 * h;
-            float v[8];
+            // this warp reduces tokens 4h .. 4h+3 of its row
+            float* dst = wsp.y32 + (static_cast<size_t>(nb) * BM + row) * kTok + kTokPerWarp * h;
+            const float* fac = wsp.factors + kTokPerWarp * h;
+            float v[4];
 #pragma unroll
-            for (int t = 0; t < 8; ++t)
-                v[t] = __uint_as_float(h ? acc[8 + t] : acc[t]) * (__ldcg(fac + t) * gw);
+            for (uint32_t t = 0; t < 4; ++t) {
+                const uint32_t a = h == 0 ? acc[t] : h == 1 ? acc[4 + t] : h == 2 ? acc[8 + t] : acc[12 + t];
+                v[t] = __uint_as_float(a) * (__ldcg(fac + t) * gw);
+            }
             red_add_v4(dst, v[0], v[1], v[2], v[3]);
-            red_add_v4(dst + 4, v[4], v[5], v[6], v[7]);
             __threadfence();
-            // All 8 warps have reduced (segA, one arrive per warp), then warp 2 publishes the
+            // All warps have reduced (segA, one arrive per warp), then warp 2 publishes the
             // finished stages and tells the others whether this CTA completes the block (segB).
             // mbarriers rather than bar.sync so that every wait stays bounded.
             __syncwarp();
@@ -518,19 +529,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             seg_len = 0;
             if (*reinterpret_cast<volatile uint32_t*>(&s.finalize)) {
                 __threadfence();
-                // 256 threads: token t = tid / 16, 8 consecutive columns (tid % 16) * 8
+                // 512 threads: token t = tid / 32, four consecutive columns (tid % 32) * 4
                 const uint32_t tid = (warp - 2) * 32 + lane;
-                const uint32_t t = tid / 16, c0 = (tid % 16) * 8;
+                const uint32_t t = tid / 32, c0 = (tid % 32) * 4;
                 if (t < M) {
-                    uint32_t o[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float a0 = __ldcg(wsp.y32 + (static_cast<size_t>(nb) * BM + c0 + 2 * j) * kTok + t);
-                        const float a1 = __ldcg(wsp.y32 + (static_cast<size_t>(nb) * BM + c0 + 2 * j + 1) * kTok + t);
-                        o[j] = dt::bf16x2_from_f32(a0, a1);
-                    }
-                    *reinterpret_cast<uint4*>(y + static_cast<size_t>(t) * N + nb * BM + c0) =
-                        make_uint4(o[0], o[1], o[2], o[3]);
+                    const float* src = wsp.y32 + (static_cast<size_t>(nb) * BM + c0) * kTok + t;
+                    const uint32_t o0 = dt::bf16x2_from_f32(__ldcg(src), __ldcg(src + kTok));
+                    const uint32_t o1 = dt::bf16x2_from_f32(__ldcg(src + 2 * kTok), __ldcg(src + 3 * kTok));
+                    *reinterpret_cast<uint2*>(y + static_cast<size_t>(t) * N + nb * BM + c0) =
+                        make_uint2(o0, o1);
                 }
             }
         }
