@@ -96,6 +96,43 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     return true;
 }
 
+// ---- clusters (src/cluster.rs, src/globals.rs) -----------------------------------------------
+// block_rank_in_cluster (globals.rs:283).
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// map_to_cta (cluster.rs:117): this CTA's .shared::cta address -> the same variable in CTA `rank`
+// of the cluster, as a .shared::cluster address.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+// cluster::barrier_sync (cluster.rs:91): every thread of every CTA of the cluster.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+                 ::: "memory");
+}
+// Remote arrive on an mbarrier of another CTA of the cluster (MBarrier::arrive on a
+// map_to_cta_rank barrier, mbarrier.rs:698).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
+// tma_load_tile_to_cluster::<2, CtaGroup::Two> without multicast (src/tma/tensor.rs:441-480): the
+// tile lands in this CTA's smem and completes on an mbarrier that may live in the peer CTA of the
+// pair (`bar` is a .shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar,
+                                                 int32_t c0, int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::"
+        "bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
 // ---- fences (src/fence.rs) -------------------------------------------------------------------
 // fence_proxy::<AsyncSharedCta> (:107): generic-proxy smem writes -> async proxy (TMA, tcgen05).
 __device__ __forceinline__ void fence_proxy_async_smem() {

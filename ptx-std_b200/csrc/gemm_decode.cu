@@ -218,6 +218,21 @@ __device__ __forceinline__ bool aborted(Smem& s) {
     return *reinterpret_cast<volatile uint32_t*>(&s.abort) != 0u;
 }
 
+// Eight E2M1 values (one 32-bit word, element 0 in the low nibble) times an f16x2 scale ->
+// four f16x2 words: the word is unpacked into its four bytes, each converted by one
+// cvt.rn.f16x2.e2m1x2 (narrow.rs pair_to_f16) and multiplied by the scale. Exact: e2m1 x e4m3
+// has at most 6 significant bits and lies in [2^-10, 2688].
+__device__ __forceinline__ void dequant8(uint32_t w, uint32_t scale2, uint32_t* o) {
+    asm("{\n\t.reg .b8 t0, t1, t2, t3;\n\t.reg .b32 u0, u1, u2, u3;\n\t"
+        "mov.b32 {t0, t1, t2, t3}, %4;\n\t"
+        "cvt.rn.f16x2.e2m1x2 u0, t0;\n\tcvt.rn.f16x2.e2m1x2 u1, t1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 u2, t2;\n\tcvt.rn.f16x2.e2m1x2 u3, t3;\n\t"
+        "mul.rn.f16x2 %0, u0, %5;\n\tmul.rn.f16x2 %1, u1, %5;\n\t"
+        "mul.rn.f16x2 %2, u2, %5;\n\tmul.rn.f16x2 %3, u3, %5;\n\t}"
+        : "=r"(o[0]), "=r"(o[1]), "=r"(o[2]), "=r"(o[3])
+        : "r"(w), "r"(scale2));
+}
+
 // tcgen05.st.32x32b.x32: 32 consecutive columns of this warp's lane quarter.
 __device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&v)[32]) {
     asm volatile(
@@ -439,19 +454,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t shi = __byte_perm(s2, 0, 0x3232);  // scale of the next 16
                 const uint32_t wv[4] = {pk[i].x, pk[i].y, pk[i].z, pk[i].w};
 #pragma unroll
-                for (uint32_t j = 0; j < 4; ++j) {
-                    const uint32_t sx = j < 2 ? slo : shi;
-#pragma unroll
-                    for (uint32_t b = 0; b < 4; ++b) {
-                        uint32_t hf;
-                        asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
-                            : "=r"(hf)
-                            : "r"(wv[j] >> (8 * b)));
-                        uint32_t prod;
-                        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(prod) : "r"(hf), "r"(sx));
-                        out[i * 16 + j * 4 + b] = prod;
-                    }
-                }
+                for (uint32_t j = 0; j < 4; ++j)
+                    dequant8(wv[j], j < 2 ? slo : shi, &out[i * 16 + j * 4]);
             }
             bool okA = mbar_wait(&s.aempty[abuf], aphase ^ 1u);
             okA = __all_sync(0xffffffffu, okA);

@@ -235,6 +235,263 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) t5::tmem_dealloc(tmem, kTmemCols);
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// CTA-pair form (tcgen05 CtaGroup::Two, src/tcgen05/mod.rs:40-57): a cluster of two CTAs computes
+// a 256 x 256 tile. CTA r of the pair TMA-loads A rows [128 r, 128 r + 128) and B rows
+// [128 r, 128 r + 128) of the tile into its own smem, each load completing on the leader's (r = 0)
+// `full` barrier (tma_load_tile_to_cluster with CtaGroup::Two and no multicast,
+// src/tma/tensor.rs:441-480). The leader alone issues tcgen05.mma.cta_group::2 (M = 256, N = 256,
+// K = 32), which reads A from each CTA's smem and the two halves of B from both, and accumulates
+// each CTA's 128 rows in that CTA's TMEM. Commits go to the matching barrier of both CTAs as two
+// unicast commits (one through mapa, src/tcgen05/sync.rs:56-57). Each CTA's epilogue drains its own
+// TMEM; the follower's epilogue warps release an accumulator by arriving on the leader's barrier.
+// Per MMA each CTA's smem supplies 4 KiB of A and 4 KiB of B, against 4 + 8 KiB in the one-CTA
+// form, and the 32 KiB stage lets the ring hold 6 stages.
+constexpr uint32_t P_BM = 256, P_BN = 256;          // tile of the pair
+constexpr uint32_t P_HALF = 128;                    // rows of A and of B per CTA
+constexpr uint32_t P_STAGES = 6;
+constexpr uint32_t kPHalfBytes = P_HALF * BK;        // 16 KiB
+constexpr uint32_t kPStageBytesPair = 4 * kPHalfBytes;  // both CTAs' A and B halves
+
+struct alignas(1024) SmemPair {
+    uint8_t a[P_STAGES][kPHalfBytes];
+    uint8_t b[P_STAGES][kPHalfBytes];
+    uint64_t full[P_STAGES];   // leader's counts both CTAs' bytes
+    uint64_t empty[P_STAGES];
+    uint64_t tfull[2];
+    uint64_t tempty[2];        // leader's: 8 arrivals (4 epilogue warps of each CTA)
+    uint64_t drain;
+    uint32_t tmem_base;
+    uint32_t abort;
+};
+constexpr size_t kSmemPairBytes = sizeof(SmemPair) + 1024;
+static_assert(kSmemPairBytes <= 232448, "shared memory budget");
+
+__device__ __forceinline__ void fail_pair(SmemPair& s, uint32_t* err, uint32_t detail) {
+    ptxstd::record_error(err, PTXSTD_ETIMEOUT, detail);
+    *reinterpret_cast<volatile uint32_t*>(&s.abort) = 1u;
+}
+__device__ __forceinline__ bool aborted_pair(SmemPair& s) {
+    return *reinterpret_cast<volatile uint32_t*>(&s.abort) != 0u;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                         const __grid_constant__ CUtensorMap tmB, uint16_t* __restrict__ C,
+                         uint32_t M, uint32_t N, uint32_t K, float alpha, uint32_t* err) {
+    extern __shared__ uint8_t smem_raw[];
+    SmemPair& s = *reinterpret_cast<SmemPair*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const uint32_t warp = ptxstd::warp_id();
+    const uint32_t lane = ptxstd::lane_id();
+    const uint32_t rank = ptxstd::cluster_ctarank();        // 0 = leader
+    const uint32_t pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+    const uint32_t num_m = M / P_BM, num_n = N / P_BN, num_tiles = num_m * num_n, num_k = K / BK;
+
+    if (warp == 0 && lane == 0) {
+        ptxstd::prefetch_tensormap(&tmA);
+        ptxstd::prefetch_tensormap(&tmB);
+        for (uint32_t i = 0; i < P_STAGES; ++i) {
+            ptxstd::mbar_init(&s.full[i], 1);
+            ptxstd::mbar_init(&s.empty[i], 1);
+        }
+        for (uint32_t i = 0; i < 2; ++i) {
+            ptxstd::mbar_init(&s.tfull[i], 1);
+            ptxstd::mbar_init(&s.tempty[i], 8);
+        }
+        ptxstd::mbar_init(&s.drain, 1);
+        s.abort = 0;
+        ptxstd::fence_mbarrier_init();
+    }
+    if (warp == 1) {
+        t5::tmem_alloc_pair(&s.tmem_base, kTmemCols);
+        t5::tmem_relinquish_pair();
+    }
+    t5::fence_before_thread_sync();
+    ptxstd::cluster_sync();  // both CTAs' barriers and TMEM exist before any remote use
+    t5::fence_after_thread_sync();
+    const uint32_t tmem = s.tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (ptxstd::elect_one()) {
+            uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
+            for (uint32_t t = pair; t < num_tiles && !aborted_pair(s); t += n_pairs) {
+                uint32_t mb, nb;
+                tile_coords(t, num_m, num_n, mb, nb);
+                for (uint32_t kb = 0; kb < num_k; ++kb) {
+                    if (!mbar_wait(&s.empty[stage], phase ^ 1u)) {
+                        fail_pair(s, err, kDetailProducer | 0x80 | stage);
+                        break;
+                    }
+                    if (aborted_pair(s)) break;
+                    const uint32_t full_leader =
+                        ptxstd::mapa_shared(ptxstd::smem_u32(&s.full[stage]), 0);
+                    if (rank == 0) ptxstd::mbar_arrive_expect_tx(&s.full[stage], kPStageBytesPair);
+                    ptxstd::tma_load_2d_pair(s.a[stage], &tmA, full_leader,
+                                             static_cast<int32_t>(kb * BK),
+                                             static_cast<int32_t>(mb * P_BM + rank * P_HALF));
+                    ptxstd::tma_load_2d_pair(s.b[stage], &tmB, full_leader,
+                                             static_cast<int32_t>(kb * BK),
+                                             static_cast<int32_t>(nb * P_BN + rank * P_HALF));
+                    issued |= 1u << stage;
+                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (aborted_pair(s) && rank == 0) {
+                for (uint32_t i = 0; i < P_STAGES; ++i)
+                    if (issued & (1u << i)) mbar_wait(&s.full[i], (issued_parity >> i) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (leader only) ----------------
+        if (rank == 0 && ptxstd::elect_one()) {
+            uint32_t idesc = 0;
+            t5::idesc_dense(/*E4m3*/ 0, /*E4m3*/ 0, /*F32*/ 1, P_BM, P_BN, idesc);
+            uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+            const uint32_t peer = 1;
+            for (uint32_t t = pair; t < num_tiles && !aborted_pair(s); t += n_pairs) {
+                if (!mbar_wait(&s.tempty[acc], acc_phase ^ 1u)) {
+                    fail_pair(s, err, kDetailMma | 0x90 | acc);
+                    break;
+                }
+                t5::fence_after_thread_sync();
+                const uint32_t d = tmem + acc * kAccCols;
+                bool ok = true;
+                for (uint32_t kb = 0; kb < num_k; ++kb) {
+                    if (!mbar_wait(&s.full[stage], phase)) {
+                        fail_pair(s, err, kDetailMma | 0x80 | stage);
+                        ok = false;
+                        break;
+                    }
+                    t5::fence_after_thread_sync();
+                    const uint64_t ad = t5::smem_desc_k128(ptxstd::smem_u32(s.a[stage]));
+                    const uint64_t bd = t5::smem_desc_k128(ptxstd::smem_u32(s.b[stage]));
+#pragma unroll
+                    for (uint32_t k = 0; k < BK / kMmaK; ++k)
+                        t5::mma_f8f6f4_pair(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0u);
+                    const uint32_t e = ptxstd::smem_u32(&s.empty[stage]);
+                    t5::commit_pair(e);
+                    t5::commit_pair(ptxstd::mapa_shared(e, peer));
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                const uint32_t f = ptxstd::smem_u32(&s.tfull[acc]);
+                t5::commit_pair(f);
+                t5::commit_pair(ptxstd::mapa_shared(f, peer));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            t5::commit_pair(ptxstd::smem_u32(&s.drain));
+            mbar_wait(&s.drain, 0);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+        const uint32_t q = warp & 3u;
+        uint32_t acc = 0, acc_phase = 0;
+        for (uint32_t t = pair; t < num_tiles; t += n_pairs) {
+            bool ok = !aborted_pair(s) && mbar_wait(&s.tfull[acc], acc_phase);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                if (lane == 0 && !aborted_pair(s)) fail_pair(s, err, kDetailEpilogue | 0x80 | acc);
+                break;
+            }
+            t5::fence_after_thread_sync();
+            uint32_t mb, nb;
+            tile_coords(t, num_m, num_n, mb, nb);
+            const uint32_t row = mb * P_BM + rank * P_HALF + 32 * q + lane;
+            uint16_t* crow = C + static_cast<size_t>(row) * N + nb * P_BN;
+            const uint32_t tbase = tmem + ((32 * q) << 16) + acc * kAccCols;
+#pragma unroll 1
+            for (uint32_t c = 0; c < P_BN / 32; ++c) {
+                uint32_t r[32];
+                t5::ld_32x32b_x32(tbase + 32 * c, r);
+                t5::wait_ld();
+                uint32_t p[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    p[j] = dt::bf16x2_from_f32(__uint_as_float(r[2 * j]) * alpha,
+                                               __uint_as_float(r[2 * j + 1]) * alpha);
+                uint4* dst = reinterpret_cast<uint4*>(crow + 32 * c);
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                    dst[v] = make_uint4(p[4 * v], p[4 * v + 1], p[4 * v + 2], p[4 * v + 3]);
+            }
+            t5::fence_before_thread_sync();
+            __syncwarp();
+            if (lane == 0)
+                ptxstd::mbar_arrive_cluster(ptxstd::mapa_shared(ptxstd::smem_u32(&s.tempty[acc]), 0));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    t5::fence_before_thread_sync();
+    ptxstd::cluster_sync();  // neither CTA of the pair leaves while the other may still use it
+    t5::fence_after_thread_sync();
+    if (warp == 1) t5::tmem_dealloc_pair(tmem, kTmemCols);
+}
+
+int launch_pair(const uint8_t* d_a, const uint8_t* d_b, uint16_t* d_c, int64_t M, int64_t N,
+                int64_t K, float alpha, cudaStream_t stream) {
+    CUtensorMap ta, tb;
+    int st = ptxstd::make_tmap_2d(&ta, d_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, K, BK, P_HALF,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = ptxstd::make_tmap_2d(&tb, d_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, K, BK, P_HALF,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(gemm_fp8_pair_kernel),
+                                      static_cast<int>(kSmemPairBytes));
+    if (st) return st;
+    uint32_t* err = ptxstd::device_error_word();
+    if (!err) return PTXSTD_ECUDA;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemPairBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // As many pairs as can be resident at once (a persistent grid), but no more than tiles.
+    static int max_pairs[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PTXSTD_ECUDA;
+    if (max_pairs[dev] == 0) {
+        cfg.gridDim = dim3(2 * static_cast<uint32_t>(ptxstd::sm_count() / 2));
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, gemm_fp8_pair_kernel, &cfg) != cudaSuccess ||
+            clusters <= 0)
+            return PTXSTD_ECUDA;
+        max_pairs[dev] = clusters;
+    }
+    const uint32_t tiles = static_cast<uint32_t>((M / P_BM) * (N / P_BN));
+    const uint32_t pairs = tiles < static_cast<uint32_t>(max_pairs[dev]) ? tiles
+                                                                        : static_cast<uint32_t>(max_pairs[dev]);
+    cfg.gridDim = dim3(2 * pairs);
+    if (cudaLaunchKernelEx(&cfg, gemm_fp8_pair_kernel, ta, tb, d_c, static_cast<uint32_t>(M),
+                           static_cast<uint32_t>(N), static_cast<uint32_t>(K), alpha,
+                           err) != cudaSuccess)
+        return PTXSTD_ECUDA;
+    return ptxstd::launch_status();
+}
+
 }  // namespace
 
 extern "C" int ptxstd_gemm_fp8(const uint8_t* d_a, const uint8_t* d_b, float sa, float sb,
@@ -262,6 +519,8 @@ extern "C" int ptxstd_gemm_fp8(const uint8_t* d_a, const uint8_t* d_b, float sa,
     uint32_t* err = ptxstd::device_error_word();
     if (!err) return PTXSTD_ECUDA;
     const float alpha = sa * sb;
+    if (M % P_BM == 0 && N % P_BN == 0)
+        return launch_pair(d_a, d_b, d_c, M, N, K, alpha, static_cast<cudaStream_t>(stream));
     gemm_fp8_kernel<<<grid, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(
         ta, tb, d_c, static_cast<uint32_t>(M), static_cast<uint32_t>(N),
         static_cast<uint32_t>(K), alpha, err);

@@ -272,6 +272,295 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) t5::tmem_dealloc(tmem, kTmemCols);
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// CTA-pair form (CtaGroup::Two): a cluster of two CTAs computes a 256 x 256 tile; CTA r loads A
+// rows [128 r, +128) and B rows [128 r, +128) into its own smem, plus the scales its own TMEM needs:
+// A's for its 128 rows and B's for all 256 columns (each CTA accumulates all N columns of its
+// rows). Scales are fetched with 2-D TMA over the blocked layout viewed as u32 [tiles, 128] (box
+// 128 x 4 = the four 512-byte tiles of one stage), so that, like the operand tiles, they complete
+// on the leader's `full` barrier. The leader issues tcgen05.cp.cta_group::2 (each CTA copies its
+// own smem scales into its own TMEM) and tcgen05.mma.cta_group::2.kind::mxf4nvf4 (M = 256).
+constexpr uint32_t P_BM = 256, P_BN = 256, P_HALF = 128;
+constexpr uint32_t P_STAGES = 5;
+constexpr uint32_t kPABytes = P_HALF * BKB;            // 16 KiB
+constexpr uint32_t kPBBytes = P_HALF * BKB;            // 16 KiB
+constexpr uint32_t kPSfaBytes = kMmas * 512;           // 2 KiB: this CTA's 128 rows
+constexpr uint32_t kPSfbBytes = (P_BN / 128) * kMmas * 512;  // 4 KiB: all 256 columns
+constexpr uint32_t kPCtaStageBytes = kPABytes + kPBBytes + kPSfaBytes + kPSfbBytes;
+constexpr uint32_t kPSfbCols = 4 * (P_BN / 128);
+constexpr uint32_t kPSlotCols = 4 + kPSfbCols;
+static_assert(kSfBase + P_STAGES * kMmas * kPSlotCols <= kTmemCols, "TMEM budget (pair)");
+
+struct alignas(1024) SmemPair {
+    uint8_t a[P_STAGES][kPABytes];
+    uint8_t b[P_STAGES][kPBBytes];
+    uint8_t sfa[P_STAGES][kPSfaBytes];
+    uint8_t sfb[P_STAGES][kPSfbBytes];
+    uint64_t full[P_STAGES];
+    uint64_t empty[P_STAGES];
+    uint64_t tfull;
+    uint64_t tempty;  // leader's: one arrive per epilogue warp of both CTAs
+    uint64_t drain;
+    uint32_t tmem_base;
+    uint32_t abort;
+};
+constexpr size_t kSmemPairBytes = sizeof(SmemPair) + 1024;
+static_assert(kSmemPairBytes <= 232448, "shared memory budget (pair)");
+
+__device__ __forceinline__ void fail_pair(SmemPair& s, uint32_t* err, uint32_t detail) {
+    ptxstd::record_error(err, PTXSTD_ETIMEOUT, detail);
+    *reinterpret_cast<volatile uint32_t*>(&s.abort) = 1u;
+}
+__device__ __forceinline__ bool aborted_pair(SmemPair& s) {
+    return *reinterpret_cast<volatile uint32_t*>(&s.abort) != 0u;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_nvfp4_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                           const __grid_constant__ CUtensorMap tmB,
+                           const __grid_constant__ CUtensorMap tmSfa,
+                           const __grid_constant__ CUtensorMap tmSfb, uint16_t* __restrict__ C,
+                           uint32_t M, uint32_t N, uint32_t K, float alpha, uint32_t* err) {
+    extern __shared__ uint8_t smem_raw[];
+    SmemPair& s = *reinterpret_cast<SmemPair*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const uint32_t warp = ptxstd::warp_id();
+    const uint32_t lane = ptxstd::lane_id();
+    const uint32_t rank = ptxstd::cluster_ctarank();
+    const uint32_t pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+    const uint32_t num_m = M / P_BM, num_n = N / P_BN, num_tiles = num_m * num_n, num_k = K / BK;
+    const uint32_t sf_tiles_per_row = K / 64;
+
+    if (warp == 0 && lane == 0) {
+        ptxstd::prefetch_tensormap(&tmA);
+        ptxstd::prefetch_tensormap(&tmB);
+        ptxstd::prefetch_tensormap(&tmSfa);
+        ptxstd::prefetch_tensormap(&tmSfb);
+        for (uint32_t i = 0; i < P_STAGES; ++i) {
+            ptxstd::mbar_init(&s.full[i], 1);
+            ptxstd::mbar_init(&s.empty[i], 1);
+        }
+        ptxstd::mbar_init(&s.tfull, 1);
+        ptxstd::mbar_init(&s.tempty, 2 * kEpiWarps);
+        ptxstd::mbar_init(&s.drain, 1);
+        s.abort = 0;
+        ptxstd::fence_mbarrier_init();
+    }
+    if (warp == 1) {
+        t5::tmem_alloc_pair(&s.tmem_base, kTmemCols);
+        t5::tmem_relinquish_pair();
+    }
+    t5::fence_before_thread_sync();
+    ptxstd::cluster_sync();
+    t5::fence_after_thread_sync();
+    const uint32_t tmem = s.tmem_base;
+
+    if (warp == 0) {
+        // ---------------- producer (both CTAs) ----------------
+        if (ptxstd::elect_one()) {
+            uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
+            for (uint32_t t = pair; t < num_tiles && !aborted_pair(s); t += n_pairs) {
+                uint32_t mb, nb;
+                tile_coords(t, num_m, num_n, mb, nb);
+                for (uint32_t kb = 0; kb < num_k; ++kb) {
+                    if (!mbar_wait(&s.empty[stage], phase ^ 1u)) {
+                        fail_pair(s, err, kDetailProducer | 0x80 | stage);
+                        break;
+                    }
+                    if (aborted_pair(s)) break;
+                    const uint32_t fl = ptxstd::mapa_shared(ptxstd::smem_u32(&s.full[stage]), 0);
+                    if (rank == 0) ptxstd::mbar_arrive_expect_tx(&s.full[stage], 2 * kPCtaStageBytes);
+                    ptxstd::tma_load_2d_pair(s.a[stage], &tmA, fl, static_cast<int32_t>(kb * BKB),
+                                             static_cast<int32_t>(mb * P_BM + rank * P_HALF));
+                    ptxstd::tma_load_2d_pair(s.b[stage], &tmB, fl, static_cast<int32_t>(kb * BKB),
+                                             static_cast<int32_t>(nb * P_BN + rank * P_HALF));
+                    const int32_t ktile = static_cast<int32_t>(kb * kMmas);
+                    ptxstd::tma_load_2d_pair(
+                        s.sfa[stage], &tmSfa, fl, 0,
+                        static_cast<int32_t>((mb * 2 + rank) * sf_tiles_per_row) + ktile);
+#pragma unroll
+                    for (uint32_t j = 0; j < P_BN / 128; ++j)
+                        ptxstd::tma_load_2d_pair(
+                            s.sfb[stage] + j * (kMmas * 512), &tmSfb, fl, 0,
+                            static_cast<int32_t>((nb * 2 + j) * sf_tiles_per_row) + ktile);
+                    issued |= 1u << stage;
+                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (aborted_pair(s) && rank == 0) {
+                for (uint32_t i = 0; i < P_STAGES; ++i)
+                    if (issued & (1u << i)) mbar_wait(&s.full[i], (issued_parity >> i) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (leader) ----------------
+        if (rank == 0 && ptxstd::elect_one()) {
+            uint32_t idesc = 0;
+            t5::idesc_mxf4nvf4(/*Ue4m3*/ 0, P_BM, P_BN, idesc);
+            uint32_t stage = 0, phase = 0, acc_phase = 0;
+            for (uint32_t t = pair; t < num_tiles && !aborted_pair(s); t += n_pairs) {
+                if (!mbar_wait(&s.tempty, acc_phase ^ 1u)) {
+                    fail_pair(s, err, kDetailMma | 0x90);
+                    break;
+                }
+                t5::fence_after_thread_sync();
+                bool ok = true;
+                for (uint32_t kb = 0; kb < num_k; ++kb) {
+                    if (!mbar_wait(&s.full[stage], phase)) {
+                        fail_pair(s, err, kDetailMma | 0x80 | stage);
+                        ok = false;
+                        break;
+                    }
+                    t5::fence_after_thread_sync();
+                    const uint64_t ad = t5::smem_desc_k128(ptxstd::smem_u32(s.a[stage]));
+                    const uint64_t bd = t5::smem_desc_k128(ptxstd::smem_u32(s.b[stage]));
+#pragma unroll
+                    for (uint32_t j = 0; j < kMmas; ++j) {
+                        const uint32_t slot = tmem + kSfBase + (stage * kMmas + j) * kPSlotCols;
+                        t5::cp_32x128b_warpx4_pair(
+                            slot, t5::smem_desc_nosw(ptxstd::smem_u32(s.sfa[stage] + 512 * j), 0, 128));
+#pragma unroll
+                        for (uint32_t h = 0; h < P_BN / 128; ++h)
+                            t5::cp_32x128b_warpx4_pair(
+                                slot + 4 + 4 * h,
+                                t5::smem_desc_nosw(
+                                    ptxstd::smem_u32(s.sfb[stage] + h * (kMmas * 512) + 512 * j), 0,
+                                    128));
+                        t5::mma_mxf4nvf4_block16_pair(tmem, ad + 2 * j, bd + 2 * j, idesc, slot,
+                                                      slot + 4, (kb | j) != 0u);
+                    }
+                    const uint32_t e = ptxstd::smem_u32(&s.empty[stage]);
+                    t5::commit_pair(e);
+                    t5::commit_pair(ptxstd::mapa_shared(e, 1));
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                const uint32_t f = ptxstd::smem_u32(&s.tfull);
+                t5::commit_pair(f);
+                t5::commit_pair(ptxstd::mapa_shared(f, 1));
+                acc_phase ^= 1u;
+            }
+            t5::commit_pair(ptxstd::smem_u32(&s.drain));
+            mbar_wait(&s.drain, 0);
+        }
+    } else {
+        // ---------------- epilogue: warps 2..9 of both CTAs ----------------
+        const uint32_t q = warp & 3u;
+        const uint32_t half = (warp - 2u) >> 2;
+        uint32_t acc_phase = 0;
+        const uint32_t tempty_leader = ptxstd::mapa_shared(ptxstd::smem_u32(&s.tempty), 0);
+        for (uint32_t t = pair; t < num_tiles; t += n_pairs) {
+            bool ok = !aborted_pair(s) && mbar_wait(&s.tfull, acc_phase);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                if (lane == 0 && !aborted_pair(s)) fail_pair(s, err, kDetailEpilogue | 0x80);
+                break;
+            }
+            t5::fence_after_thread_sync();
+            uint32_t r[128];
+            const uint32_t tbase = tmem + ((32 * q) << 16) + half * 128;
+            {
+                uint32_t(&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
+                uint32_t(&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
+                uint32_t(&r2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[64]);
+                uint32_t(&r3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[96]);
+                t5::ld_32x32b_x32(tbase, r0);
+                t5::ld_32x32b_x32(tbase + 32, r1);
+                t5::ld_32x32b_x32(tbase + 64, r2);
+                t5::ld_32x32b_x32(tbase + 96, r3);
+                t5::wait_ld();
+            }
+            t5::fence_before_thread_sync();
+            __syncwarp();
+            if (lane == 0) ptxstd::mbar_arrive_cluster(tempty_leader);
+            acc_phase ^= 1u;
+
+            uint32_t mb, nb;
+            tile_coords(t, num_m, num_n, mb, nb);
+            const uint32_t row = mb * P_BM + rank * P_HALF + 32 * q + lane;
+            uint16_t* crow = C + static_cast<size_t>(row) * N + nb * P_BN + half * 128;
+#pragma unroll
+            for (uint32_t c = 0; c < 16; ++c) {
+                uint32_t p[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    p[j] = dt::bf16x2_from_f32(__uint_as_float(r[8 * c + 2 * j]) * alpha,
+                                               __uint_as_float(r[8 * c + 2 * j + 1]) * alpha);
+                reinterpret_cast<uint4*>(crow)[c] = make_uint4(p[0], p[1], p[2], p[3]);
+            }
+        }
+    }
+
+    t5::fence_before_thread_sync();
+    ptxstd::cluster_sync();
+    t5::fence_after_thread_sync();
+    if (warp == 1) t5::tmem_dealloc_pair(tmem, kTmemCols);
+}
+
+int launch_pair(const uint8_t* d_a, const uint8_t* d_sfa, const uint8_t* d_b,
+                const uint8_t* d_sfb, uint16_t* d_c, int64_t M, int64_t N, int64_t K, float alpha,
+                cudaStream_t stream) {
+    CUtensorMap ta, tb, tsa, tsb;
+    int st = ptxstd::make_tmap_2d(&ta, d_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, M, K / 2, BKB,
+                                  P_HALF, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = ptxstd::make_tmap_2d(&tb, d_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2, BKB,
+                              P_HALF, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    // blocked scales as u32 [tiles, 128]: one row per 512-byte tile
+    st = ptxstd::make_tmap_2d(&tsa, d_sfa, CU_TENSOR_MAP_DATA_TYPE_UINT32, 128,
+                              (M / 128) * (K / 64), 512, 128, kMmas, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    st = ptxstd::make_tmap_2d(&tsb, d_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 128,
+                              (N / 128) * (K / 64), 512, 128, kMmas, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(gemm_nvfp4_pair_kernel),
+                                      static_cast<int>(kSmemPairBytes));
+    if (st) return st;
+    uint32_t* err = ptxstd::device_error_word();
+    if (!err) return PTXSTD_ECUDA;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemPairBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static int max_pairs[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PTXSTD_ECUDA;
+    if (max_pairs[dev] == 0) {
+        cfg.gridDim = dim3(2 * static_cast<uint32_t>(ptxstd::sm_count() / 2));
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, gemm_nvfp4_pair_kernel, &cfg) !=
+                cudaSuccess ||
+            clusters <= 0)
+            return PTXSTD_ECUDA;
+        max_pairs[dev] = clusters;
+    }
+    const uint32_t tiles = static_cast<uint32_t>((M / P_BM) * (N / P_BN));
+    const uint32_t pairs =
+        tiles < static_cast<uint32_t>(max_pairs[dev]) ? tiles : static_cast<uint32_t>(max_pairs[dev]);
+    cfg.gridDim = dim3(2 * pairs);
+    if (cudaLaunchKernelEx(&cfg, gemm_nvfp4_pair_kernel, ta, tb, tsa, tsb, d_c,
+                           static_cast<uint32_t>(M), static_cast<uint32_t>(N),
+                           static_cast<uint32_t>(K), alpha, err) != cudaSuccess)
+        return PTXSTD_ECUDA;
+    return ptxstd::launch_status();
+}
+
 }  // namespace
 
 extern "C" int ptxstd_gemm_nvfp4(const uint8_t* d_a, const uint8_t* d_sfa, float ga,
@@ -284,6 +573,9 @@ extern "C" int ptxstd_gemm_nvfp4(const uint8_t* d_a, const uint8_t* d_sfa, float
         !ptxstd::aligned16(d_b) || !ptxstd::aligned16(d_c) || !ptxstd::aligned16(d_sfa) ||
         !ptxstd::aligned16(d_sfb))
         return PTXSTD_EINVAL;
+    if (M % P_BM == 0 && N % P_BN == 0)
+        return launch_pair(d_a, d_sfa, d_b, d_sfb, d_c, M, N, K, ga * gb,
+                           static_cast<cudaStream_t>(stream));
     CUtensorMap ta, tb;
     int st = ptxstd::make_tmap_2d(&ta, d_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, M, K / 2, BKB,
                                   BM, CU_TENSOR_MAP_SWIZZLE_128B);

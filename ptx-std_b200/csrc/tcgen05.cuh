@@ -291,6 +291,55 @@ __device__ __forceinline__ void cp_32x128b_warpx4(uint32_t taddr, uint64_t src_d
                  : "memory");
 }
 
+// ---- CtaGroup::Two forms: one thread of the CTA pair issues for both CTAs ------------------
+// (src/tcgen05/mod.rs:40-57). A kernel uses either these or the cta_group::1 forms, never both.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(smem_slot)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+// commit::<Two> to an mbarrier given as a .shared::cluster address (own or peer CTA).
+__device__ __forceinline__ void commit_pair(uint32_t cluster_bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            cluster_bar)
+        : "memory");
+}
+// mma::<Two> kind::f8f6f4: M = 256 rows over the pair (128 from each CTA's smem), B's N rows split
+// across the two CTAs' smem, D in both CTAs' TMEM at the same address.
+__device__ __forceinline__ void mma_f8f6f4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_mxf4nvf4_block16_pair(uint32_t d_tmem, uint64_t a_desc,
+                                                          uint64_t b_desc, uint32_t idesc,
+                                                          uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %6, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%4], "
+        "[%5], p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+        : "memory");
+}
+// copy::<Two, S32x128bWarpx4>: each CTA of the pair copies from its own smem to its own TMEM.
+__device__ __forceinline__ void cp_32x128b_warpx4_pair(uint32_t taddr, uint64_t src_desc) {
+    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc)
+                 : "memory");
+}
+
 // load::<S32x32b, x32> (src/tcgen05/ld_st.rs:252-300): lane (32 * (warp % 4) + laneid), 32
 // consecutive columns -> 32 registers.
 __device__ __forceinline__ void ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {

@@ -56,11 +56,13 @@ def _ones(rows, K):
     return np.full((rows, K // 2), 0x22, dtype=np.uint8)  # E2M1 1.0 in both nibbles
 
 
-def test_row_scales(cuda, oracle):
-    """A = B = 1, sfA[m, :] = 2^(m % 8 - 4), sfB = 1: C[m, n] = K * sfA(m)."""
-    M, N, K = 128, 256, 256
+@pytest.mark.parametrize("M", [128, 256])
+def test_row_scales(cuda, oracle, M):
+    """A = B = 1, sfA[m, :] = 2^(m % 8 - 4), sfB = 1: C[m, n] = K * sfA(m).
+    M = 256 runs the CTA-pair kernel (rows 128..255 come from the second CTA)."""
+    N, K = 256, 256
     A, B = _ones(M, K), _ones(N, K)
-    e = (np.arange(M) % 8) - 4
+    e = (np.arange(M) % 8) - 4 + (np.arange(M) >= 128)
     sfA = np.repeat((0x38 + 8 * e).astype(np.uint8)[:, None], K // 16, axis=1)
     sfB = np.full((N, K // 16), 0x38, dtype=np.uint8)
     Cg = _run(cuda, A, sfA, 1.0, B, sfB, 1.0)
@@ -68,9 +70,10 @@ def test_row_scales(cuda, oracle):
     assert np.array_equal(Cg, want.astype(np.float32)), np.argwhere(Cg != want)[:8]
 
 
-def test_k_block_scales(cuda, oracle):
+@pytest.mark.parametrize("M", [128, 256])
+def test_k_block_scales(cuda, oracle, M):
     """sfA[m, s] = 2^(s % 4), sfB[n, s] = 2^((s // 4) % 4): each K block weighs differently."""
-    M, N, K = 128, 256, 1024
+    N, K = 256, 1024
     A, B = _ones(M, K), _ones(N, K)
     s = np.arange(K // 16)
     sfA = np.repeat((0x38 + 8 * (s % 4)).astype(np.uint8)[None, :], M, axis=0)
@@ -80,9 +83,10 @@ def test_k_block_scales(cuda, oracle):
     assert np.all(Cg == want), (Cg[0, :4], want)
 
 
-def test_col_scales(cuda, oracle):
+@pytest.mark.parametrize("M", [128, 256])
+def test_col_scales(cuda, oracle, M):
     """sfB[n, :] = 2^(n % 14 - 6) (normal E4M3 powers of two): C[m, n] = K * sfB(n)."""
-    M, N, K = 128, 512, 256
+    N, K = 512, 256
     A, B = _ones(M, K), _ones(N, K)
     e = (np.arange(N) % 14) - 6
     sfA = np.full((M, K // 16), 0x38, dtype=np.uint8)
