@@ -393,6 +393,7 @@ class DecodeGemm:
         self.bytes = w_bytes + self.M * self.K * 2 + self.M * self.n_local * 2
         self.in_bytes = self.M * self.K * 2            # per step from host: the activations
         self.out_bytes = self.M * self.N * 2           # per step to host: the gathered output
+        self.gather_bytes = (world - 1) * self.M * self.n_local * 2  # NVLink bytes in per rank
         self.config = {"workload": "decode_gemm x[16,8192] bf16 -> mxfp8, W nvfp4 [57344,8192]",
                        "M": self.M, "N": self.N, "K": self.K, "n_per_gpu": self.n_local,
                        "sharding": "W along N, NCCL all-gather of output columns",
@@ -416,37 +417,33 @@ class DecodeGemm:
             w, sfw = ptxstd.quantize_nvfp4(wb, gw, sf_layout=1)
             del wb
             self.sets.append((w, sfw, gw))
-        self.y = torch.empty((self.M, self.n_local), dtype=torch.bfloat16, device="cuda")
         self.x_host = self.x.cpu().pin_memory()
-        self.y_full = torch.empty((self.world, self.M, self.n_local), dtype=torch.bfloat16,
-                                  device="cuda")
-        self.y_host = torch.empty((self.world, self.M, self.n_local), dtype=torch.bfloat16,
-                                  pin_memory=True)
-        self.launches_per_step = 2
-
-    def _gather(self):
+        # every rank ends the step with the full [16, N] output
+        self.y = torch.empty((self.M, self.N), dtype=torch.bfloat16, device="cuda")
+        self.y_host = torch.empty((self.M, self.N), dtype=torch.bfloat16, pin_memory=True)
+        self.dist = None
         if self.world > 1:
-            import torch.distributed as td
-            td.all_gather_into_tensor(self.y_full.view(-1), self.y.view(-1))
+            from ptxstd.dist import Dist
+            self.dist = Dist.from_torch()
+
+    def _decode(self, i):
+        import ptxstd
+        w, sfw, gw = self.sets[i % 2]
+        if self.dist is None:
+            ptxstd.gemm_decode(self.x, w, sfw, gw, out=self.y)
+            return 2
+        # local shard, in-place NCCL all-gather over NVLink, device-side unshard permute
+        self.dist.gemm_decode(self.x, w, sfw, gw, self.N, out=self.y)
+        return 3
 
     def step(self, i):
-        import ptxstd
-        w, sfw, gw = self.sets[i % 2]
-        ptxstd.gemm_decode(self.x, w, sfw, gw, out=self.y)
-        self._gather()
-        return 2
+        return self._decode(i)
 
     def e2e_step(self, i):
-        import ptxstd
-        w, sfw, gw = self.sets[i % 2]
         self.x.copy_(self.x_host, non_blocking=True)
-        ptxstd.gemm_decode(self.x, w, sfw, gw, out=self.y)
-        self._gather()
-        if self.world > 1:
-            self.y_host.copy_(self.y_full, non_blocking=True)
-        else:
-            self.y_host[0].copy_(self.y, non_blocking=True)
-        return 2
+        n = self._decode(i)
+        self.y_host.copy_(self.y, non_blocking=True)
+        return n
 
     def value(self, seconds_per_step: float) -> float:
         return self.bytes / seconds_per_step / 1e9

@@ -165,6 +165,33 @@ PTXSTD_API int ptxstd_gemm_decode_noalloc(const uint16_t* d_x, const uint8_t* d_
                                           const uint8_t* d_sfw, float gw, uint16_t* d_y,
                                           int64_t M, int64_t N, int64_t K, ptxstd_stream stream);
 
+/* ---- multi-GPU: N-sharded weights over NCCL ---------------------------------------------------
+ * No counterpart in the reference (it has no host-side communication). One rank per GPU; ranks
+ * share an NCCL unique id (e.g. broadcast over torch.distributed or MPI) and create a
+ * communicator on their current device. NCCL is loaded at run time (PTXSTD_ENCCL if missing). */
+typedef struct ptxstd_dist ptxstd_dist;
+PTXSTD_API int ptxstd_dist_unique_id(uint8_t* out_128);
+PTXSTD_API int ptxstd_dist_init(const uint8_t* unique_id_128, int nranks, int rank,
+                                ptxstd_dist** out);
+PTXSTD_API int ptxstd_dist_free(ptxstd_dist* dist);
+PTXSTD_API int ptxstd_dist_size(const ptxstd_dist* dist, int* nranks, int* rank);
+/* NVFP4 GEMM with B split along N: this rank holds B rows [rank*N/world, (rank+1)*N/world) (and
+ * their scales) and computes C_shard [M, N/world]. No communication. */
+PTXSTD_API int ptxstd_gemm_nvfp4_sharded(const ptxstd_dist* dist, const uint8_t* d_a,
+                                         const uint8_t* d_sfa, float ga, const uint8_t* d_b_shard,
+                                         const uint8_t* d_sfb_shard, float gb, uint16_t* d_c_shard,
+                                         int64_t M, int64_t N, int64_t K, ptxstd_stream stream);
+/* Decode GEMM with W split along N: each rank computes its [M, N/world] block, NCCL all-gathers
+ * the blocks in place over NVLink, and y [M, N] (row-major, every rank) is assembled on the
+ * device. workspace: ptxstd_gemm_decode_sharded_workspace_bytes bytes, 1024-byte aligned. */
+PTXSTD_API size_t ptxstd_gemm_decode_sharded_workspace_bytes(const ptxstd_dist* dist, int64_t M,
+                                                             int64_t N, int64_t K);
+PTXSTD_API int ptxstd_gemm_decode_sharded(const ptxstd_dist* dist, const uint16_t* d_x,
+                                          const uint8_t* d_w_shard, const uint8_t* d_sfw_shard,
+                                          float gw, uint16_t* d_y, int64_t M, int64_t N,
+                                          int64_t K, void* d_workspace, size_t workspace_bytes,
+                                          ptxstd_stream stream);
+
 /* ---- tcgen05 descriptors (src/tcgen05/descriptor.rs) ---------------------------------------- */
 /* InstrDescriptor::<KIND>::new for each kind. Element types use the reference's discriminants:
  * F16ElementType F16 0 / Bf16 1; FloatAccumulator F16 0 / F32 1; F8f6f4ElementType E4m3 0,

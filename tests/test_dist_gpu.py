@@ -1,0 +1,100 @@
+"""N-sharded GEMMs on two GPUs through libptxstd's NCCL layer (needs >= 2 B200s; skips otherwise).
+
+Two spawned ranks (one per GPU) build the same seeded weights, keep their N shard, and run
+  - ptxstd_gemm_decode_sharded: every rank must end with the full [M, N] output, equal to the
+    single-GPU decode of the unsharded weights within the GEMM test tolerance;
+  - ptxstd_gemm_nvfp4_sharded: each rank's C columns must equal, bit for bit, the same columns of
+    the unsharded GEMM (the computation of a column does not depend on the sharding).
+torch.distributed (gloo) only carries the NCCL unique id.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _blocked(sf):
+    rows, S = sf.shape
+    r = np.arange(rows)[:, None]
+    s = np.arange(S)[None, :]
+    off = ((r // 128) * (S // 4) + s // 4) * 512 + (r % 32) * 16 + ((r // 32) % 4) * 4 + s % 4
+    out = np.empty(rows * S, dtype=np.uint8)
+    out[off.ravel()] = sf.ravel()
+    return out
+
+
+def _worker(rank, world, port, out_dir):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [os.path.join(root, "ptx-std_b200"), os.path.join(root, "oracle")]
+    import torch
+    import torch.distributed as td
+
+    import oracle as O
+    import ptxstd
+    from ptxstd import workloads
+    from ptxstd.dist import Dist, shard_range
+
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    td.init_process_group("gloo", rank=rank, world_size=world)
+    dist = Dist.from_torch()
+    msgs = []
+    M, N, K = 16, 1024, 2048
+    x = workloads.normal_bf16(M, K, seed=21)
+    wb = workloads.normal_bf16(N, K, std=0.02, seed=22)
+    gw = float(np.abs((wb.astype(np.uint32) << 16).view(np.float32)).max() / (448.0 * 6.0))
+    W, sfW = O.quantize_nvfp4(wb, gw)
+    lo, hi = shard_range(N, world, rank)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    xd = dev(x.view(np.int16)).view(torch.bfloat16)
+    y = dist.gemm_decode(xd, dev(W[lo:hi]), dev(_blocked(sfW[lo:hi])), gw, N)
+    yfull = ptxstd.gemm_decode(xd, dev(W), dev(_blocked(sfW)), gw)
+    torch.cuda.synchronize()
+    a, b = y.float().cpu().numpy(), yfull.float().cpu().numpy()
+    r, c = np.meshgrid(np.arange(M), np.arange(N), indexing="ij")
+    _, mag = O.gemm_decode_ref(x, W, sfW, gw, r.ravel(), c.ravel())
+    tol = 2.0 ** -10 * mag.reshape(M, N) + 2.0 ** -8 * np.maximum(np.abs(a), np.abs(b))
+    if not (np.abs(a - b) <= tol).all():
+        msgs.append(f"rank {rank}: sharded decode differs")
+
+    Ma = 256
+    A, sfA = O.quantize_nvfp4(workloads.normal_bf16(Ma, K, seed=23), 0.01)
+    cs = dist.gemm_nvfp4(dev(A), dev(_blocked(sfA)), 0.01, dev(W[lo:hi]),
+                         dev(_blocked(sfW[lo:hi])), gw, N)
+    cf = ptxstd.gemm_nvfp4(dev(A), dev(_blocked(sfA)), 0.01, dev(W), dev(_blocked(sfW)), gw)
+    torch.cuda.synchronize()
+    if not torch.equal(cs, cf[:, lo:hi]):
+        msgs.append(f"rank {rank}: sharded nvfp4 columns differ")
+    code, _ = ptxstd.last_device_error()
+    if code:
+        msgs.append(f"rank {rank}: device error {code}")
+    with open(os.path.join(out_dir, f"rank{rank}"), "w") as f:
+        f.write("\n".join(msgs) if msgs else "ok")
+    dist.close()
+    td.barrier()
+    td.destroy_process_group()
+
+
+def test_sharded_two_gpus(cuda, tmp_path):
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    mp.start_processes(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    for r in range(2):
+        assert open(tmp_path / f"rank{r}").read() == "ok"
