@@ -55,21 +55,57 @@ def profiled_traffic(kernel: str):
 # ---- clocks ---------------------------------------------------------------------------------
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+    """SM clock and throttle-reason samples taken while the timed region runs.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Polls NVML every 2 ms in a thread (reading clocks only; nothing is set), so that even a
+    timed region of a few tens of milliseconds gets samples; falls back to nvidia-smi -lms 100.
+    """
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap"}
 
     def __init__(self, device_index: int):
         self.dev = device_index
+        self.samples: list[tuple[float, float, int]] = []
         self.proc = None
         self.lines: list[str] = []
+        self._stop = threading.Event()
+        self.nvml = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(self.dev).uuid)
+        return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid)
 
     def start(self):
         try:
+            self.nvml, h = self._nvml_handle()
+            nv = self.nvml
+            smax = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                        r = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                        self.samples.append((sm, smax, r))
+                    except Exception:
+                        pass
+                    time.sleep(0.002)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nvml = None
+        try:
+            fields = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                      "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                      "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={fields}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
@@ -82,8 +118,20 @@ class ClockSampler:
             self.lines.append(ln.strip())
 
     def stop(self) -> dict:
+        if self.nvml is not None:
+            self._stop.set()
+            self.thread.join(timeout=2)
+            sm = [x[0] for x in self.samples]
+            reasons = set()
+            for _, _, r in self.samples:
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        reasons.add(name)
+            return {"sm_mhz": statistics.median(sm) if sm else None,
+                    "sm_max_mhz": self.samples[0][1] if self.samples else None,
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "nvml 2 ms"}
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"]}
         time.sleep(0.25)
         self.proc.terminate()
         try:
@@ -106,7 +154,7 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi 100 ms"}
 
 
 # ---- distributed plumbing -------------------------------------------------------------------
@@ -382,7 +430,6 @@ class DecodeGemm:
     dtype = "mxfp8(x) x nvfp4(W) -> f16 tensor cores, f32 acc -> bf16"
     M, N, K = 16, 57344, 8192
     kernel = "gemm_decode_kernel"
-    collective = True
     scaling = "strong"
     parallelism = "n-shard"
 
@@ -439,6 +486,11 @@ class DecodeGemm:
     def step(self, i):
         return self._decode(i)
 
+    def teardown(self):
+        if self.dist is not None:
+            self.dist.close()
+            self.dist = None
+
     def e2e_step(self, i):
         self.x.copy_(self.x_host, non_blocking=True)
         n = self._decode(i)
@@ -485,8 +537,9 @@ def run_ours(args, wl) -> dict | None:
     torch.cuda.synchronize()
 
     # The K timed steps are captured once into a CUDA graph and replayed, so that the device
-    # time is not padded by host-side launch gaps between short kernels. A step with a
-    # collective (multi-GPU decode) is launched eagerly instead.
+    # time is not padded by host-side launch gaps between short kernels. The multi-GPU decode's
+    # NCCL all-gather is issued by libptxstd on the same stream and is captured with it; a
+    # workload marked `collective` (a torch.distributed call in its step) would run eagerly.
     use_graph = not args.no_graph and not (dist.world > 1 and getattr(wl, "collective", False))
     graph = None
     launches = 0
@@ -501,7 +554,7 @@ def run_ours(args, wl) -> dict | None:
     sampler = ClockSampler(torch.cuda.current_device()) if dist.rank == 0 else None
     if sampler:
         sampler.start()
-        time.sleep(0.3)
+        time.sleep(0.02)
     dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -535,6 +588,9 @@ def run_ours(args, wl) -> dict | None:
 
     ms_max = dist.max(ms)
     e2e_max = dist.max(e2e_ms)
+    if hasattr(wl, "teardown"):
+        torch.cuda.synchronize()
+        wl.teardown()
     rank = dist.rank
     world = dist.world
     dist.close()

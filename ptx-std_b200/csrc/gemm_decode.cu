@@ -19,7 +19,11 @@
 // Kernel 2, gemm_decode (persistent, one CTA per SM, launched with programmatic dependent launch so
 //   its setup and first weight loads overlap kernel 1):
 //   work = (128-row W block, 256-K stage) units split evenly over the CTAs ("stream-K");
-//   warp 0: TMA producer (W tile 128 x 128 bytes, W scales 2 KiB, x image 8 KiB per stage);
+//   warp 0: weight producer: W tile 128 x 128 bytes + W scales 2 KiB per stage into an 8-stage
+//           ring that the dequant warps release as soon as they have read it (so the HBM stream
+//           never waits on MMA completion, nor on kernel 1);
+//   warp 18: x-image producer: the 8 KiB f16 B operand per stage into a 4-stage ring released by
+//           the MMA commit (it waits for kernel 1 with griddepcontrol.wait);
 //   warp 1: TMEM owner + MMA issuer: 16 MMAs of M=128 (W rows), N=16 (tokens), K=16 per stage with
 //           the A operand in TMEM;
 //   warps 2..17: dequantise W rows into TMEM (tcgen05.st; four warps per lane quarter, 64 K each,
@@ -46,13 +50,15 @@ constexpr uint32_t kWStageBytes = BM * BKS / 2;   // 16 KiB packed E2M1
 constexpr uint32_t kSfStageBytes = BM * BKS / 16; // 2 KiB E4M3
 constexpr uint32_t kTok = 16;           // MMA N (tokens, padded)
 constexpr uint32_t kXStageBytes = kTok * BKS * 2; // 8 KiB f16
-constexpr uint32_t kStageBytes = kWStageBytes + kSfStageBytes + kXStageBytes;
-constexpr uint32_t STAGES = 6;
+constexpr uint32_t kWRingBytes = kWStageBytes + kSfStageBytes;   // one weight stage
+constexpr uint32_t WST = 8;             // weight ring: released by the dequant warps after their loads
+constexpr uint32_t XST = 4;             // x-image ring: released by the MMA commit
 constexpr uint32_t kDqWarps = 16;                 // dequant / epilogue warps
 constexpr uint32_t kDqPerQ = kDqWarps / 4;        // per TMEM lane quarter
 constexpr uint32_t kKPerWarp = BKS / kDqPerQ;     // K elements of a row per warp and stage (64)
 constexpr uint32_t kTokPerWarp = kTok / kDqPerQ;  // tokens reduced per warp (4)
-constexpr uint32_t kThreads = 64 + 32 * kDqWarps;
+constexpr uint32_t kXWarp = 2 + kDqWarps;          // x-image producer warp
+constexpr uint32_t kThreads = 32 * (kXWarp + 1);
 constexpr uint32_t kACols = BKS / 2;    // f16 pairs per row per stage = 128 TMEM columns
 constexpr uint32_t kABufs = 3;          // A operand buffers in TMEM
 constexpr uint32_t kDCol = kABufs * kACols;  // accumulator columns after the A buffers
@@ -62,11 +68,13 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kPrepThreads = 256;
 
 struct alignas(1024) Smem {
-    uint8_t w[STAGES][kWStageBytes];
-    uint8_t x[STAGES][kXStageBytes];
-    uint8_t sf[STAGES][kSfStageBytes];
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
+    uint8_t w[WST][kWStageBytes];
+    uint8_t x[XST][kXStageBytes];
+    uint8_t sf[WST][kSfStageBytes];
+    uint64_t wfull[WST];
+    uint64_t wempty[WST];
+    uint64_t xfull[XST];
+    uint64_t xempty[XST];
     uint64_t afull[kABufs];
     uint64_t aempty[kABufs];
     uint64_t dfull;
@@ -82,7 +90,8 @@ struct alignas(1024) Smem {
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-enum : uint32_t { kDetailProducer = 0x3100, kDetailMma = 0x3200, kDetailDq = 0x3300 };
+enum : uint32_t { kDetailProducer = 0x3100, kDetailMma = 0x3200, kDetailDq = 0x3300,
+                  kDetailXProducer = 0x3400 };
 
 // Workspace layout (bytes): y32 [N][16] f32 | counters [N/128] u32 (16 B aligned) |
 // x image [K/256][8 KiB] | factors [16] f32.
@@ -289,9 +298,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0 && lane == 0) {
         ptxstd::prefetch_tensormap(&tmW);
-        for (uint32_t i = 0; i < STAGES; ++i) {
-            ptxstd::mbar_init(&s.full[i], 1);
-            ptxstd::mbar_init(&s.empty[i], kDqWarps + 1);
+        for (uint32_t i = 0; i < WST; ++i) {
+            ptxstd::mbar_init(&s.wfull[i], 1);
+            ptxstd::mbar_init(&s.wempty[i], kDqWarps);
+        }
+        for (uint32_t i = 0; i < XST; ++i) {
+            ptxstd::mbar_init(&s.xfull[i], 1);
+            ptxstd::mbar_init(&s.xempty[i], 1);
         }
         for (uint32_t i = 0; i < kABufs; ++i) {
             ptxstd::mbar_init(&s.afull[i], kDqWarps);
@@ -316,53 +329,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = s.tmem_base;
 
     if (warp == 0) {
-        // ---------------- producer ----------------
+        // ---------------- weight producer: W tiles + W scales (no dependency on decode_prep) ----
         if (ptxstd::elect_one()) {
             uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
             const uint32_t sf_tiles_per_row = K / 64;
-            // The weights do not depend on decode_prep: the first ring of W tiles and scales is
-            // issued before waiting for it; their x-image copies follow the wait.
-            bool waited = false;
-            uint32_t deferred = 0;
-            auto flush_deferred = [&]() {
-                asm volatile("griddepcontrol.wait;" ::: "memory");
-                waited = true;
-                for (uint32_t i = 0; i < deferred; ++i)
-                    ptxstd::bulk_load(s.x[i],
-                                      wsp.ximg + static_cast<size_t>((u0 + i) % S) * kXStageBytes,
-                                      kXStageBytes, &s.full[i]);
-            };
-            for (uint32_t u = u0; u < u1; ++u) {
-                const uint32_t nb = u / S, ks = u % S;
-                if (!waited && u == u0 + STAGES) flush_deferred();
-                if (!mbar_wait(&s.empty[stage], phase ^ 1u)) {
+            uint32_t nb = u0 / S, ks = u0 % S;
+            for (uint32_t u = u0; u < u1; ++u, ks = (ks + 1 == S) ? 0 : ks + 1, nb += (ks == 0)) {
+                if (!mbar_wait(&s.wempty[stage], phase ^ 1u)) {
                     fail(s, err, kDetailProducer | stage);
                     break;
                 }
                 if (aborted(s)) break;
-                ptxstd::mbar_arrive_expect_tx(&s.full[stage], kStageBytes);
-                ptxstd::tma_load_2d(s.w[stage], &tmW, &s.full[stage],
+                ptxstd::mbar_arrive_expect_tx(&s.wfull[stage], kWRingBytes);
+                ptxstd::tma_load_2d(s.w[stage], &tmW, &s.wfull[stage],
                                     static_cast<int32_t>(ks * (BKS / 2)),
                                     static_cast<int32_t>(nb * BM));
                 ptxstd::bulk_load(s.sf[stage],
                                   sfW + (static_cast<size_t>(nb) * sf_tiles_per_row + ks * 4) * 512,
-                                  kSfStageBytes, &s.full[stage]);
-                if (waited)
-                    ptxstd::bulk_load(s.x[stage], wsp.ximg + static_cast<size_t>(ks) * kXStageBytes,
-                                      kXStageBytes, &s.full[stage]);
-                else
-                    ++deferred;
+                                  kSfStageBytes, &s.wfull[stage]);
                 issued |= 1u << stage;
                 issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-                if (++stage == STAGES) {
+                if (++stage == WST) {
                     stage = 0;
                     phase ^= 1u;
                 }
             }
-            if (!waited && !aborted(s)) flush_deferred();
             if (aborted(s)) {
-                for (uint32_t i = 0; i < STAGES; ++i)
-                    if (issued & (1u << i)) mbar_wait(&s.full[i], (issued_parity >> i) & 1u);
+                for (uint32_t i = 0; i < WST; ++i)
+                    if (issued & (1u << i)) mbar_wait(&s.wfull[i], (issued_parity >> i) & 1u);
+            }
+        }
+    } else if (warp == kXWarp) {
+        // ---------------- x-image producer (waits for decode_prep) ----------------
+        if (ptxstd::elect_one()) {
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
+            uint32_t ks = u0 % S;
+            for (uint32_t u = u0; u < u1; ++u, ks = (ks + 1 == S) ? 0 : ks + 1) {
+                if (!mbar_wait(&s.xempty[stage], phase ^ 1u)) {
+                    fail(s, err, kDetailXProducer | stage);
+                    break;
+                }
+                if (aborted(s)) break;
+                ptxstd::mbar_arrive_expect_tx(&s.xfull[stage], kXStageBytes);
+                ptxstd::bulk_load(s.x[stage], wsp.ximg + static_cast<size_t>(ks) * kXStageBytes,
+                                  kXStageBytes, &s.xfull[stage]);
+                issued |= 1u << stage;
+                issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                if (++stage == XST) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (aborted(s)) {
+                for (uint32_t i = 0; i < XST; ++i)
+                    if (issued & (1u << i)) mbar_wait(&s.xfull[i], (issued_parity >> i) & 1u);
             }
         }
     } else if (warp == 1) {
@@ -382,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                 }
-                if (!mbar_wait(&s.afull[abuf], aphase) || !mbar_wait(&s.full[stage], phase)) {
+                if (!mbar_wait(&s.afull[abuf], aphase) || !mbar_wait(&s.xfull[stage], phase)) {
                     fail(s, err, kDetailMma | stage);
                     break;
                 }
@@ -396,12 +417,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mma_f16_tmem_a(d, a + 8 * j, bd, idesc, (!first || j != 0) ? 1u : 0u);
                 }
                 t5::commit(&s.aempty[abuf]);
-                t5::commit(&s.empty[stage]);
+                t5::commit(&s.xempty[stage]);
                 if (last) {
                     t5::commit(&s.dfull);
                     dphase ^= 1u;
                 }
-                if (++stage == STAGES) {
+                if (++stage == XST) {
                     stage = 0;
                     phase ^= 1u;
                 }
@@ -414,16 +435,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait(&s.drain, 0);
         }
     } else {
-        // ---------------- dequant + epilogue (warps 2 .. 2 + kDqWarps) ----------------
+        // ---------------- dequant + epilogue (warps 2 .. kXWarp - 1) ----------------
         const uint32_t q = warp & 3u;                  // lane quarter = W rows 32q .. 32q+31
         const uint32_t h = (warp - 2u) >> 2;           // which 64-element K slice of the stage
         const uint32_t row = 32 * q + lane;            // W row within the block
         uint32_t stage = 0, phase = 0, abuf = 0, aphase = 0, dphase = 0, sphase = 0;
         uint32_t seg_len = 0;
-        for (uint32_t u = u0; u < u1; ++u) {
-            const uint32_t nb = u / S, ks = u % S;
+        uint32_t nb = u0 / S, ks = u0 % S;  // (block, stage) of unit u, advanced incrementally
+        for (uint32_t u = u0; u < u1; ++u, ks = (ks + 1 == S) ? 0 : ks + 1, nb += (ks == 0)) {
             const bool last = (u + 1 == u1) || ks == S - 1;
-            bool ok = !aborted(s) && mbar_wait(&s.full[stage], phase);
+            bool ok = !aborted(s) && mbar_wait(&s.wfull[stage], phase);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
                 if (lane == 0 && !aborted(s)) fail(s, err, kDetailDq | stage);
@@ -441,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t sc = *reinterpret_cast<const uint32_t*>(
                 s.sf[stage] + h * 512 + (row & 31) * 16 + (row >> 5) * 4);
             __syncwarp();
-            if (lane == 0) ptxstd::mbar_arrive(&s.empty[stage]);
+            if (lane == 0) ptxstd::mbar_arrive(&s.wempty[stage]);
             // dequantise 64 elements into 32 f16x2 words (exact: e2m1 x e4m3 fits f16)
             uint32_t out[32];
 #pragma unroll
@@ -473,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 abuf = 0;
                 aphase ^= 1u;
             }
-            if (++stage == STAGES) {
+            if (++stage == WST) {
                 stage = 0;
                 phase ^= 1u;
             }

@@ -189,22 +189,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     t5::fence_after_thread_sync();
                     const uint64_t ad = t5::smem_desc_k128(ptxstd::smem_u32(s.a[stage]));
                     const uint64_t bd = t5::smem_desc_k128(ptxstd::smem_u32(s.b[stage]));
+                    // All scale copies of the stage first, then its MMAs, so that the copy
+                    // latency overlaps the earlier MMAs instead of stalling each one.
 #pragma unroll
                     for (uint32_t j = 0; j < kMmas; ++j) {
                         const uint32_t slot = tmem + kSfBase + (stage * kMmas + j) * kSfSlotCols;
-                        const uint32_t sfa_t = slot;
-                        const uint32_t sfb_t = slot + kSfaCols;
                         t5::cp_32x128b_warpx4(
-                            sfa_t, t5::smem_desc_nosw(ptxstd::smem_u32(s.sfa[stage] + 512 * j), 0, 128));
+                            slot, t5::smem_desc_nosw(ptxstd::smem_u32(s.sfa[stage] + 512 * j), 0, 128));
 #pragma unroll
                         for (uint32_t h = 0; h < BN / 128; ++h)
                             t5::cp_32x128b_warpx4(
-                                sfb_t + 4 * h,
+                                slot + kSfaCols + 4 * h,
                                 t5::smem_desc_nosw(
                                     ptxstd::smem_u32(s.sfb[stage] + h * (kMmas * 512) + 512 * j), 0,
                                     128));
-                        t5::mma_mxf4nvf4_block16(tmem, ad + 2 * j, bd + 2 * j, idesc, sfa_t, sfb_t,
-                                                 (kb | j) != 0u);
+                    }
+#pragma unroll
+                    for (uint32_t j = 0; j < kMmas; ++j) {
+                        const uint32_t slot = tmem + kSfBase + (stage * kMmas + j) * kSfSlotCols;
+                        t5::mma_mxf4nvf4_block16(tmem, ad + 2 * j, bd + 2 * j, idesc, slot,
+                                                 slot + kSfaCols, (kb | j) != 0u);
                     }
                     t5::commit(&s.empty[stage]);
                     if (++stage == STAGES) {
@@ -431,6 +435,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 t5::smem_desc_nosw(
                                     ptxstd::smem_u32(s.sfb[stage] + h * (kMmas * 512) + 512 * j), 0,
                                     128));
+                    }
+#pragma unroll
+                    for (uint32_t j = 0; j < kMmas; ++j) {
+                        const uint32_t slot = tmem + kSfBase + (stage * kMmas + j) * kPSlotCols;
                         t5::mma_mxf4nvf4_block16_pair(tmem, ad + 2 * j, bd + 2 * j, idesc, slot,
                                                       slot + 4, (kb | j) != 0u);
                     }
