@@ -22,15 +22,17 @@
 //   warp 0: weight producer: W tile 128 x 128 bytes + W scales 2 KiB per stage into an 8-stage
 //           ring that the dequant warps release as soon as they have read it (so the HBM stream
 //           never waits on MMA completion, nor on kernel 1);
-//   warp 18: x-image producer: the 8 KiB f16 B operand per stage into a 4-stage ring released by
+//   warp kXWarp: x-image producer: the 8 KiB f16 B operand per stage into a 4-stage ring released by
 //           the MMA commit (it waits for kernel 1 with griddepcontrol.wait);
 //   warp 1: TMEM owner + MMA issuer: 16 MMAs of M=128 (W rows), N=16 (tokens), K=16 per stage with
-//           the A operand in TMEM;
-//   warps 2..17: dequantise W rows into TMEM (tcgen05.st; four warps per lane quarter, 64 K each,
-//           three A buffers)
-//           and, at the end of each W-block segment, reduce the 128 x 16 fp32 partial into the
-//           scratch with red.global.add.v4.f32. A per-block counter of finished K stages elects the
-//           CTA that completes a block; it converts the block to bf16 and writes y (transposed).
+//           the A operand in TMEM, into one of two accumulators (one per W-block segment);
+//   warps 2 .. 2 + kDqWarps - 1: dequantise W rows into TMEM (tcgen05.st; kDqPerQ warps per lane
+//           quarter, each a kKPerWarp-element K slice of the stage; three A buffers);
+//   warps kEpiWarp .. kEpiWarp + 3 (one per lane quarter): at the end of each W-block segment,
+//           drain the accumulator and reduce the 128 x 16 fp32 partial into the scratch with
+//           red.global.add.v4.f32, off the dequant / MMA path (the MMA already fills the other
+//           accumulator). A per-block counter of finished K stages elects the CTA that completes a
+//           block; its epilogue warps convert the block to bf16 and write y (transposed).
 #include <mutex>
 
 #include "common.cuh"
@@ -53,17 +55,20 @@ constexpr uint32_t kXStageBytes = kTok * BKS * 2; // 8 KiB f16
 constexpr uint32_t kWRingBytes = kWStageBytes + kSfStageBytes;   // one weight stage
 constexpr uint32_t WST = 8;             // weight ring: released by the dequant warps after their loads
 constexpr uint32_t XST = 4;             // x-image ring: released by the MMA commit
-constexpr uint32_t kDqWarps = 16;                 // dequant / epilogue warps
-constexpr uint32_t kDqPerQ = kDqWarps / 4;        // per TMEM lane quarter
-constexpr uint32_t kKPerWarp = BKS / kDqPerQ;     // K elements of a row per warp and stage (64)
-constexpr uint32_t kTokPerWarp = kTok / kDqPerQ;  // tokens reduced per warp (4)
-constexpr uint32_t kXWarp = 2 + kDqWarps;          // x-image producer warp
-constexpr uint32_t kThreads = 32 * (kXWarp + 1);
+constexpr uint32_t kDqPerQ = 4;                    // dequant warps per TMEM lane quarter
+constexpr uint32_t kDqWarps = 4 * kDqPerQ;
+constexpr uint32_t kKPerWarp = BKS / kDqPerQ;      // K elements of a row per warp and stage
+constexpr uint32_t kChunks = kKPerWarp / 32;       // 16-byte W chunks of a row per warp and stage
+constexpr uint32_t kFirstDqWarp = 2;
+constexpr uint32_t kXWarp = kFirstDqWarp + kDqWarps;   // x-image producer warp
+constexpr uint32_t kEpiWarp = kXWarp + 1;              // first of the four epilogue warps
+constexpr uint32_t kThreads = 32 * (kEpiWarp + 4);
 constexpr uint32_t kACols = BKS / 2;    // f16 pairs per row per stage = 128 TMEM columns
 constexpr uint32_t kABufs = 3;          // A operand buffers in TMEM
+constexpr uint32_t kDBufs = 2;          // accumulators (one per W-block segment in flight)
 constexpr uint32_t kDCol = kABufs * kACols;  // accumulator columns after the A buffers
-static_assert(kDCol + kTok <= 512, "TMEM budget");
-static_assert(kKPerWarp == 64 && kTokPerWarp == 4, "dequant layout below assumes 4 warps per quarter");
+static_assert(kDCol + kDBufs * kTok <= 512, "TMEM budget");
+static_assert(kKPerWarp % 64 == 0 && kChunks % 2 == 0, "a warp's slice is whole 64-K scale words");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kPrepThreads = 256;
 
@@ -77,21 +82,20 @@ struct alignas(1024) Smem {
     uint64_t xempty[XST];
     uint64_t afull[kABufs];
     uint64_t aempty[kABufs];
-    uint64_t dfull;
-    uint64_t dempty;
+    uint64_t dfull[kDBufs];
+    uint64_t dempty[kDBufs];
     uint64_t segA;
     uint64_t segB;
     uint64_t drain;
     uint32_t tmem_base;
     uint32_t abort;
     uint32_t finalize;
-    float factor[kTok];
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 enum : uint32_t { kDetailProducer = 0x3100, kDetailMma = 0x3200, kDetailDq = 0x3300,
-                  kDetailXProducer = 0x3400 };
+                  kDetailXProducer = 0x3400, kDetailEpi = 0x3500 };
 
 // Workspace layout (bytes): y32 [N][16] f32 | counters [N/128] u32 (16 B aligned) |
 // x image [K/256][8 KiB] | factors [16] f32.
@@ -243,7 +247,7 @@ __device__ __forceinline__ void dequant8(uint32_t w, uint32_t scale2, uint32_t* 
 }
 
 // tcgen05.st.32x32b.x32: 32 consecutive columns of this warp's lane quarter.
-__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&v)[32]) {
+__device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t* v) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
         "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
@@ -310,9 +314,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptxstd::mbar_init(&s.afull[i], kDqWarps);
             ptxstd::mbar_init(&s.aempty[i], 1);
         }
-        ptxstd::mbar_init(&s.dfull, 1);
-        ptxstd::mbar_init(&s.dempty, kDqWarps);
-        ptxstd::mbar_init(&s.segA, kDqWarps);
+        for (uint32_t i = 0; i < kDBufs; ++i) {
+            ptxstd::mbar_init(&s.dfull[i], 1);
+            ptxstd::mbar_init(&s.dempty[i], 4);
+        }
+        ptxstd::mbar_init(&s.segA, 4);
         ptxstd::mbar_init(&s.segB, 1);
         ptxstd::mbar_init(&s.drain, 1);
         s.abort = 0;
@@ -391,18 +397,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ptxstd::elect_one()) {
             uint32_t idesc = 0;
             t5::idesc_dense(/*F16*/ 0, /*F16*/ 0, /*F32*/ 1, BM, kTok, idesc);
-            uint32_t stage = 0, phase = 0, abuf = 0, aphase = 0, dphase = 0;
-            const uint32_t d = tmem + kDCol;
-            for (uint32_t u = u0; u < u1 && !aborted(s); ++u) {
-                const uint32_t ks = u % S;
+            uint32_t stage = 0, phase = 0, abuf = 0, aphase = 0, dbuf = 0, dphase = 0;
+            uint32_t ks = u0 % S;
+            for (uint32_t u = u0; u < u1 && !aborted(s); ++u, ks = (ks + 1 == S) ? 0 : ks + 1) {
                 const bool first = (u == u0) || ks == 0;
                 const bool last = (u + 1 == u1) || ks == S - 1;
                 if (first) {
-                    if (!mbar_wait(&s.dempty, dphase ^ 1u)) {
+                    // the epilogue warps have drained this accumulator's previous segment
+                    if (!mbar_wait(&s.dempty[dbuf], dphase ^ 1u)) {
                         fail(s, err, kDetailMma | 0x30);
                         break;
                     }
                 }
+                const uint32_t d = tmem + kDCol + dbuf * kTok;
                 if (!mbar_wait(&s.afull[abuf], aphase) || !mbar_wait(&s.xfull[stage], phase)) {
                     fail(s, err, kDetailMma | stage);
                     break;
@@ -419,8 +426,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 t5::commit(&s.aempty[abuf]);
                 t5::commit(&s.xempty[stage]);
                 if (last) {
-                    t5::commit(&s.dfull);
-                    dphase ^= 1u;
+                    t5::commit(&s.dfull[dbuf]);
+                    if (++dbuf == kDBufs) {
+                        dbuf = 0;
+                        dphase ^= 1u;
+                    }
                 }
                 if (++stage == XST) {
                     stage = 0;
@@ -434,41 +444,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             t5::commit(&s.drain);
             mbar_wait(&s.drain, 0);
         }
-    } else {
-        // ---------------- dequant + epilogue (warps 2 .. kXWarp - 1) ----------------
-        const uint32_t q = warp & 3u;                  // lane quarter = W rows 32q .. 32q+31
-        const uint32_t h = (warp - 2u) >> 2;           // which 64-element K slice of the stage
-        const uint32_t row = 32 * q + lane;            // W row within the block
-        uint32_t stage = 0, phase = 0, abuf = 0, aphase = 0, dphase = 0, sphase = 0;
-        uint32_t seg_len = 0;
-        uint32_t nb = u0 / S, ks = u0 % S;  // (block, stage) of unit u, advanced incrementally
-        for (uint32_t u = u0; u < u1; ++u, ks = (ks + 1 == S) ? 0 : ks + 1, nb += (ks == 0)) {
-            const bool last = (u + 1 == u1) || ks == S - 1;
-            bool ok = !aborted(s) && mbar_wait(&s.wfull[stage], phase);
+    } else if (warp < kXWarp) {
+        // ---------------- dequant (warps kFirstDqWarp .. kXWarp - 1) ----------------
+        const uint32_t q = warp & 3u;                    // lane quarter = W rows 32q .. 32q+31
+        const uint32_t h = (warp - kFirstDqWarp) >> 2;   // K slice of the stage
+        const uint32_t row = 32 * q + lane;              // W row within the block
+        const uint32_t taddr = tmem + ((32 * q) << 16) + h * (kKPerWarp / 2);
+        uint32_t stage = 0, phase = 0, abuf = 0, aphase = 0;
+        for (uint32_t u = u0; u < u1; ++u) {
+            bool ok = mbar_wait(&s.wfull[stage], phase) && !aborted(s);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
                 if (lane == 0 && !aborted(s)) fail(s, err, kDetailDq | stage);
                 break;
             }
-            // packed W: 32 bytes of this row (2 swizzled 16-byte chunks); scales: one 4-byte
-            // word of the blocked tile that covers these 64 K elements
+            // packed W: kChunks swizzled 16-byte chunks of this row; scales: one 4-byte word of
+            // the blocked scale tile per 64 K elements
             const uint8_t* wrow = s.w[stage] + row * 128;
-            uint4 pk[2];
+            uint4 pk[kChunks];
+            uint32_t sc[kChunks / 2];
 #pragma unroll
-            for (uint32_t i = 0; i < 2; ++i) {
-                const uint32_t c = h * 2 + i;
+            for (uint32_t i = 0; i < kChunks; ++i) {
+                const uint32_t c = h * kChunks + i;
                 pk[i] = *reinterpret_cast<const uint4*>(wrow + ((c ^ (row & 7)) << 4));
             }
-            const uint32_t sc = *reinterpret_cast<const uint32_t*>(
-                s.sf[stage] + h * 512 + (row & 31) * 16 + (row >> 5) * 4);
+#pragma unroll
+            for (uint32_t i = 0; i < kChunks / 2; ++i)
+                sc[i] = *reinterpret_cast<const uint32_t*>(
+                    s.sf[stage] + (h * (kChunks / 2) + i) * 512 + (row & 31) * 16 + (row >> 5) * 4);
             __syncwarp();
             if (lane == 0) ptxstd::mbar_arrive(&s.wempty[stage]);
-            // dequantise 64 elements into 32 f16x2 words (exact: e2m1 x e4m3 fits f16)
-            uint32_t out[32];
+            // dequantise into f16x2 words (exact: e2m1 x e4m3 fits f16)
+            uint32_t out[kChunks * 16];
 #pragma unroll
-            for (uint32_t i = 0; i < 2; ++i) {
-                // chunk i covers K elements 32 i .. 32 i + 31 of this slice: scales 2i, 2i+1
-                const uint32_t sbytes = (sc >> (16 * i)) & 0xFFFFu;
+            for (uint32_t i = 0; i < kChunks; ++i) {
+                // chunk i covers 32 K elements: scale bytes 2 (i % 2) and 2 (i % 2) + 1 of word i / 2
+                const uint32_t sbytes = (sc[i / 2] >> (16 * (i % 2))) & 0xFFFFu;
                 uint32_t s2;
                 asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(s2) : "h"(static_cast<uint16_t>(sbytes)));
                 const uint32_t slo = __byte_perm(s2, 0, 0x1010);  // scale of the first 16
@@ -485,7 +496,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             t5::fence_after_thread_sync();
-            tmem_st_x32(tmem + ((32 * q) << 16) + abuf * kACols + h * (kKPerWarp / 2), out);
+#pragma unroll
+            for (uint32_t g = 0; g < kChunks / 2; ++g)
+                tmem_st_x32(taddr + abuf * kACols + 32 * g, out + 32 * g);
             tmem_wait_st();
             t5::fence_before_thread_sync();
             __syncwarp();
@@ -498,71 +511,92 @@ __global__ void __launch_bounds__(kThreads, 1)
                 stage = 0;
                 phase ^= 1u;
             }
-            ++seg_len;
-            if (!last) continue;
-
-            // ---- end of a W-block segment: reduce the 128 x 16 partial into y32 ----
-            bool okD = mbar_wait(&s.dfull, dphase);
-            okD = __all_sync(0xffffffffu, okD);
-            if (!okD) {
-                if (lane == 0) fail(s, err, kDetailDq | 0x50);
+        }
+    } else if (warp >= kEpiWarp) {
+        // ---------------- epilogue (warps kEpiWarp .. kEpiWarp + 3) ----------------
+        // decode_prep clears y32 and the counters and writes the token factors.
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        const uint32_t q = warp & 3u;
+        const uint32_t row = 32 * q + lane;                    // W row of the block (TMEM lane)
+        const uint32_t col = (warp - kEpiWarp) * 32 + lane;    // block column this thread writes
+        float fac[kTok];
+#pragma unroll
+        for (uint32_t t = 0; t < kTok; ++t) fac[t] = __ldcg(wsp.factors + t) * gw;
+        uint32_t dbuf = 0, dphase = 0, sphase = 0;
+        for (uint32_t u = u0; u < u1;) {
+            // one W-block segment: units u .. end - 1 of block nb
+            const uint32_t nb = u / S;
+            const uint32_t end = min(u1, (nb + 1) * S);
+            const uint32_t seg_len = end - u;
+            u = end;
+            bool ok = mbar_wait(&s.dfull[dbuf], dphase);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                if (lane == 0) fail(s, err, kDetailEpi | 0x10);
                 break;
             }
-            dphase ^= 1u;
             t5::fence_after_thread_sync();
-            uint32_t acc[16];
-            t5::ld_32x32b_x16(tmem + ((32 * q) << 16) + kDCol, acc);
+            uint32_t acc[kTok];
+            t5::ld_32x32b_x16(tmem + ((32 * q) << 16) + kDCol + dbuf * kTok, acc);
             t5::wait_ld();
             t5::fence_before_thread_sync();
             __syncwarp();
-            if (lane == 0) ptxstd::mbar_arrive(&s.dempty);
-            // this warp reduces tokens 4h .. 4h+3 of its row
-            float* dst = wsp.y32 + (static_cast<size_t>(nb) * BM + row) * kTok + kTokPerWarp * h;
-            const float* fac = wsp.factors + kTokPerWarp * h;
-            float v[4];
+            if (lane == 0) ptxstd::mbar_arrive(&s.dempty[dbuf]);
+            if (++dbuf == kDBufs) {
+                dbuf = 0;
+                dphase ^= 1u;
+            }
+            // this row's 16 token partials
+            float* dst = wsp.y32 + (static_cast<size_t>(nb) * BM + row) * kTok;
 #pragma unroll
-            for (uint32_t t = 0; t < 4; ++t) {
-                const uint32_t a = h == 0 ? acc[t] : h == 1 ? acc[4 + t] : h == 2 ? acc[8 + t] : acc[12 + t];
-                v[t] = __uint_as_float(a) * (__ldcg(fac + t) * gw);
-            }
-            red_add_v4(dst, v[0], v[1], v[2], v[3]);
+            for (uint32_t t = 0; t < kTok; t += 4)
+                red_add_v4(dst + t, __uint_as_float(acc[t]) * fac[t],
+                           __uint_as_float(acc[t + 1]) * fac[t + 1],
+                           __uint_as_float(acc[t + 2]) * fac[t + 2],
+                           __uint_as_float(acc[t + 3]) * fac[t + 3]);
             __threadfence();
-            // All warps have reduced (segA, one arrive per warp), then warp 2 publishes the
-            // finished stages and tells the others whether this CTA completes the block (segB).
-            // mbarriers rather than bar.sync so that every wait stays bounded.
             __syncwarp();
+            // All four warps have reduced (segA), then the first publishes the finished stages
+            // and tells the others whether this CTA completes the block (segB). mbarriers rather
+            // than bar.sync so that every wait stays bounded.
             if (lane == 0) ptxstd::mbar_arrive(&s.segA);
-            bool okS = mbar_wait(&s.segA, sphase);
-            okS = __all_sync(0xffffffffu, okS);
-            if (!okS) {
-                if (lane == 0) fail(s, err, kDetailDq | 0x60);
-                break;
+            if (warp == kEpiWarp) {
+                bool okA = mbar_wait(&s.segA, sphase);
+                okA = __all_sync(0xffffffffu, okA);
+                if (!okA) {
+                    if (lane == 0) fail(s, err, kDetailEpi | 0x20);
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t before = atomicAdd(wsp.counters + nb, seg_len);
+                    *reinterpret_cast<volatile uint32_t*>(&s.finalize) =
+                        (before + seg_len == S) ? 1u : 0u;
+                    ptxstd::mbar_arrive(&s.segB);
+                }
             }
-            if (warp == 2 && lane == 0) {
-                const uint32_t before = atomicAdd(wsp.counters + nb, seg_len);
-                *reinterpret_cast<volatile uint32_t*>(&s.finalize) =
-                    (before + seg_len == S) ? 1u : 0u;
-                ptxstd::mbar_arrive(&s.segB);
-            }
-            okS = mbar_wait(&s.segB, sphase);
-            okS = __all_sync(0xffffffffu, okS);
-            if (!okS) {
-                if (lane == 0) fail(s, err, kDetailDq | 0x70);
+            bool okB = mbar_wait(&s.segB, sphase);
+            okB = __all_sync(0xffffffffu, okB);
+            if (!okB) {
+                if (lane == 0) fail(s, err, kDetailEpi | 0x30);
                 break;
             }
             sphase ^= 1u;
-            seg_len = 0;
             if (*reinterpret_cast<volatile uint32_t*>(&s.finalize)) {
                 __threadfence();
-                // 512 threads: token t = tid / 32, four consecutive columns (tid % 32) * 4
-                const uint32_t tid = (warp - 2) * 32 + lane;
-                const uint32_t t = tid / 32, c0 = (tid % 32) * 4;
-                if (t < M) {
-                    const float* src = wsp.y32 + (static_cast<size_t>(nb) * BM + c0) * kTok + t;
-                    const uint32_t o0 = dt::bf16x2_from_f32(__ldcg(src), __ldcg(src + kTok));
-                    const uint32_t o1 = dt::bf16x2_from_f32(__ldcg(src + 2 * kTok), __ldcg(src + 3 * kTok));
-                    *reinterpret_cast<uint2*>(y + static_cast<size_t>(t) * N + nb * BM + c0) =
-                        make_uint2(o0, o1);
+                // column `col` of the block: its 16 token sums -> y[t][nb * BM + col]
+                const float4* src = reinterpret_cast<const float4*>(
+                    wsp.y32 + (static_cast<size_t>(nb) * BM + col) * kTok);
+                uint16_t* yc = y + static_cast<size_t>(nb) * BM + col;
+#pragma unroll
+                for (uint32_t i = 0; i < kTok / 4; ++i) {
+                    const float4 f = __ldcg(src + i);
+                    const uint32_t p0 = dt::bf16x2_from_f32(f.x, f.y);
+                    const uint32_t p1 = dt::bf16x2_from_f32(f.z, f.w);
+                    const uint16_t o[4] = {static_cast<uint16_t>(p0), static_cast<uint16_t>(p0 >> 16),
+                                           static_cast<uint16_t>(p1), static_cast<uint16_t>(p1 >> 16)};
+#pragma unroll
+                    for (uint32_t k = 0; k < 4; ++k)
+                        if (4 * i + k < M) yc[static_cast<size_t>(4 * i + k) * N] = o[k];
                 }
             }
         }
