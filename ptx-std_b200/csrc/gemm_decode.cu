@@ -27,7 +27,8 @@
 //   warp 1: TMEM owner + MMA issuer: 16 MMAs of M=128 (W rows), N=16 (tokens), K=16 per stage with
 //           the A operand in TMEM, into one of two accumulators (one per W-block segment);
 //   warps 2 .. 2 + kDqWarps - 1: dequantise W rows into TMEM (tcgen05.st; kDqPerQ warps per lane
-//           quarter, each a kKPerWarp-element K slice of the stage; three A buffers);
+//           quarter in kTeams teams that take the units in turn, each warp a 64 * kSubs-element
+//           K slice of its team's units; three A buffers);
 //   warps kEpiWarp .. kEpiWarp + 3 (one per lane quarter): at the end of each W-block segment,
 //           drain the accumulator and reduce the 128 x 16 fp32 partial into the scratch with
 //           red.global.add.v4.f32, off the dequant / MMA path (the MMA already fills the other
@@ -57,8 +58,14 @@ constexpr uint32_t WST = 8;             // weight ring: released by the dequant 
 constexpr uint32_t XST = 4;             // x-image ring: released by the MMA commit
 constexpr uint32_t kDqPerQ = 4;                    // dequant warps per TMEM lane quarter
 constexpr uint32_t kDqWarps = 4 * kDqPerQ;
-constexpr uint32_t kKPerWarp = BKS / kDqPerQ;      // K elements of a row per warp and stage
-constexpr uint32_t kChunks = kKPerWarp / 32;       // 16-byte W chunks of a row per warp and stage
+// The dequant warps form kTeams teams that take the units in turn (team t: the CTA's units
+// t, t + kTeams, ...), so each warp has kTeams units' time for the latency of one unit (shared
+// memory loads, the TMEM store and its wait, the barrier hand-offs).
+constexpr uint32_t kTeams = 2;
+constexpr uint32_t kTeamWarpsPerQ = kDqPerQ / kTeams;   // warps of a team per lane quarter
+constexpr uint32_t kTeamWarps = 4 * kTeamWarpsPerQ;     // arrivals per unit on wempty / afull
+constexpr uint32_t kSubs = 4 / kTeamWarpsPerQ;          // 64-K slices of a row per warp and unit
+static_assert(kDqPerQ % kTeams == 0 && 4 % kTeamWarpsPerQ == 0, "team layout");
 constexpr uint32_t kFirstDqWarp = 2;
 constexpr uint32_t kXWarp = kFirstDqWarp + kDqWarps;   // x-image producer warp
 constexpr uint32_t kEpiWarp = kXWarp + 1;              // first of the four epilogue warps
@@ -68,7 +75,12 @@ constexpr uint32_t kABufs = 3;          // A operand buffers in TMEM
 constexpr uint32_t kDBufs = 2;          // accumulators (one per W-block segment in flight)
 constexpr uint32_t kDCol = kABufs * kACols;  // accumulator columns after the A buffers
 static_assert(kDCol + kDBufs * kTok <= 512, "TMEM budget");
-static_assert(kKPerWarp % 64 == 0 && kChunks % 2 == 0, "a warp's slice is whole 64-K scale words");
+// Parity waits only tell a phase from the one before it. A team at unit i has already waited on
+// its unit i - kTeams, so (a) with kTeams <= kABufs the MMA has finished unit i - 2 kABufs when
+// the team waits for buffer i % kABufs to be freed from unit i - kABufs, and (b) with
+// WST % kTeams == 0 the team itself consumed unit i - WST of stage i % WST. Either way no wait is
+// ever two phases ahead of its barrier.
+static_assert(kTeams <= kABufs && WST % kTeams == 0, "team count vs. A buffers and weight ring");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kPrepThreads = 256;
 
@@ -304,14 +316,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptxstd::prefetch_tensormap(&tmW);
         for (uint32_t i = 0; i < WST; ++i) {
             ptxstd::mbar_init(&s.wfull[i], 1);
-            ptxstd::mbar_init(&s.wempty[i], kDqWarps);
+            ptxstd::mbar_init(&s.wempty[i], kTeamWarps);
         }
         for (uint32_t i = 0; i < XST; ++i) {
             ptxstd::mbar_init(&s.xfull[i], 1);
             ptxstd::mbar_init(&s.xempty[i], 1);
         }
         for (uint32_t i = 0; i < kABufs; ++i) {
-            ptxstd::mbar_init(&s.afull[i], kDqWarps);
+            ptxstd::mbar_init(&s.afull[i], kTeamWarps);
             ptxstd::mbar_init(&s.aempty[i], 1);
         }
         for (uint32_t i = 0; i < kDBufs; ++i) {
@@ -446,49 +458,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp < kXWarp) {
         // ---------------- dequant (warps kFirstDqWarp .. kXWarp - 1) ----------------
-        const uint32_t q = warp & 3u;                    // lane quarter = W rows 32q .. 32q+31
-        const uint32_t h = (warp - kFirstDqWarp) >> 2;   // K slice of the stage
-        const uint32_t row = 32 * q + lane;              // W row within the block
-        const uint32_t taddr = tmem + ((32 * q) << 16) + h * (kKPerWarp / 2);
-        uint32_t stage = 0, phase = 0, abuf = 0, aphase = 0;
-        for (uint32_t u = u0; u < u1; ++u) {
+        const uint32_t q = warp & 3u;                        // lane quarter = W rows 32q .. 32q+31
+        const uint32_t h = (warp - kFirstDqWarp) >> 2;       // 0 .. kDqPerQ - 1
+        const uint32_t team = h % kTeams;
+        const uint32_t slice0 = (h / kTeams) * kSubs;        // first 64-K slice of this warp
+        const uint32_t row = 32 * q + lane;                  // W row within the block
+        const uint32_t taddr = tmem + ((32 * q) << 16) + slice0 * 32;
+        const uint32_t n_units = u1 - u0;
+        for (uint32_t i = team; i < n_units; i += kTeams) {
+            // i-th unit of this CTA: weight stage i % WST, A buffer i % kABufs
+            const uint32_t stage = i % WST, phase = (i / WST) & 1u;
+            const uint32_t abuf = i % kABufs, aphase = (i / kABufs) & 1u;
             bool ok = mbar_wait(&s.wfull[stage], phase) && !aborted(s);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
                 if (lane == 0 && !aborted(s)) fail(s, err, kDetailDq | stage);
                 break;
             }
-            // packed W: kChunks swizzled 16-byte chunks of this row; scales: one 4-byte word of
-            // the blocked scale tile per 64 K elements
+            // packed W: two swizzled 16-byte chunks of this row per 64-K slice; scales: one
+            // 4-byte word of the blocked scale tile per slice
             const uint8_t* wrow = s.w[stage] + row * 128;
-            uint4 pk[kChunks];
-            uint32_t sc[kChunks / 2];
+            uint4 pk[2 * kSubs];
+            uint32_t sc[kSubs];
 #pragma unroll
-            for (uint32_t i = 0; i < kChunks; ++i) {
-                const uint32_t c = h * kChunks + i;
-                pk[i] = *reinterpret_cast<const uint4*>(wrow + ((c ^ (row & 7)) << 4));
+            for (uint32_t j = 0; j < kSubs; ++j) {
+#pragma unroll
+                for (uint32_t c2 = 0; c2 < 2; ++c2) {
+                    const uint32_t c = 2 * (slice0 + j) + c2;
+                    pk[2 * j + c2] = *reinterpret_cast<const uint4*>(wrow + ((c ^ (row & 7)) << 4));
+                }
+                sc[j] = *reinterpret_cast<const uint32_t*>(
+                    s.sf[stage] + (slice0 + j) * 512 + (row & 31) * 16 + (row >> 5) * 4);
             }
-#pragma unroll
-            for (uint32_t i = 0; i < kChunks / 2; ++i)
-                sc[i] = *reinterpret_cast<const uint32_t*>(
-                    s.sf[stage] + (h * (kChunks / 2) + i) * 512 + (row & 31) * 16 + (row >> 5) * 4);
             __syncwarp();
             if (lane == 0) ptxstd::mbar_arrive(&s.wempty[stage]);
-            // dequantise into f16x2 words (exact: e2m1 x e4m3 fits f16)
-            uint32_t out[kChunks * 16];
-#pragma unroll
-            for (uint32_t i = 0; i < kChunks; ++i) {
-                // chunk i covers 32 K elements: scale bytes 2 (i % 2) and 2 (i % 2) + 1 of word i / 2
-                const uint32_t sbytes = (sc[i / 2] >> (16 * (i % 2))) & 0xFFFFu;
-                uint32_t s2;
-                asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(s2) : "h"(static_cast<uint16_t>(sbytes)));
-                const uint32_t slo = __byte_perm(s2, 0, 0x1010);  // scale of the first 16
-                const uint32_t shi = __byte_perm(s2, 0, 0x3232);  // scale of the next 16
-                const uint32_t wv[4] = {pk[i].x, pk[i].y, pk[i].z, pk[i].w};
-#pragma unroll
-                for (uint32_t j = 0; j < 4; ++j)
-                    dequant8(wv[j], j < 2 ? slo : shi, &out[i * 16 + j * 4]);
-            }
             bool okA = mbar_wait(&s.aempty[abuf], aphase ^ 1u);
             okA = __all_sync(0xffffffffu, okA);
             if (!okA) {
@@ -497,20 +500,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             t5::fence_after_thread_sync();
 #pragma unroll
-            for (uint32_t g = 0; g < kChunks / 2; ++g)
-                tmem_st_x32(taddr + abuf * kACols + 32 * g, out + 32 * g);
+            for (uint32_t j = 0; j < kSubs; ++j) {
+                // dequantise 64 elements into 32 f16x2 words (exact: e2m1 x e4m3 fits f16)
+                uint32_t out[32];
+#pragma unroll
+                for (uint32_t c2 = 0; c2 < 2; ++c2) {
+                    // chunk c2 covers 32 K elements: scale bytes 2 c2 and 2 c2 + 1 of the word
+                    const uint32_t sbytes = (sc[j] >> (16 * c2)) & 0xFFFFu;
+                    uint32_t s2;
+                    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(s2) : "h"(static_cast<uint16_t>(sbytes)));
+                    const uint32_t slo = __byte_perm(s2, 0, 0x1010);  // scale of the first 16
+                    const uint32_t shi = __byte_perm(s2, 0, 0x3232);  // scale of the next 16
+                    const uint4 v = pk[2 * j + c2];
+                    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (uint32_t k = 0; k < 4; ++k)
+                        dequant8(wv[k], k < 2 ? slo : shi, &out[c2 * 16 + k * 4]);
+                }
+                tmem_st_x32(taddr + abuf * kACols + 32 * j, out);
+            }
             tmem_wait_st();
             t5::fence_before_thread_sync();
             __syncwarp();
             if (lane == 0) ptxstd::mbar_arrive(&s.afull[abuf]);
-            if (++abuf == kABufs) {
-                abuf = 0;
-                aphase ^= 1u;
-            }
-            if (++stage == WST) {
-                stage = 0;
-                phase ^= 1u;
-            }
         }
     } else if (warp >= kEpiWarp) {
         // ---------------- epilogue (warps kEpiWarp .. kEpiWarp + 3) ----------------
