@@ -203,7 +203,7 @@ class MxFp8Quantize:
     unit = "GB/s"
     dtype = "bf16->e4m3+ue8m0"
     rows = cols = 8192
-    kernel = "quantize_mxfp8_kernel"
+    kernel = "quantize_kernel<Mxfp8>"
 
     def __init__(self, world: int = 1):
         self.in_bytes = self.rows * self.cols * 2
@@ -275,7 +275,7 @@ class Fp8Gemm:
     unit = "TFLOP/s"
     dtype = "e4m3 x e4m3 -> f32 acc -> bf16"
     M = N = K = 8192
-    kernel = "gemm_fp8_kernel"
+    kernel = "gemm_fp8_pair_kernel"
     bound = "tensor"
     peak_ratio_to_bf16 = 2.0
     peak_note = "dense FP8 = 2x bf16"
@@ -327,7 +327,7 @@ class Fp8Gemm:
 
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
-        A, B = self.host_input()
+        A, B = self.host_input()[:2]
         rows = 256
         if getattr(self, "_dec", None) is None:
             self._dec = (O.decode(0, A[:rows].ravel()).reshape(rows, self.K),
@@ -339,6 +339,55 @@ class Fp8Gemm:
         return 2 * rows * self.N * self.K / el / 1e12, "256x8192x8192 row block, f32 blocked GEMM"
 
 
+class Mxfp8Gemm(Fp8Gemm):
+    """MXFP8 (OCP MX) A [8192, 8192] x B [8192, 8192]: E4M3 with UE8M0 scales per 32 K elements
+    in the blocked layout the quantiser writes -> bf16 C."""
+
+    name = "mxfp8_gemm"
+    dtype = "e4m3 x e4m3 (ue8m0/32 scales) -> f32 acc -> bf16"
+    kernel = "gemm_mxfp8_pair_kernel"
+    peak_note = "dense MXFP8 = 2x bf16"
+
+    def __init__(self, world: int = 1):
+        super().__init__(world)
+        self.in_bytes += (self.M + self.N) * self.K // 32
+        self.bytes = self.in_bytes + self.out_bytes
+        self.config = {"workload": "mxfp8_gemm e4m3+ue8m0/32 8192x8192x8192 -> bf16",
+                       "M": self.M, "N": self.N, "K": self.K,
+                       "l2": "operands 132 MiB + output 128 MiB per step (> L2)"}
+
+    def host_input(self):
+        if getattr(self, "_abs", None) is None:
+            import numpy as np
+            a, b = super().host_input()
+            rng = np.random.default_rng(33)
+            # scales 2^-5 .. 2^5, as bytes in the blocked layout (any byte order is a valid input)
+            self._abs = (a, b, rng.integers(122, 133, self.M * self.K // 32, dtype=np.uint8),
+                         rng.integers(122, 133, self.N * self.K // 32, dtype=np.uint8))
+        return self._abs
+
+    def setup(self, torch, abs_):
+        super().setup(torch, abs_[:2])
+        self.sfa_host = torch.from_numpy(abs_[2]).pin_memory()
+        self.sfb_host = torch.from_numpy(abs_[3]).pin_memory()
+        self.sfa = self.sfa_host.cuda()
+        self.sfb = self.sfb_host.cuda()
+
+    def step(self, i):
+        import ptxstd
+        ptxstd.gemm_mxfp8(self.a, self.sfa, self.b, self.sfb, out=self.c)
+        return 1
+
+    def e2e_step(self, i):
+        import ptxstd
+        for dst, src in ((self.a, self.a_host), (self.b, self.b_host), (self.sfa, self.sfa_host),
+                         (self.sfb, self.sfb_host)):
+            dst.copy_(src, non_blocking=True)
+        ptxstd.gemm_mxfp8(self.a, self.sfa, self.b, self.sfb, out=self.c)
+        self.c_host.copy_(self.c, non_blocking=True)
+        return 1
+
+
 class Nvfp4Gemm:
     """NVFP4 MLP up-projection: A [8192, 8192] x B [28672, 8192] (E2M1 + E4M3/16 + f32 global)
     -> bf16 [8192, 28672]; B is sharded along N across ranks (no communication)."""
@@ -347,7 +396,7 @@ class Nvfp4Gemm:
     unit = "TFLOP/s"
     dtype = "e2m1 x e2m1 (e4m3/16 scales) -> f32 acc -> bf16"
     M, N, K = 8192, 28672, 8192
-    kernel = "gemm_nvfp4_kernel"
+    kernel = "gemm_nvfp4_pair_kernel"
     bound = "tensor"
     peak_ratio_to_bf16 = 4.0
     peak_note = "dense NVFP4 = 4x bf16"
@@ -520,7 +569,7 @@ class DecodeGemm:
 
 
 WORKLOADS = {"mxfp8_quantize": MxFp8Quantize, "fp8_gemm": Fp8Gemm, "nvfp4_gemm": Nvfp4Gemm,
-             "decode_gemm": DecodeGemm}
+             "decode_gemm": DecodeGemm, "mxfp8_gemm": Mxfp8Gemm}
 
 
 # ---- arms -----------------------------------------------------------------------------------

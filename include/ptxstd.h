@@ -128,6 +128,16 @@ PTXSTD_API int ptxstd_gemm_nvfp4(const uint8_t* d_a, const uint8_t* d_sfa, float
                                  const uint8_t* d_b, const uint8_t* d_sfb, float gb,
                                  uint16_t* d_c, int64_t M, int64_t N, int64_t K,
                                  ptxstd_stream stream);
+/* MXFP8 GEMM (OCP MX): C[M,N] bf16 = sum_k (A[m,k] 2^(sfA[m,k/32]-127)) (B[n,k] 2^(sfB[n,k/32]-127)).
+ * A [M,K], B [N,K]: E4M3, K contiguous. sfA, sfB: UE8M0 scales per 32 K elements in the blocked
+ * layout of ptxstd_quantize_mxfp8_layout(sf_layout = 1), so quantised activations feed it as they
+ * are. tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale.block32 (mma_block_scaled with
+ * MmaKind::Mxf8f6f4 and ScaleVectorSize::Block32, src/tcgen05/mma.rs:58-97, :698-724;
+ * InstrDescriptor::<Mxf8f6f4>::new and its scale ids, src/tcgen05/descriptor.rs:601-611).
+ * M % 256 == 0, N % 256 == 0, K % 128 == 0. */
+PTXSTD_API int ptxstd_gemm_mxfp8(const uint8_t* d_a, const uint8_t* d_sfa, const uint8_t* d_b,
+                                 const uint8_t* d_sfb, uint16_t* d_c, int64_t M, int64_t N,
+                                 int64_t K, ptxstd_stream stream);
 
 /* Decode-shape GEMM: y[M,N] bf16 = MXFP8(x)[M,K] * NVFP4(W)[N,K]^T * gw, M <= 16 tokens.
  * x: bf16 [M,K] row-major, quantised inside the call with the recipe of ptxstd_quantize_mxfp8

@@ -559,6 +559,40 @@ void ptxo_gemm_nvfp4_ref(const uint8_t* A, const uint8_t* sfA, float ga, const u
     parallel_for((uint64_t)n_samples, threads, nvfp4_samples, &c);
 }
 
+/* MXFP8 element: E4M3 code times its UE8M0 block scale (OCP MX; f8e8m0 decode 2^(b-127),
+ * src/data_types/float8.rs:148-152; f8e4m3 decode, vector.rs:61-95). */
+static inline double mxfp8_elem(const uint8_t* q, const uint8_t* sf, int64_t k, const double* lut) {
+    return lut[q[k]] * (double)ptxo_ue8m0_to_f32(sf[k >> 5]);
+}
+
+static void mxfp8_samples(void* p, uint64_t lo, uint64_t hi) {
+    gemm_ctx* c = (gemm_ctx*)p;
+    double lut[256];
+    for (int i = 0; i < 256; ++i) lut[i] = ptxo_e4m3_to_f32((uint8_t)i);
+    for (uint64_t s = lo; s < hi; ++s) {
+        const uint8_t* a = c->A + c->rows[s] * c->K;
+        const uint8_t* sa = c->sfA + c->rows[s] * (c->K / 32);
+        const uint8_t* b = c->B + c->cols[s] * c->K;
+        const uint8_t* sb = c->sfB + c->cols[s] * (c->K / 32);
+        double acc = 0, mag = 0;
+        for (int64_t k = 0; k < c->K; ++k) {
+            double t = mxfp8_elem(a, sa, k, lut) * mxfp8_elem(b, sb, k, lut);
+            acc += t; mag += fabs(t);
+        }
+        c->ref[s] = acc; c->mag[s] = mag;
+    }
+}
+
+void ptxo_gemm_mxfp8_ref(const uint8_t* A, const uint8_t* sfA, const uint8_t* B,
+                         const uint8_t* sfB, int64_t M, int64_t N, int64_t K,
+                         const int64_t* rows, const int64_t* cols, int64_t n_samples, double* ref,
+                         double* mag, int threads) {
+    gemm_ctx c; memset(&c, 0, sizeof c);
+    c.A = A; c.sfA = sfA; c.B = B; c.sfB = sfB;
+    c.M = M; c.N = N; c.K = K; c.rows = rows; c.cols = cols; c.ref = ref; c.mag = mag;
+    parallel_for((uint64_t)n_samples, threads, mxfp8_samples, &c);
+}
+
 static void decode_samples(void* p, uint64_t lo, uint64_t hi) {
     gemm_ctx* c = (gemm_ctx*)p;
     int64_t K = c->K;

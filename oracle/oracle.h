@@ -115,6 +115,12 @@ void ptxo_gemm_nvfp4_ref(const uint8_t* A, const uint8_t* sfA, float ga, const u
                          const uint8_t* sfB, float gb, int64_t M, int64_t N, int64_t K,
                          const int64_t* rows, const int64_t* cols, int64_t n_samples, double* ref,
                          double* mag, int threads);
+/* MXFP8 (OCP MX): A [M,K], B [N,K] E4M3 (K contiguous), sfA [M,K/32], sfB [N,K/32] UE8M0
+ * (row-major); C[i,j] = sum_k A[i,k] 2^(sfA-127) * B[j,k] 2^(sfB-127). */
+void ptxo_gemm_mxfp8_ref(const uint8_t* A, const uint8_t* sfA, const uint8_t* B,
+                         const uint8_t* sfB, int64_t M, int64_t N, int64_t K,
+                         const int64_t* rows, const int64_t* cols, int64_t n_samples, double* ref,
+                         double* mag, int threads);
 /* Decode: x bf16 [M,K] is MXFP8-quantised (32-blocks) by the recipe above, W NVFP4 [N,K/2] with
  * sfW [N,K/16] and gw; C[i,j] = sum_k xq[i,k] 2^(sx-127) * w[j,k] sfW gw. */
 void ptxo_gemm_decode_ref(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float gw,

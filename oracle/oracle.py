@@ -73,6 +73,7 @@ def _declare(L: C.CDLL) -> None:
         "ptxo_gemm_nvfp4_ref": (None, [p, p, f32, p, p, f32, i64, i64, i64, p, p, i64, p, p,
                                        i32]),
         "ptxo_gemm_decode_ref": (None, [p, p, p, f32, i64, i64, i64, p, p, i64, p, p, i32]),
+        "ptxo_gemm_mxfp8_ref": (None, [p, p, p, p, i64, i64, i64, p, p, i64, p, p, i32]),
         "ptxo_sgemm_nt": (None, [p, p, p, i64, i64, i64, i32]),
         "ptxo_idesc_f16": (i32, [i32, i32, i32, u32, u32, C.POINTER(u32)]),
         "ptxo_idesc_tf32": (i32, [u32, u32, C.POINTER(u32)]),
@@ -171,6 +172,16 @@ def gemm_nvfp4_ref(A, sfA, ga, B, sfB, gb, rows, cols, threads=0):
     r, c, ref, mag = _samples(rows, cols)
     lib().ptxo_gemm_nvfp4_ref(_ptr(A), _ptr(sfA), ga, _ptr(B), _ptr(sfB), gb, M, N, K, _ptr(r),
                               _ptr(c), r.size, _ptr(ref), _ptr(mag), threads)
+    return ref, mag
+
+
+def gemm_mxfp8_ref(A, sfA, B, sfB, rows, cols, threads=0):
+    """MXFP8 GEMM reference at sampled outputs; scales row-major [rows, K/32]."""
+    A, sfA, B, sfB = (np.ascontiguousarray(t, dtype=np.uint8) for t in (A, sfA, B, sfB))
+    (M, K), N = A.shape, B.shape[0]
+    r, c, ref, mag = _samples(rows, cols)
+    lib().ptxo_gemm_mxfp8_ref(_ptr(A), _ptr(sfA), _ptr(B), _ptr(sfB), M, N, K, _ptr(r), _ptr(c),
+                              r.size, _ptr(ref), _ptr(mag), threads)
     return ref, mag
 
 

@@ -60,6 +60,8 @@ _SIGS = {
     "ptxstd_gemm_nvfp4": (C.c_int, [C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p,
                                     C.c_float, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
                                     C.c_void_p]),
+    "ptxstd_gemm_mxfp8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.c_int64, C.c_int64, C.c_int64, C.c_void_p]),
     "ptxstd_gemm_decode_workspace_bytes": (C.c_size_t, [C.c_int64, C.c_int64, C.c_int64]),
     "ptxstd_gemm_decode": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p,
                                      C.c_int64, C.c_int64, C.c_int64, C.c_void_p, C.c_size_t,
@@ -146,9 +148,9 @@ def last_device_error(clear: bool = True, stream=None) -> tuple[int, int]:
 
 
 from . import data_types, tcgen05  # noqa: E402
-from .kernels import (gemm_decode, gemm_fp8, gemm_nvfp4, quantize_mxfp8,  # noqa: E402
-                      quantize_nvfp4)
+from .kernels import (gemm_decode, gemm_fp8, gemm_mxfp8, gemm_nvfp4,  # noqa: E402
+                      quantize_mxfp8, quantize_nvfp4)
 
 __all__ = ["lib", "check", "PtxStdError", "status_string", "last_device_error", "data_types",
-           "tcgen05", "quantize_mxfp8", "quantize_nvfp4", "gemm_fp8", "gemm_nvfp4",
-           "gemm_decode"]
+           "tcgen05", "quantize_mxfp8", "quantize_nvfp4", "gemm_fp8", "gemm_mxfp8",
+           "gemm_nvfp4", "gemm_decode"]

@@ -41,6 +41,21 @@ def gemm_fp8(a, b, sa: float = 1.0, sb: float = 1.0, out=None, stream=None):
     return c
 
 
+def gemm_mxfp8(a, sfa, b, sfb, out=None, stream=None):
+    """MXFP8 a [M, K], b [N, K] (uint8, E4M3) with blocked UE8M0 scales per 32 -> bf16 [M, N]."""
+    torch = _torch()
+    M, K = a.shape
+    N = b.shape[0]
+    if b.shape[1] != K:
+        raise ValueError("K mismatch")
+    if sfa.numel() != M * K // 32 or sfb.numel() != N * K // 32:
+        raise ValueError("scale tensors must hold one UE8M0 per 32 elements")
+    c = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    check(lib().ptxstd_gemm_mxfp8(_dev(a), _dev(sfa), _dev(b), _dev(sfb), _dev(c), M, N, K,
+                                  _stream(stream)), "gemm_mxfp8")
+    return c
+
+
 def gemm_nvfp4(a, sfa, ga: float, b, sfb, gb: float, out=None, stream=None):
     """NVFP4 a [M, K/2], b [N, K/2] (uint8, E2M1x2) with blocked E4M3 scales -> bf16 [M, N]."""
     torch = _torch()

@@ -250,6 +250,26 @@ def test_gemm_refs_small(oracle):
     assert np.allclose(mag, (np.abs(da) @ np.abs(db).T).ravel(), rtol=1e-12)
 
 
+def test_gemm_mxfp8_ref_small(oracle):
+    """MXFP8 reference = E4M3 decode x 2^(UE8M0 - 127) per 32-element block, summed in f64."""
+    rng = np.random.default_rng(6)
+    M, N, K = 5, 7, 128
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(0, 256, (N, K), dtype=np.uint8)
+    A[(A & 0x7F) == 0x7F] = 0  # no NaNs
+    B[(B & 0x7F) == 0x7F] = 0
+    sfA = rng.integers(100, 160, (M, K // 32), dtype=np.uint8)
+    sfB = rng.integers(100, 160, (N, K // 32), dtype=np.uint8)
+    rows, cols = np.meshgrid(np.arange(M), np.arange(N), indexing="ij")
+    ref, mag = oracle.gemm_mxfp8_ref(A, sfA, B, sfB, rows.ravel(), cols.ravel())
+    da = oracle.decode(0, A.ravel()).reshape(M, K).astype(np.float64)
+    db = oracle.decode(0, B.ravel()).reshape(N, K).astype(np.float64)
+    da *= np.exp2(np.repeat(sfA.astype(np.float64) - 127, 32, axis=1))
+    db *= np.exp2(np.repeat(sfB.astype(np.float64) - 127, 32, axis=1))
+    assert np.allclose(ref, (da @ db.T).ravel(), rtol=1e-12, atol=0)
+    assert np.allclose(mag, (np.abs(da) @ np.abs(db).T).ravel(), rtol=1e-12)
+
+
 DIGESTS = os.path.join(GOLDEN, "cvt_sweep_digests.json")
 
 
