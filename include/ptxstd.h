@@ -78,9 +78,22 @@ PTXSTD_API int ptxstd_cvt_e5m2_to_f32(const uint8_t* d_codes, float* d_out, size
 PTXSTD_API int ptxstd_cvt_e2m1x2_to_f32(const uint8_t* d_codes, float* d_out, size_t n_bytes,
                              ptxstd_stream stream);
 PTXSTD_API int ptxstd_cvt_ue8m0_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
+/* Vector<f6e2m3, N> / Vector<f6e3m2, N>::from_f32::<RELU> (src/data_types/float6.rs, narrow_cvt!
+ * core from_f32 = cvt.rn.satfinite{.relu}.{e2m3,e3m2}x2.f32): RN, .satfinite, one value in the
+ * low 6 bits of each output byte. E2M3: bias 1, max 7.5; E3M2: bias 3, max 28; no infinities or
+ * NaNs (a NaN input becomes the code the hardware writes, pinned by the sweep). n any size. */
+PTXSTD_API int ptxstd_cvt_f32_to_e2m3(const float* d_x, uint8_t* d_out, size_t n, int relu,
+                           ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_f32_to_e3m2(const float* d_x, uint8_t* d_out, size_t n, int relu,
+                           ptxstd_stream stream);
+/* FP6 to_f32: exact, via cvt.rn.f16x2.{e2m3,e3m2}x2 (float6.rs core to_f16x2). Only the low 6 bits
+ * of each code byte are significant (float6.rs:1-8: the two top bits must be zero). */
+PTXSTD_API int ptxstd_cvt_e2m3_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_e3m2_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
 /* Exhaustive-sweep helper: encodes the n f32 bit patterns base, base+1, ... (no input array) with
  * one of the variants 0 e4m3, 1 e5m2, 2 e2m1 (one nibble per byte), 3-5 the same with .relu,
- * 6 ue8m0 RZ satfinite, 7 ue8m0 RP satfinite. base + n <= 2^32. */
+ * 6 ue8m0 RZ satfinite, 7 ue8m0 RP satfinite, 8 e2m3, 9 e3m2, 10-11 the same with .relu.
+ * base + n <= 2^32. */
 PTXSTD_API int ptxstd_cvt_sweep(int variant, uint64_t base, uint64_t n, uint8_t* d_out,
                      ptxstd_stream stream);
 

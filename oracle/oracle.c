@@ -90,6 +90,10 @@ float ptxo_e4m3_to_f32(uint8_t b) { return ptxo_minifloat_to_f32(b, 4, 3, 7, 2);
 float ptxo_e5m2_to_f32(uint8_t b) { return ptxo_minifloat_to_f32(b, 5, 2, 15, 1); }
 /* f4e2m1 decode: minifloat_to_f32(bits, 2, 1, 1, None) (src/data_types/float4.rs:24). */
 float ptxo_e2m1_to_f32(uint8_t b) { return ptxo_minifloat_to_f32(b & 0xF, 2, 1, 1, 0); }
+/* FP6 (src/data_types/float6.rs: f6e2m3 decode minifloat_to_f32(bits, 2, 3, 1, Specials::None),
+ * f6e3m2 decode (bits, 3, 2, 3, Specials::None)); the value is in the low 6 bits. */
+float ptxo_e2m3_to_f32(uint8_t b) { return ptxo_minifloat_to_f32(b & 0x3F, 2, 3, 1, 0); }
+float ptxo_e3m2_to_f32(uint8_t b) { return ptxo_minifloat_to_f32(b & 0x3F, 3, 2, 3, 0); }
 
 /* f8e8m0 decode (src/data_types/float8.rs:148-152): 0xff NaN, 0 -> 2^-127, else bits << 23. */
 float ptxo_ue8m0_to_f32(uint8_t b) {
@@ -107,6 +111,8 @@ float ptxo_to_f32_via_half(int format, uint8_t bits) {
     switch (format) {
     case PTXO_E4M3: v = ptxo_e4m3_to_f32(bits); break;
     case PTXO_E5M2: v = ptxo_e5m2_to_f32(bits); break;
+    case PTXO_E2M3: v = ptxo_e2m3_to_f32(bits); break;
+    case PTXO_E3M2: v = ptxo_e3m2_to_f32(bits); break;
     default: v = ptxo_e2m1_to_f32(bits); break;
     }
     if (v != v) return u2f(0x7FFFFFFFu);
@@ -138,9 +144,19 @@ static const narrow_fmt FMT_E5M2 = {5, 2, 15, 0x7B, 0x7F, 0x80};
 /* E2M1: max 0x7 = 6 (src/data_types/float4.rs:35-36); no NaN, so NaN becomes +max
  * (src/data_types/narrow.rs:125-130). */
 static const narrow_fmt FMT_E2M1 = {2, 1, 1, 0x7, 0x7, 0x8};
+/* E2M3: max 0x1F = 7.5, E3M2: max 0x1F = 28 (src/data_types/float6.rs consts MAX); sign bit 0x20;
+ * no NaN, so, as for E2M1, NaN becomes +max. */
+static const narrow_fmt FMT_E2M3 = {2, 3, 1, 0x1F, 0x1F, 0x20};
+static const narrow_fmt FMT_E3M2 = {3, 2, 3, 0x1F, 0x1F, 0x20};
 
 static inline const narrow_fmt* fmt_of(int format) {
-    return format == PTXO_E4M3 ? &FMT_E4M3 : format == PTXO_E5M2 ? &FMT_E5M2 : &FMT_E2M1;
+    switch (format) {
+    case PTXO_E4M3: return &FMT_E4M3;
+    case PTXO_E5M2: return &FMT_E5M2;
+    case PTXO_E2M3: return &FMT_E2M3;
+    case PTXO_E3M2: return &FMT_E3M2;
+    default: return &FMT_E2M1;
+    }
 }
 
 /* Round-to-nearest-even of a finite, non-negative f32 (given as bits) to the magnitude code of
@@ -294,7 +310,11 @@ uint8_t ptxo_encode_variant(int variant, float x) {
     case PTXO_V_E5M2_RELU: return encode_narrow(&FMT_E5M2, x, 1);
     case PTXO_V_E2M1_RELU: return encode_narrow(&FMT_E2M1, x, 1);
     case PTXO_V_UE8M0_RZ: return ptxo_f32_to_ue8m0(x, 0, 1);
-    default: return ptxo_f32_to_ue8m0(x, 1, 1);
+    case PTXO_V_UE8M0_RP: return ptxo_f32_to_ue8m0(x, 1, 1);
+    case PTXO_V_E2M3: return encode_narrow(&FMT_E2M3, x, 0);
+    case PTXO_V_E3M2: return encode_narrow(&FMT_E3M2, x, 0);
+    case PTXO_V_E2M3_RELU: return encode_narrow(&FMT_E2M3, x, 1);
+    default: return encode_narrow(&FMT_E3M2, x, 1);
     }
 }
 

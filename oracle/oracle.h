@@ -31,6 +31,8 @@ enum ptxo_format {
     PTXO_E4M3 = 0, /* FP8 E4M3, NaN-only specials, max 448 (src/data_types/float8.rs:13-42) */
     PTXO_E5M2 = 1, /* FP8 E5M2, IEEE specials, max 57344 (src/data_types/float8.rs:70-133) */
     PTXO_E2M1 = 2, /* FP4 E2M1, no specials, max 6 (src/data_types/float4.rs:14-43) */
+    PTXO_E2M3 = 3, /* FP6 E2M3, no specials, max 7.5, one value per byte (src/data_types/float6.rs) */
+    PTXO_E3M2 = 4, /* FP6 E3M2, no specials, max 28, one value per byte (src/data_types/float6.rs) */
 };
 
 /* Exact soft decode (src/data_types/vector.rs:61-95). specials: 0 none, 1 IEEE, 2 NaN-only. */
@@ -39,6 +41,8 @@ float ptxo_minifloat_to_f32(uint8_t bits, uint32_t exp_bits, uint32_t man_bits, 
 float ptxo_e4m3_to_f32(uint8_t bits);
 float ptxo_e5m2_to_f32(uint8_t bits);
 float ptxo_e2m1_to_f32(uint8_t nibble);
+float ptxo_e2m3_to_f32(uint8_t bits);
+float ptxo_e3m2_to_f32(uint8_t bits);
 /* UE8M0 decode, 2^(b-127), 0xff NaN (src/data_types/float8.rs:148-152). */
 float ptxo_ue8m0_to_f32(uint8_t bits);
 
@@ -77,6 +81,7 @@ enum ptxo_variant {
     PTXO_V_E4M3 = 0, PTXO_V_E5M2 = 1, PTXO_V_E2M1 = 2,
     PTXO_V_E4M3_RELU = 3, PTXO_V_E5M2_RELU = 4, PTXO_V_E2M1_RELU = 5,
     PTXO_V_UE8M0_RZ = 6, PTXO_V_UE8M0_RP = 7,
+    PTXO_V_E2M3 = 8, PTXO_V_E3M2 = 9, PTXO_V_E2M3_RELU = 10, PTXO_V_E3M2_RELU = 11,
 };
 uint8_t ptxo_encode_variant(int variant, float x);
 uint64_t ptxo_sweep_compare(int variant, uint64_t base, uint64_t n, const uint8_t* device_out,

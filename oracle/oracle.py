@@ -16,11 +16,11 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 
-E4M3, E5M2, E2M1 = 0, 1, 2
+E4M3, E5M2, E2M1, E2M3, E3M2 = 0, 1, 2, 3, 4
 (V_E4M3, V_E5M2, V_E2M1, V_E4M3_RELU, V_E5M2_RELU, V_E2M1_RELU, V_UE8M0_RZ,
  V_UE8M0_RP) = range(8)
 VARIANT_NAMES = ["e4m3", "e5m2", "e2m1", "e4m3_relu", "e5m2_relu", "e2m1_relu", "ue8m0_rz",
-                 "ue8m0_rp"]
+                 "ue8m0_rp", "e2m3", "e3m2", "e2m3_relu", "e3m2_relu"]
 
 _lib = None
 

@@ -8,9 +8,19 @@ namespace dt = ptxstd::data_types;
 
 namespace {
 
-enum Op : int { kE4M3 = 0, kE5M2 = 1, kE2M1 = 2 };
+enum Op : int { kE4M3 = 0, kE5M2 = 1, kE2M1 = 2, kE2M3 = 3, kE3M2 = 4 };
 
-// f32 -> FP8, 4 elements per thread per step (one 16-byte load, one 4-byte store).
+// One f32 pair -> two one-byte codes (x0 in the low byte) for the byte-per-element formats.
+template <int OP, bool RELU>
+__device__ __forceinline__ uint32_t encode_pair(float x0, float x1) {
+    if constexpr (OP == kE4M3) return dt::e4m3x2_from_f32<RELU>(x0, x1);
+    else if constexpr (OP == kE5M2) return dt::e5m2x2_from_f32<RELU>(x0, x1);
+    else if constexpr (OP == kE2M3) return dt::e2m3x2_from_f32<RELU>(x0, x1);
+    else return dt::e3m2x2_from_f32<RELU>(x0, x1);
+}
+
+// f32 -> FP8 or FP6 (one code per byte), 4 elements per thread per step (one 16-byte load, one
+// 4-byte store).
 template <int OP, bool RELU>
 __global__ void __launch_bounds__(256) encode_fp8_kernel(const float* __restrict__ x,
                                                          uint8_t* __restrict__ out, size_t n) {
@@ -19,22 +29,14 @@ __global__ void __launch_bounds__(256) encode_fp8_kernel(const float* __restrict
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
          i += stride) {
         const float4 v = reinterpret_cast<const float4*>(x)[i];
-        uint32_t lo, hi;
-        if constexpr (OP == kE4M3) {
-            lo = dt::e4m3x2_from_f32<RELU>(v.x, v.y);
-            hi = dt::e4m3x2_from_f32<RELU>(v.z, v.w);
-        } else {
-            lo = dt::e5m2x2_from_f32<RELU>(v.x, v.y);
-            hi = dt::e5m2x2_from_f32<RELU>(v.z, v.w);
-        }
+        const uint32_t lo = encode_pair<OP, RELU>(v.x, v.y);
+        const uint32_t hi = encode_pair<OP, RELU>(v.z, v.w);
         reinterpret_cast<uint32_t*>(out)[i] = lo | (hi << 16);
     }
     // Tail: the scalar form is the pair instruction with a zero lane (narrow.rs:243-247).
     const size_t t = n4 * 4 + static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (t < n) {
-        uint32_t c = (OP == kE4M3) ? dt::e4m3x2_from_f32<RELU>(x[t], 0.0f)
-                                   : dt::e5m2x2_from_f32<RELU>(x[t], 0.0f);
-        out[t] = static_cast<uint8_t>(c & 0xFFu);
+        out[t] = static_cast<uint8_t>(encode_pair<OP, RELU>(x[t], 0.0f) & 0xFFu);
     }
 }
 
@@ -69,7 +71,8 @@ __global__ void __launch_bounds__(256) encode_ue8m0_kernel(const float* __restri
     }
 }
 
-// codes -> f32. Formats: 0 e4m3, 1 e5m2, 2 e2m1x2 (two values per byte), 3 ue8m0.
+// codes -> f32. Formats: 0 e4m3, 1 e5m2, 2 e2m1x2 (two values per byte), 3 ue8m0, 4 e2m3,
+// 5 e3m2 (one FP6 value in the low 6 bits of each byte).
 template <int FMT>
 __global__ void __launch_bounds__(256) decode_kernel(const uint8_t* __restrict__ c,
                                                      float* __restrict__ out, size_t n) {
@@ -85,6 +88,10 @@ __global__ void __launch_bounds__(256) decode_kernel(const uint8_t* __restrict__
             const float2 v = dt::e2m1x2_to_f32(b);
             out[2 * i] = v.x;
             out[2 * i + 1] = v.y;
+        } else if constexpr (FMT == 4) {
+            out[i] = dt::e2m3x2_to_f32(static_cast<uint16_t>(b)).x;
+        } else if constexpr (FMT == 5) {
+            out[i] = dt::e3m2x2_to_f32(static_cast<uint16_t>(b)).x;
         } else {
             // Scalar ue8m0 to_f32: the pair with ONE (0x7f) in the other lane (narrow.rs:676-679).
             out[i] = dt::ue8m0x2_to_f32(static_cast<uint16_t>(b | 0x7F00u)).x;
@@ -110,7 +117,11 @@ __global__ void __launch_bounds__(256) sweep_kernel(int v, uint64_t base, uint64
             case 4: c = dt::e5m2x2_from_f32<true>(f, 0.0f) & 0xFFu; break;
             case 5: c = dt::e2m1x2_from_f32<true>(f, 0.0f) & 0xFu; break;
             case 6: c = dt::ue8m0_from_f32<false, true>(f); break;
-            default: c = dt::ue8m0_from_f32<true, true>(f); break;
+            case 7: c = dt::ue8m0_from_f32<true, true>(f); break;
+            case 8: c = dt::e2m3x2_from_f32<false>(f, 0.0f) & 0xFFu; break;
+            case 9: c = dt::e3m2x2_from_f32<false>(f, 0.0f) & 0xFFu; break;
+            case 10: c = dt::e2m3x2_from_f32<true>(f, 0.0f) & 0xFFu; break;
+            default: c = dt::e3m2x2_from_f32<true>(f, 0.0f) & 0xFFu; break;
             }
             codes |= c << (8 * j);
         }
@@ -192,6 +203,48 @@ int ptxstd_cvt_f32_to_ue8m0(const float* d_x, uint8_t* d_out, size_t n, int roun
     });
 }
 
+int ptxstd_cvt_f32_to_e2m3(const float* d_x, uint8_t* d_out, size_t n, int relu,
+                           ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_x || !d_out || !ptxstd::aligned16(d_x) || (reinterpret_cast<uintptr_t>(d_out) & 3))
+        return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int g = grid_for(n / 4 + 1);
+    return launch([&] {
+        if (relu) encode_fp8_kernel<kE2M3, true><<<g, 256, 0, s>>>(d_x, d_out, n);
+        else encode_fp8_kernel<kE2M3, false><<<g, 256, 0, s>>>(d_x, d_out, n);
+    });
+}
+
+int ptxstd_cvt_f32_to_e3m2(const float* d_x, uint8_t* d_out, size_t n, int relu,
+                           ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_x || !d_out || !ptxstd::aligned16(d_x) || (reinterpret_cast<uintptr_t>(d_out) & 3))
+        return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int g = grid_for(n / 4 + 1);
+    return launch([&] {
+        if (relu) encode_fp8_kernel<kE3M2, true><<<g, 256, 0, s>>>(d_x, d_out, n);
+        else encode_fp8_kernel<kE3M2, false><<<g, 256, 0, s>>>(d_x, d_out, n);
+    });
+}
+
+int ptxstd_cvt_e2m3_to_f32(const uint8_t* d_codes, float* d_out, size_t n,
+                           ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_codes || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    return launch([&] { decode_kernel<4><<<grid_for(n), 256, 0, s>>>(d_codes, d_out, n); });
+}
+
+int ptxstd_cvt_e3m2_to_f32(const uint8_t* d_codes, float* d_out, size_t n,
+                           ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_codes || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    return launch([&] { decode_kernel<5><<<grid_for(n), 256, 0, s>>>(d_codes, d_out, n); });
+}
+
 int ptxstd_cvt_e4m3_to_f32(const uint8_t* d_codes, float* d_out, size_t n,
                            ptxstd_stream stream) {
     if (n == 0) return PTXSTD_OK;
@@ -228,7 +281,7 @@ int ptxstd_cvt_ue8m0_to_f32(const uint8_t* d_codes, float* d_out, size_t n,
 int ptxstd_cvt_sweep(int variant, uint64_t base, uint64_t n, uint8_t* d_out,
                      ptxstd_stream stream) {
     if (n == 0) return PTXSTD_OK;
-    if (!d_out || variant < 0 || variant > 7 || base + n > (1ull << 32) ||
+    if (!d_out || variant < 0 || variant > 11 || base + n > (1ull << 32) ||
         (reinterpret_cast<uintptr_t>(d_out) & 3))
         return PTXSTD_EINVAL;
     auto s = static_cast<cudaStream_t>(stream);

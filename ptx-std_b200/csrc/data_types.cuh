@@ -32,6 +32,27 @@ __device__ __forceinline__ uint16_t e5m2x2_from_f32(float x0, float x1) {
         asm("cvt.rn.satfinite.e5m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
     return r;
 }
+// f6e2m3x2 / f6e3m2x2::pair_from_f32 (src/data_types/float6.rs, narrow_cvt! core from_f32):
+// cvt.rn.satfinite{.relu}.e2m3x2.f32 / .e3m2x2.f32, one value in the low 6 bits of each byte,
+// x0 in the low byte.
+template <bool RELU = false>
+__device__ __forceinline__ uint16_t e2m3x2_from_f32(float x0, float x1) {
+    uint16_t r;
+    if constexpr (RELU)
+        asm("cvt.rn.satfinite.relu.e2m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    else
+        asm("cvt.rn.satfinite.e2m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    return r;
+}
+template <bool RELU = false>
+__device__ __forceinline__ uint16_t e3m2x2_from_f32(float x0, float x1) {
+    uint16_t r;
+    if constexpr (RELU)
+        asm("cvt.rn.satfinite.relu.e3m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    else
+        asm("cvt.rn.satfinite.e3m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(x1), "f"(x0));
+    return r;
+}
 // f4e2m1x2::pair_from_f32: cvt.rn.satfinite{.relu}.e2m1x2.f32 (one byte, x0 in the low nibble).
 template <bool RELU = false>
 __device__ __forceinline__ uint32_t e2m1x2_from_f32(float x0, float x1) {
@@ -94,6 +115,17 @@ __device__ __forceinline__ float2 e2m1x2_to_f32(uint32_t byte) {
     asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
         : "=r"(h2)
         : "r"(byte));
+    return half2_bits_to_float2(h2);
+}
+// FP6 to_f32 = to_f16 (cvt.rn.f16x2.e2m3x2 / .e3m2x2, exact) then widening.
+__device__ __forceinline__ float2 e2m3x2_to_f32(uint16_t codes) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e2m3x2 %0, %1;" : "=r"(h2) : "h"(codes));
+    return half2_bits_to_float2(h2);
+}
+__device__ __forceinline__ float2 e3m2x2_to_f32(uint16_t codes) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e3m2x2 %0, %1;" : "=r"(h2) : "h"(codes));
     return half2_bits_to_float2(h2);
 }
 // ue8m0 to_f32 = to_bf16 then widening (narrow.rs:683-690): cvt.rn.bf16x2.ue8m0x2.

@@ -46,6 +46,12 @@ _SIGS = {
     "ptxstd_cvt_e5m2_to_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "ptxstd_cvt_e2m1x2_to_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "ptxstd_cvt_ue8m0_to_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ptxstd_cvt_f32_to_e2m3": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
+                                         C.c_void_p]),
+    "ptxstd_cvt_f32_to_e3m2": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
+                                         C.c_void_p]),
+    "ptxstd_cvt_e2m3_to_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ptxstd_cvt_e3m2_to_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "ptxstd_cvt_sweep": (C.c_int, [C.c_int, C.c_uint64, C.c_uint64, C.c_void_p, C.c_void_p]),
     "ptxstd_quantize_mxfp8": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p,
                                         C.c_void_p, C.c_void_p]),

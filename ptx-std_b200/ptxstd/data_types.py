@@ -4,7 +4,8 @@ Each function mirrors a reference conversion applied element-wise, computed by l
 kernels with the same `cvt` instructions the reference's pair methods wrap:
 
 - ``from_f32(fmt, x, relu)``: Vector<fmt, N>::from_f32::<RELU> (src/data_types/narrow.rs:354-361),
-  RN .satfinite; one code per byte for FP8, two per byte (element 0 low nibble) for E2M1.
+  RN .satfinite; one code per byte for FP8 and FP6 (src/data_types/float6.rs: the value in the
+  low 6 bits), two per byte (element 0 low nibble) for E2M1.
 - ``to_f32(fmt, codes)``: exact decode through f16 (narrow.rs:292-299).
 - ``ue8m0_from_f32(x, round_up, satfinite)``: f8e8m0::from_f32::<RND, OVERFLOW>
   (narrow.rs:600-617); ``ue8m0_to_f32``: through bf16 (narrow.rs:683-690).
@@ -14,12 +15,14 @@ from __future__ import annotations
 
 from . import _dev, _stream, _torch, check, lib
 
-E4M3, E5M2, E2M1 = "e4m3", "e5m2", "e2m1"
+E4M3, E5M2, E2M1, E2M3, E3M2 = "e4m3", "e5m2", "e2m1", "e2m3", "e3m2"
 
 _ENC = {E4M3: "ptxstd_cvt_f32_to_e4m3", E5M2: "ptxstd_cvt_f32_to_e5m2",
-        E2M1: "ptxstd_cvt_f32_to_e2m1x2"}
+        E2M1: "ptxstd_cvt_f32_to_e2m1x2", E2M3: "ptxstd_cvt_f32_to_e2m3",
+        E3M2: "ptxstd_cvt_f32_to_e3m2"}
 _DEC = {E4M3: "ptxstd_cvt_e4m3_to_f32", E5M2: "ptxstd_cvt_e5m2_to_f32",
-        E2M1: "ptxstd_cvt_e2m1x2_to_f32"}
+        E2M1: "ptxstd_cvt_e2m1x2_to_f32", E2M3: "ptxstd_cvt_e2m3_to_f32",
+        E3M2: "ptxstd_cvt_e3m2_to_f32"}
 
 
 def from_f32(fmt: str, x, relu: bool = False, stream=None):

@@ -100,7 +100,8 @@ def _doc_value(doc: str) -> str:
 
 def extract_constants(ref: str) -> dict:
     out = {}
-    for fname, fmts in (("float8.rs", ("f8e4m3", "f8e5m2", "f8e8m0")), ("float4.rs", ("f4e2m1",))):
+    for fname, fmts in (("float8.rs", ("f8e4m3", "f8e5m2", "f8e8m0")), ("float4.rs", ("f4e2m1",)),
+                        ("float6.rs", ("f6e2m3", "f6e3m2"))):
         path = os.path.join(ref, "src", "data_types", fname)
         lines = open(path).read().split("\n")
         cur, doc = None, None

@@ -1,9 +1,10 @@
 """Device conversions vs the oracle, bit-exact (B200).
 
 - every code of every format decoded on the device equals the oracle's decode (bits, NaN too);
-- the narrow-float round-trip set (2^24 seeded values with specials) encoded to E4M3, E5M2 and
-  E2M1x2 (RN .satfinite, with and without .relu) and decoded back matches the oracle bit for bit;
-- all 2^32 f32 bit patterns, through the device's `cvt` for the eight encode variants, match the
+- the narrow-float round-trip set (2^24 seeded values with specials) encoded to E4M3, E5M2,
+  E2M1x2, E2M3 and E3M2 (RN .satfinite, with and without .relu) and decoded back matches the
+  oracle bit for bit;
+- all 2^32 f32 bit patterns, through the device's `cvt` for the twelve encode variants, match the
   oracle (the exhaustive pin of the oracle against the instructions the reference wraps).
 """
 
@@ -29,6 +30,12 @@ def test_decode_every_code(cuda, oracle):
     got = _to_np(dt.to_f32(dt.E2M1, codes)).view(np.uint32)
     want = oracle.decode(2, np.arange(256, dtype=np.uint8)).view(np.uint32)
     assert np.array_equal(got, want)
+    # FP6: the value lives in the low 6 bits (src/data_types/float6.rs:1-8)
+    for fmt, fid in ((dt.E2M3, 3), (dt.E3M2, 4)):
+        got = _to_np(dt.to_f32(fmt, codes[:64])).view(np.uint32)
+        want = np.array([oracle.lib().ptxo_to_f32_via_half(fid, c) for c in range(64)],
+                        dtype=np.float32).view(np.uint32)
+        assert np.array_equal(got, want), (fmt, np.nonzero(got != want)[0][:8])
     # ue8m0 widens through bf16 with a bit shift (bf16::to_f32, src/data_types/bfloat16.rs:84-86)
     got = _to_np(dt.ue8m0_to_f32(codes)).view(np.uint32)
     want = np.array([oracle.lib().ptxo_ue8m0_to_f32_via_bf16(c) for c in range(256)],
@@ -43,7 +50,7 @@ def test_roundtrip_set(cuda, oracle, relu):
     torch = cuda
     x = workloads.conversion_inputs(1 << 24)
     xd = torch.from_numpy(x).cuda()
-    for fmt, fid in ((dt.E4M3, 0), (dt.E5M2, 1), (dt.E2M1, 2)):
+    for fmt, fid in ((dt.E4M3, 0), (dt.E5M2, 1), (dt.E2M1, 2), (dt.E2M3, 3), (dt.E3M2, 4)):
         codes = dt.from_f32(fmt, xd, relu=relu)
         want = oracle.encode(fid, x, relu=relu)
         got = _to_np(codes)
@@ -74,14 +81,14 @@ def test_ue8m0_set(cuda, oracle):
 
 
 def test_exhaustive_all_f32(cuda, oracle):
-    """All 2^32 inputs, 8 variants, in 2^28 chunks: zero mismatches."""
+    """All 2^32 inputs, 12 variants, in 2^28 chunks: zero mismatches."""
     import ptxstd.data_types as dt
     torch = cuda
     chunk = 1 << 28
     dev = torch.empty(chunk, dtype=torch.uint8, device="cuda")
     host = torch.empty(chunk, dtype=torch.uint8, pin_memory=True)
     total_bad = {}
-    for v in range(8):
+    for v in range(len(oracle.VARIANT_NAMES)):
         bad = 0
         report = []
         for base in range(0, 1 << 32, chunk):
