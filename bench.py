@@ -568,8 +568,51 @@ class DecodeGemm:
         return wbytes / el / 1e9, "16x8192x8192 block, f32 blocked GEMM on decoded weights"
 
 
+class MxFp8QuantizeSR(MxFp8Quantize):
+    """The same MXFP8 quantise with stochastic rounding of the elements (cvt.rs, random bits from
+    SplitMix64 of a per-step seed, generated on the device)."""
+
+    name = "mxfp8_quantize_sr"
+    kernel = "quantize_kernel<Mxfp8Rs>"
+
+    def __init__(self, world: int = 1):
+        super().__init__(world)
+        self.config = dict(self.config, workload="mxfp8_quantize_sr bf16 8192x8192 -> e4m3 "
+                           "(stochastic rounding) + ue8m0/32", rounding="cvt.rs, SplitMix64 bits")
+
+    def step(self, i):
+        import ptxstd
+        x, q, sf = self.sets[i % 2]
+        ptxstd.quantize_mxfp8(x, out=(q, sf), seed=0x5EED + i)
+        return 1
+
+    def e2e_step(self, i):
+        import ptxstd
+        x, q, sf = self.sets[i % 2]
+        x.copy_(self.x_host, non_blocking=True)
+        ptxstd.quantize_mxfp8(x, out=(q, sf), seed=0x5EED + i)
+        self.q_host.copy_(q, non_blocking=True)
+        self.sf_host.copy_(sf, non_blocking=True)
+        return 1
+
+    def cpu_sample(self, threads: int, budget_s: float):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        x = self.host_input()
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            O.quantize_mxfp8_rs(x, 0x5EED + reps, threads)
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= budget_s or reps >= 20:
+                break
+        return self.bytes * reps / el / 1e9, f"{reps} x full 8192x8192 stochastic quantise"
+
+
 WORKLOADS = {"mxfp8_quantize": MxFp8Quantize, "fp8_gemm": Fp8Gemm, "nvfp4_gemm": Nvfp4Gemm,
-             "decode_gemm": DecodeGemm, "mxfp8_gemm": Mxfp8Gemm}
+             "decode_gemm": DecodeGemm, "mxfp8_gemm": Mxfp8Gemm,
+             "mxfp8_quantize_sr": MxFp8QuantizeSR}
 
 
 # ---- arms -----------------------------------------------------------------------------------

@@ -90,10 +90,44 @@ PTXSTD_API int ptxstd_cvt_f32_to_e3m2(const float* d_x, uint8_t* d_out, size_t n
  * of each code byte are significant (float6.rs:1-8: the two top bits must be zero). */
 PTXSTD_API int ptxstd_cvt_e2m3_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
 PTXSTD_API int ptxstd_cvt_e3m2_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
+/* Stochastic rounding: Vector<E, N>::from_f32_stochastic::<RELU> (src/data_types/narrow.rs:494-505;
+ * core quad_from_f32_stochastic = cvt.rs.satfinite{.relu}.<fmt>x4.f32, :217-229). Elements
+ * 4g .. 4g+3 are converted together with the random bits d_rbits[g] (ceil(n/4) words); a last
+ * group of fewer than four is padded with zeros whose results are dropped (:483-486). Each value
+ * is rounded toward zero unless the discarded mantissa bits plus its random bits carry. Which
+ * rbits bits serve which element: FP8/FP6 "the lower 16 bits for elements 0 and 1, the upper 16
+ * for elements 2 and 3" (src/data_types/float8.rs:59, float6.rs:61); E2M1 "the lower 8 bits of
+ * both 16-bit halves for elements 0 and 1, the upper 8 bits of both halves for elements 2 and 3"
+ * (float4.rs:60). Needs sm_100a. E2M1 output is packed two per byte (n even). d_x 16-byte
+ * aligned; d_rbits 4-byte aligned. */
+PTXSTD_API int ptxstd_cvt_f32_to_e4m3_rs(const float* d_x, const uint32_t* d_rbits, uint8_t* d_out,
+                              size_t n, int relu, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_f32_to_e5m2_rs(const float* d_x, const uint32_t* d_rbits, uint8_t* d_out,
+                              size_t n, int relu, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_f32_to_e2m3_rs(const float* d_x, const uint32_t* d_rbits, uint8_t* d_out,
+                              size_t n, int relu, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_f32_to_e3m2_rs(const float* d_x, const uint32_t* d_rbits, uint8_t* d_out,
+                              size_t n, int relu, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_f32_to_e2m1x2_rs(const float* d_x, const uint32_t* d_rbits, uint8_t* d_out,
+                                size_t n, int relu, ptxstd_stream stream);
+/* bf16xN / f16xN::from_f32_stochastic::<R, O> (src/data_types/bfloat16.rs:572-598,
+ * src/data_types/float16.rs:740-766; cvt.rs{.relu}{.satfinite}.{bf16x2,f16x2}.f32): elements 2p,
+ * 2p+1 with d_rbits[p] (ceil(n/2) words), the lower 16 bits for the even element (bf16: all 16;
+ * f16: the 13 least significant), the upper for the odd one. satfinite = 0 lets overflow become
+ * infinity. d_x 8-byte aligned; d_out 4-byte aligned. */
+PTXSTD_API int ptxstd_cvt_f32_to_bf16_rs(const float* d_x, const uint32_t* d_rbits, uint16_t* d_out,
+                              size_t n, int relu, int satfinite, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_f32_to_f16_rs(const float* d_x, const uint32_t* d_rbits, uint16_t* d_out,
+                             size_t n, int relu, int satfinite, ptxstd_stream stream);
 /* Exhaustive-sweep helper: encodes the n f32 bit patterns base, base+1, ... (no input array) with
  * one of the variants 0 e4m3, 1 e5m2, 2 e2m1 (one nibble per byte), 3-5 the same with .relu,
- * 6 ue8m0 RZ satfinite, 7 ue8m0 RP satfinite, 8 e2m3, 9 e3m2, 10-11 the same with .relu.
- * base + n <= 2^32. */
+ * 6 ue8m0 RZ satfinite, 7 ue8m0 RP satfinite, 8 e2m3, 9 e3m2, 10-11 the same with .relu;
+ * stochastic rounding: 12 e4m3, 13 e5m2, 14 e2m3, 15 e3m2, 16 e2m1 (nibble per byte), 17-21 the
+ * same with .relu, then two bytes per input: 22 bf16, 23 .relu, 24 .satfinite, 25 both, 26-29
+ * the same for f16. Pattern p of a stochastic variant takes the random bits of group p / 4
+ * (p / 2 for bf16/f16): word (group % 2) of SplitMix64 output group / 2 from the seed
+ * 0x2545F4914F6CDD1D (the generator of ptxstd_quantize_mxfp8_rs). base + n <= 2^32; base % 4 == 0
+ * for the stochastic variants. */
 PTXSTD_API int ptxstd_cvt_sweep(int variant, uint64_t base, uint64_t n, uint8_t* d_out,
                      ptxstd_stream stream);
 
@@ -121,6 +155,17 @@ PTXSTD_API int ptxstd_quantize_mxfp8_layout(const uint16_t* d_x, int64_t rows, i
 PTXSTD_API int ptxstd_quantize_nvfp4_layout(const uint16_t* d_x, int64_t rows, int64_t cols,
                                  float global_scale, uint8_t* d_q, uint8_t* d_sf, int sf_layout,
                                  ptxstd_stream stream);
+/* Stochastic-rounding quantise (the from_f32_stochastic element conversion of
+ * src/data_types/narrow.rs:494-505 inside the same recipes; scales unchanged). Element i of the
+ * flat row-major input belongs to group i / 4, whose random bits are word (group % 2) of
+ * SplitMix64 output group / 2 started at `seed`: z = seed + (k + 1) * 0x9E3779B97F4A7C15;
+ * z = (z ^ z >> 30) * 0xBF58476D1CE4E5B9; z = (z ^ z >> 27) * 0x94D049BB133111EB; z ^ z >> 31.
+ * The same seed gives the same codes on every call and every launch shape. */
+PTXSTD_API int ptxstd_quantize_mxfp8_rs(const uint16_t* d_x, int64_t rows, int64_t cols, uint8_t* d_q,
+                             uint8_t* d_sf, int sf_layout, uint64_t seed, ptxstd_stream stream);
+PTXSTD_API int ptxstd_quantize_nvfp4_rs(const uint16_t* d_x, int64_t rows, int64_t cols,
+                             float global_scale, uint8_t* d_q, uint8_t* d_sf, int sf_layout,
+                             uint64_t seed, ptxstd_stream stream);
 
 /* ---- block-scaled / narrow GEMMs on tcgen05 --------------------------------------------------- */
 /* FP8 GEMM: C[M,N] bf16 row-major = sa * sb * A[M,K] * B[N,K]^T with E4M3 A and B (K contiguous),

@@ -239,6 +239,140 @@ uint16_t ptxo_f32_to_bf16(float x) {
 float ptxo_bf16_to_f32(uint16_t h) { return u2f((uint32_t)h << 16); }
 
 /* ------------------------------------------------------------------------------------------ */
+/* stochastic rounding                                                                        */
+/* ------------------------------------------------------------------------------------------ */
+
+static inline uint32_t bitrev8(uint32_t v) {
+    uint32_t r = 0;
+    for (int i = 0; i < 8; ++i) r |= ((v >> i) & 1u) << (7 - i);
+    return r;
+}
+static inline uint32_t bitrev16(uint32_t v) { return (bitrev8(v & 0xFFu) << 8) | bitrev8(v >> 8); }
+
+/* Element k's random value. FP8/FP6 (narrow.rs quad_from_f32_stochastic, float8.rs:59: "the lower
+ * 16 bits are used for elements 0 and 1 and the upper 16 bits for elements 2 and 3"): the even
+ * element reads its half most significant bit first, the odd element reads it bit-reversed (bit
+ * 0 or 16 most significant). E2M1 (float4.rs:60: "the lower 8 bits of both 16-bit halves are used
+ * for elements 0 and 1 and the upper 8 bits of both halves for elements 2 and 3"): a 16-bit value
+ * from two bytes, the byte of the upper half first for the even element; the odd element reads
+ * both bytes bit-reversed, the lower half's first. bf16 (bfloat16.rs:572-579): the low 16 bits
+ * for element 0, the high 16 for element 1; f16 (float16.rs:740-745): the 13 low bits of each
+ * half. */
+uint32_t ptxo_rs_random(int kind, uint32_t rb, int k) {
+    switch (kind) {
+    case PTXO_RS_X4: {
+        uint32_t half = (k < 2) ? (rb & 0xFFFFu) : (rb >> 16);
+        return (k & 1) ? bitrev16(half) : half;
+    }
+    case PTXO_RS_E2M1:
+        switch (k) {
+        case 0: return (((rb >> 16) & 0xFFu) << 8) | (rb & 0xFFu);
+        case 1: return (bitrev8(rb & 0xFFu) << 8) | bitrev8((rb >> 16) & 0xFFu);
+        case 2: return ((rb >> 24) << 8) | ((rb >> 8) & 0xFFu);
+        default: return (bitrev8((rb >> 8) & 0xFFu) << 8) | bitrev8(rb >> 24);
+        }
+    case PTXO_RS_BF16: return k ? (rb >> 16) : (rb & 0xFFFFu);
+    default: return (k ? (rb >> 16) : rb) & 0x1FFFu;
+    }
+}
+
+/* |x| (finite, bits a, a normal f32) split at the quantum of the target binade: the number n of
+ * whole quanta and the carry of (discarded part, truncated to w bits) + r out of w bits.
+ * shift = number of significand bits below the quantum. */
+static inline uint32_t rs_quanta(uint32_t a, int man_bits, int emin, uint32_t r, int w, int* te) {
+    uint64_t sig = (uint64_t)((a & 0x7FFFFFu) | 0x800000u);
+    int e = (int)(a >> 23) - 127;
+    *te = e < emin ? emin : e;
+    int shift = 23 - man_bits + (*te - e);
+    uint64_t n = 0, fw = 0;
+    if (shift < 64) {
+        n = sig >> shift;
+        fw = ((sig & ((1ull << shift) - 1)) << w) >> shift;
+    }
+    if (fw + r >= (1ull << w)) n++;
+    return (uint32_t)n;
+}
+
+/* Stochastic rounding of a finite, non-negative f32 (bits a) to a narrow magnitude code with
+ * .satfinite. f32 subnormals lie below 2^-126, where every format's discarded fraction has no
+ * set bit among its top 16, so they give 0. */
+static inline uint32_t encode_mag_rs(const narrow_fmt* f, uint32_t a, uint32_t r) {
+    if ((a >> 23) == 0) return 0;
+    int emin = 1 - f->bias, te;
+    uint32_t n = rs_quanta(a, f->man_bits, emin, r, 16, &te);
+    uint32_t one = 1u << f->man_bits;
+    if (n >= (one << 1)) { te++; n >>= 1; }
+    uint32_t code;
+    if (te == emin && n < one) code = n;
+    else code = ((uint32_t)(te + f->bias) << f->man_bits) | (n - one);
+    if (code > f->max_mag) code = f->max_mag;
+    return code;
+}
+
+uint8_t ptxo_f32_to_narrow_rs(int format, float x, uint32_t r, int relu) {
+    const narrow_fmt* f = fmt_of(format);
+    uint32_t u = f2u(x);
+    uint32_t a = u & 0x7FFFFFFFu;
+    if (a > 0x7F800000u) return f->nan_code;
+    uint8_t sign = (u >> 31) ? f->sign_bit : 0;
+    if (relu && sign) return 0;
+    uint32_t mag = (a == 0x7F800000u) ? f->max_mag : encode_mag_rs(f, a, r);
+    return (uint8_t)(mag | sign);
+}
+
+/* bf16 keeps the f32 exponent, so the discarded part is the low 16 bits of the pattern (for f32
+ * subnormals too: bf16's subnormal quantum is 2^-133, bit 16 of the f32 subnormal). */
+uint16_t ptxo_f32_to_bf16_rs(float x, uint32_t r, int relu, int satfinite) {
+    uint32_t u = f2u(x), a = u & 0x7FFFFFFFu;
+    if (a > 0x7F800000u) return 0x7FFF;
+    uint32_t m;
+    if (a == 0x7F800000u) {
+        m = satfinite ? 0x7F7Fu : 0x7F80u;
+    } else {
+        m = a >> 16;
+        if ((a & 0xFFFFu) + (r & 0xFFFFu) >= 0x10000u) m++;
+        if (m >= 0x7F80u) m = satfinite ? 0x7F7Fu : 0x7F80u;
+    }
+    if (relu && (u >> 31)) return 0;
+    return (uint16_t)(((u >> 16) & 0x8000u) | m);
+}
+
+uint16_t ptxo_f32_to_f16_rs(float x, uint32_t r, int relu, int satfinite) {
+    uint32_t u = f2u(x), a = u & 0x7FFFFFFFu;
+    if (a > 0x7F800000u) return 0x7FFF;
+    uint32_t m;
+    if (a == 0x7F800000u) {
+        m = satfinite ? 0x7BFFu : 0x7C00u;
+    } else if ((a >> 23) == 0) {
+        m = 0; /* below 2^-126: nothing within the top 13 bits of a 2^-24 quantum */
+    } else {
+        int te;
+        uint32_t n = rs_quanta(a, 10, -14, r & 0x1FFFu, 13, &te);
+        if (te == -14) {
+            m = n; /* subnormal, or the first normal binade reached by the carry */
+        } else {
+            if (n == 2048) { te++; n = 1024; }
+            m = ((uint32_t)(te + 15) << 10) | (n - 1024);
+        }
+        if (m >= 0x7C00u) m = satfinite ? 0x7BFFu : 0x7C00u;
+    }
+    if (relu && (u >> 31)) return 0;
+    return (uint16_t)(((u >> 16) & 0x8000u) | m);
+}
+
+uint64_t ptxo_splitmix64(uint64_t seed, uint64_t i) {
+    uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+uint32_t ptxo_sr_rbits(uint64_t seed, uint64_t group) {
+    uint64_t h = ptxo_splitmix64(seed, group >> 1);
+    return (group & 1) ? (uint32_t)(h >> 32) : (uint32_t)h;
+}
+
+/* ------------------------------------------------------------------------------------------ */
 /* bulk conversions                                                                           */
 /* ------------------------------------------------------------------------------------------ */
 
@@ -297,6 +431,55 @@ void ptxo_ue8m0_encode_array(const float* x, uint8_t* out, size_t n, int rnd_up,
     parallel_for(n, threads, ue_range, &c);
 }
 
+typedef struct {
+    int format, relu, sat; const float* x; const uint32_t* rb; uint8_t* out8; uint16_t* out16;
+} rs_ctx;
+
+static void rs_range(void* p, uint64_t lo, uint64_t hi) {
+    rs_ctx* c = (rs_ctx*)p;
+    if (c->format == PTXO_E2M1) {
+        for (uint64_t i = lo; i < hi; ++i) { /* i indexes output bytes: elements 2i, 2i + 1 */
+            uint8_t b = 0;
+            for (int h = 0; h < 2; ++h) {
+                uint64_t e = 2 * i + h;
+                uint32_t r = ptxo_rs_random(PTXO_RS_E2M1, c->rb[e / 4], (int)(e % 4));
+                b |= (uint8_t)(ptxo_f32_to_narrow_rs(PTXO_E2M1, c->x[e], r, c->relu) << (4 * h));
+            }
+            c->out8[i] = b;
+        }
+    } else if (c->format >= 0) {
+        for (uint64_t i = lo; i < hi; ++i) {
+            uint32_t r = ptxo_rs_random(PTXO_RS_X4, c->rb[i / 4], (int)(i % 4));
+            c->out8[i] = ptxo_f32_to_narrow_rs(c->format, c->x[i], r, c->relu);
+        }
+    } else {
+        int bf = c->format == -1;
+        for (uint64_t i = lo; i < hi; ++i) {
+            uint32_t r = ptxo_rs_random(bf ? PTXO_RS_BF16 : PTXO_RS_F16, c->rb[i / 2], (int)(i % 2));
+            c->out16[i] = bf ? ptxo_f32_to_bf16_rs(c->x[i], r, c->relu, c->sat)
+                             : ptxo_f32_to_f16_rs(c->x[i], r, c->relu, c->sat);
+        }
+    }
+}
+
+void ptxo_encode_rs_array(int format, const float* x, const uint32_t* rbits, uint8_t* out,
+                          size_t n, int relu, int threads) {
+    rs_ctx c = {format, relu, 1, x, rbits, out, NULL};
+    parallel_for(format == PTXO_E2M1 ? n / 2 : n, threads, rs_range, &c);
+}
+
+void ptxo_bf16_rs_array(const float* x, const uint32_t* rbits, uint16_t* out, size_t n, int relu,
+                        int satfinite, int threads) {
+    rs_ctx c = {-1, relu, satfinite, x, rbits, NULL, out};
+    parallel_for(n, threads, rs_range, &c);
+}
+
+void ptxo_f16_rs_array(const float* x, const uint32_t* rbits, uint16_t* out, size_t n, int relu,
+                       int satfinite, int threads) {
+    rs_ctx c = {-2, relu, satfinite, x, rbits, NULL, out};
+    parallel_for(n, threads, rs_range, &c);
+}
+
 /* ------------------------------------------------------------------------------------------ */
 /* exhaustive sweep support                                                                   */
 /* ------------------------------------------------------------------------------------------ */
@@ -318,6 +501,26 @@ uint8_t ptxo_encode_variant(int variant, float x) {
     }
 }
 
+int ptxo_sweep_width(int variant) { return variant >= PTXO_V_BF16_RS ? 2 : 1; }
+
+uint32_t ptxo_sweep_code(int variant, uint64_t p) {
+    float x = u2f((uint32_t)p);
+    if (variant < PTXO_V_E4M3_RS) return ptxo_encode_variant(variant, x);
+    if (variant < PTXO_V_BF16_RS) {
+        static const int fmts[5] = {PTXO_E4M3, PTXO_E5M2, PTXO_E2M3, PTXO_E3M2, PTXO_E2M1};
+        int v = variant - PTXO_V_E4M3_RS;
+        int fmt = fmts[v % 5], relu = v >= 5;
+        uint32_t rb = ptxo_sr_rbits(PTXO_SWEEP_SEED, p >> 2);
+        uint32_t r = ptxo_rs_random(fmt == PTXO_E2M1 ? PTXO_RS_E2M1 : PTXO_RS_X4, rb, (int)(p & 3));
+        return ptxo_f32_to_narrow_rs(fmt, x, r, relu);
+    }
+    int v = variant - PTXO_V_BF16_RS;
+    int bf = v < 4, relu = v & 1, sat = (v >> 1) & 1;
+    uint32_t rb = ptxo_sr_rbits(PTXO_SWEEP_SEED, p >> 1);
+    uint32_t r = ptxo_rs_random(bf ? PTXO_RS_BF16 : PTXO_RS_F16, rb, (int)(p & 1));
+    return bf ? ptxo_f32_to_bf16_rs(x, r, relu, sat) : ptxo_f32_to_f16_rs(x, r, relu, sat);
+}
+
 typedef struct {
     int variant; uint64_t base; const uint8_t* dev;
     uint32_t* report; uint64_t max_report;
@@ -327,10 +530,12 @@ typedef struct {
 static void sweep_range(void* p, uint64_t lo, uint64_t hi) {
     sweep_ctx* c = (sweep_ctx*)p;
     uint64_t local = 0;
+    const int w = ptxo_sweep_width(c->variant);
     for (uint64_t i = lo; i < hi; ++i) {
         uint32_t bits = (uint32_t)(c->base + i);
-        uint8_t want = ptxo_encode_variant(c->variant, u2f(bits));
-        uint8_t got = c->dev[i];
+        uint32_t want = ptxo_sweep_code(c->variant, c->base + i);
+        uint32_t got = c->dev[w * i];
+        if (w == 2) got |= (uint32_t)c->dev[w * i + 1] << 8;
         if (want != got) {
             pthread_mutex_lock(&c->mu);
             if (c->mismatches < c->max_report && c->report) {
@@ -370,22 +575,26 @@ typedef struct { int variant; uint64_t base; uint64_t* part; uint64_t chunk; } d
 
 static void dig_range(void* p, uint64_t lo, uint64_t hi) {
     dig_ctx* c = (dig_ctx*)p;
+    const int w = ptxo_sweep_width(c->variant);
     for (uint64_t k = lo; k < hi; ++k) {
         uint64_t h = FNV_OFFSET;
         uint64_t b0 = c->base + k * c->chunk;
         for (uint64_t i = 0; i < c->chunk; ++i) {
-            h ^= ptxo_encode_variant(c->variant, u2f((uint32_t)(b0 + i)));
-            h *= FNV_PRIME;
+            uint32_t code = ptxo_sweep_code(c->variant, b0 + i);
+            for (int j = 0; j < w; ++j) {
+                h ^= (code >> (8 * j)) & 0xFFu;
+                h *= FNV_PRIME;
+            }
         }
         c->part[k] = h;
     }
 }
 
-/* Digest of [base, base + n): FNV-1a 64 of each 2^16-input piece, then FNV-1a 64 over those
- * digests' little-endian bytes (so that the pieces can be hashed in parallel). n must be a
- * multiple of 2^16. */
+/* Digest of [base, base + n): FNV-1a 64 of each 2^16-byte piece of the codes (width bytes per
+ * input, little-endian), then FNV-1a 64 over those digests' little-endian bytes (so that the
+ * pieces can be hashed in parallel). n * width must be a multiple of 2^16. */
 uint64_t ptxo_sweep_digest(int variant, uint64_t base, uint64_t n, int threads) {
-    const uint64_t chunk = 1u << 16;
+    const uint64_t chunk = (1u << 16) / (uint64_t)ptxo_sweep_width(variant);
     uint64_t parts = n / chunk;
     uint64_t* part = (uint64_t*)malloc(sizeof(uint64_t) * (parts ? parts : 1));
     dig_ctx c = {variant, base, part, chunk};
@@ -504,6 +713,70 @@ int ptxo_quantize_nvfp4(const uint16_t* x, int64_t rows, int64_t cols, float g, 
     if (!(g > 0.0f) || isinf(g)) return -1;
     quant_ctx c = {x, cols, q, sf, g};
     parallel_for((uint64_t)rows, threads, nvfp4_rows, &c);
+    return 0;
+}
+
+typedef struct {
+    const uint16_t* x; int64_t cols; uint8_t* q; uint8_t* sf; float g; uint64_t seed;
+} quant_rs_ctx;
+
+/* Element i of the flat input: rs_random(kind, sr_rbits(seed, i / 4), i % 4). */
+static inline uint32_t quant_rs_random(uint64_t seed, uint64_t i, int kind) {
+    return ptxo_rs_random(kind, ptxo_sr_rbits(seed, i >> 2), (int)(i & 3));
+}
+
+static void mxfp8_rs_rows(void* p, uint64_t lo, uint64_t hi) {
+    quant_rs_ctx* c = (quant_rs_ctx*)p;
+    float buf[32];
+    for (uint64_t r = lo; r < hi; ++r) {
+        const uint16_t* xr = c->x + r * c->cols;
+        for (int64_t b = 0; b < c->cols / 32; ++b) {
+            for (int i = 0; i < 32; ++i) buf[i] = ptxo_bf16_to_f32(xr[b * 32 + i]);
+            uint8_t qtmp[32];
+            uint8_t code = ptxo_mxfp8_block(buf, qtmp); /* the scale; elements redone below */
+            float inv = ue8m0_inverse(code);
+            uint64_t e0 = r * (uint64_t)c->cols + (uint64_t)b * 32;
+            for (int i = 0; i < 32; ++i)
+                c->q[e0 + i] = ptxo_f32_to_narrow_rs(PTXO_E4M3, buf[i] * inv,
+                                                     quant_rs_random(c->seed, e0 + i, PTXO_RS_X4), 0);
+            c->sf[r * (c->cols / 32) + b] = code;
+        }
+    }
+}
+
+void ptxo_quantize_mxfp8_rs(const uint16_t* x, int64_t rows, int64_t cols, uint64_t seed,
+                            uint8_t* q, uint8_t* sf, int threads) {
+    quant_rs_ctx c = {x, cols, q, sf, 0.0f, seed};
+    parallel_for((uint64_t)rows, threads, mxfp8_rs_rows, &c);
+}
+
+static void nvfp4_rs_rows(void* p, uint64_t lo, uint64_t hi) {
+    quant_rs_ctx* c = (quant_rs_ctx*)p;
+    float buf[16];
+    uint8_t nib[16];
+    for (uint64_t r = lo; r < hi; ++r) {
+        const uint16_t* xr = c->x + r * c->cols;
+        uint8_t* qr = c->q + r * (c->cols / 2);
+        for (int64_t b = 0; b < c->cols / 16; ++b) {
+            for (int i = 0; i < 16; ++i) buf[i] = ptxo_bf16_to_f32(xr[b * 16 + i]);
+            uint8_t sf = ptxo_nvfp4_block(buf, c->g, nib); /* the scale; elements redone below */
+            float t = ptxo_e4m3_to_f32(sf) * c->g;
+            float rcp = (t == 0.0f) ? 0.0f : 1.0f / t;
+            uint64_t e0 = r * (uint64_t)c->cols + (uint64_t)b * 16;
+            for (int i = 0; i < 16; ++i)
+                nib[i] = ptxo_f32_to_narrow_rs(PTXO_E2M1, buf[i] * rcp,
+                                               quant_rs_random(c->seed, e0 + i, PTXO_RS_E2M1), 0);
+            c->sf[r * (c->cols / 16) + b] = sf;
+            for (int i = 0; i < 8; ++i) qr[b * 8 + i] = (uint8_t)(nib[2 * i] | (nib[2 * i + 1] << 4));
+        }
+    }
+}
+
+int ptxo_quantize_nvfp4_rs(const uint16_t* x, int64_t rows, int64_t cols, float g, uint64_t seed,
+                           uint8_t* q, uint8_t* sf, int threads) {
+    if (!(g > 0.0f) || isinf(g)) return -1;
+    quant_rs_ctx c = {x, cols, q, sf, g, seed};
+    parallel_for((uint64_t)rows, threads, nvfp4_rs_rows, &c);
     return 0;
 }
 

@@ -20,7 +20,14 @@ E4M3, E5M2, E2M1, E2M3, E3M2 = 0, 1, 2, 3, 4
 (V_E4M3, V_E5M2, V_E2M1, V_E4M3_RELU, V_E5M2_RELU, V_E2M1_RELU, V_UE8M0_RZ,
  V_UE8M0_RP) = range(8)
 VARIANT_NAMES = ["e4m3", "e5m2", "e2m1", "e4m3_relu", "e5m2_relu", "e2m1_relu", "ue8m0_rz",
-                 "ue8m0_rp", "e2m3", "e3m2", "e2m3_relu", "e3m2_relu"]
+                 "ue8m0_rp", "e2m3", "e3m2", "e2m3_relu", "e3m2_relu",
+                 "e4m3_rs", "e5m2_rs", "e2m3_rs", "e3m2_rs", "e2m1_rs",
+                 "e4m3_rs_relu", "e5m2_rs_relu", "e2m3_rs_relu", "e3m2_rs_relu", "e2m1_rs_relu",
+                 "bf16_rs", "bf16_rs_relu", "bf16_rs_sat", "bf16_rs_relu_sat",
+                 "f16_rs", "f16_rs_relu", "f16_rs_sat", "f16_rs_relu_sat"]
+# stochastic-rounding random-value kinds (ptxo_rs_random)
+RS_X4, RS_E2M1, RS_BF16, RS_F16 = 0, 1, 2, 3
+SWEEP_SEED = 0x2545F4914F6CDD1D
 
 _lib = None
 
@@ -90,6 +97,19 @@ def _declare(L: C.CDLL) -> None:
         "ptxo_zero_mask_with_sub_mask_start": (i32, [u64, u32, i32, u32, C.POINTER(u64)]),
         "ptxo_zero_mask_with_column_shift": (i32, [u64, u32, C.POINTER(u64)]),
         "ptxo_hardware_threads": (i32, []),
+        "ptxo_rs_random": (u32, [i32, u32, i32]),
+        "ptxo_f32_to_narrow_rs": (u8, [i32, f32, u32, i32]),
+        "ptxo_f32_to_bf16_rs": (u16, [f32, u32, i32, i32]),
+        "ptxo_f32_to_f16_rs": (u16, [f32, u32, i32, i32]),
+        "ptxo_encode_rs_array": (None, [i32, p, p, p, C.c_size_t, i32, i32]),
+        "ptxo_bf16_rs_array": (None, [p, p, p, C.c_size_t, i32, i32, i32]),
+        "ptxo_f16_rs_array": (None, [p, p, p, C.c_size_t, i32, i32, i32]),
+        "ptxo_splitmix64": (u64, [u64, u64]),
+        "ptxo_sr_rbits": (u32, [u64, u64]),
+        "ptxo_sweep_code": (u32, [i32, u64]),
+        "ptxo_sweep_width": (i32, [i32]),
+        "ptxo_quantize_mxfp8_rs": (None, [p, i64, i64, u64, p, p, i32]),
+        "ptxo_quantize_nvfp4_rs": (i32, [p, i64, i64, f32, u64, p, p, i32]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(L, name)
@@ -206,13 +226,82 @@ def sgemm_nt(A, B, threads=0):
     return Cm
 
 
+def sweep_width(variant: int) -> int:
+    """Bytes per input of a sweep variant (2 for the bf16/f16 stochastic forms)."""
+    return int(lib().ptxo_sweep_width(variant))
+
+
 def sweep_compare(variant: int, base: int, dev_codes: np.ndarray, max_report: int = 64,
                   threads: int = 0):
     dev = np.ascontiguousarray(dev_codes, dtype=np.uint8)
     rep = np.zeros((max_report, 3), dtype=np.uint32)
-    n = lib().ptxo_sweep_compare(variant, base, dev.size, _ptr(dev), _ptr(rep), max_report,
-                                 threads)
+    n = lib().ptxo_sweep_compare(variant, base, dev.size // sweep_width(variant), _ptr(dev),
+                                 _ptr(rep), max_report, threads)
     return int(n), rep[: min(int(n), max_report)]
+
+
+def encode_rs(fmt: int, x: np.ndarray, rbits: np.ndarray, relu: bool = False,
+              threads: int = 0) -> np.ndarray:
+    """Stochastic rounding of x (f32) with rbits[i // 4] (E2M1 packed two per byte)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rb = np.ascontiguousarray(rbits, dtype=np.uint32)
+    assert rb.size >= (x.size + 3) // 4
+    out = np.empty(x.size // 2 if fmt == E2M1 else x.size, dtype=np.uint8)
+    lib().ptxo_encode_rs_array(fmt, _ptr(x), _ptr(rb), _ptr(out), x.size, int(relu), threads)
+    return out
+
+
+def bf16_rs(x: np.ndarray, rbits: np.ndarray, relu=False, satfinite=False, threads=0):
+    """Stochastic rounding f32 -> bf16 bit patterns with rbits[i // 2]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rb = np.ascontiguousarray(rbits, dtype=np.uint32)
+    assert rb.size >= (x.size + 1) // 2
+    out = np.empty(x.size, dtype=np.uint16)
+    lib().ptxo_bf16_rs_array(_ptr(x), _ptr(rb), _ptr(out), x.size, int(relu), int(satfinite),
+                             threads)
+    return out
+
+
+def f16_rs(x: np.ndarray, rbits: np.ndarray, relu=False, satfinite=False, threads=0):
+    """Stochastic rounding f32 -> f16 bit patterns with rbits[i // 2]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rb = np.ascontiguousarray(rbits, dtype=np.uint32)
+    assert rb.size >= (x.size + 1) // 2
+    out = np.empty(x.size, dtype=np.uint16)
+    lib().ptxo_f16_rs_array(_ptr(x), _ptr(rb), _ptr(out), x.size, int(relu), int(satfinite),
+                            threads)
+    return out
+
+
+def sr_rbits(seed: int, groups: int) -> np.ndarray:
+    """rbits of groups 0 .. groups-1 of the seeded quantisers (vectorised SplitMix64)."""
+    g = np.arange((groups + 1) // 2, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        z = np.uint64(seed) + (g + np.uint64(1)) * np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        z = z ^ (z >> np.uint64(31))
+    return z.view(np.uint32)[:groups].copy()
+
+
+def quantize_mxfp8_rs(x_bf16: np.ndarray, seed: int, threads: int = 0):
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    rows, cols = x.shape
+    q = np.empty((rows, cols), dtype=np.uint8)
+    sf = np.empty((rows, cols // 32), dtype=np.uint8)
+    lib().ptxo_quantize_mxfp8_rs(_ptr(x), rows, cols, seed, _ptr(q), _ptr(sf), threads)
+    return q, sf
+
+
+def quantize_nvfp4_rs(x_bf16: np.ndarray, g: float, seed: int, threads: int = 0):
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    rows, cols = x.shape
+    q = np.empty((rows, cols // 2), dtype=np.uint8)
+    sf = np.empty((rows, cols // 16), dtype=np.uint8)
+    if lib().ptxo_quantize_nvfp4_rs(_ptr(x), rows, cols, float(g), seed, _ptr(q), _ptr(sf),
+                                    threads) != 0:
+        raise ValueError("bad global scale")
+    return q, sf
 
 
 def sweep_digest(variant: int, base: int, n: int, threads: int = 0) -> int:

@@ -1,6 +1,8 @@
 // Element-wise conversion kernels of the narrow formats (the reference's Vector<E, N>::from_f32 /
-// to_f32 family, src/data_types/narrow.rs:354-425, applied over device arrays), plus the
-// exhaustive-sweep kernel that converts f32 bit patterns generated from the thread index.
+// to_f32 family, src/data_types/narrow.rs:354-425, applied over device arrays), their
+// stochastic-rounding forms (from_f32_stochastic, narrow.rs:494-505; bf16/f16
+// bfloat16.rs:572-598, float16.rs:740-766), plus the exhaustive-sweep kernel that converts f32
+// bit patterns generated from the thread index.
 #include "common.cuh"
 #include "data_types.cuh"
 
@@ -61,6 +63,69 @@ __global__ void __launch_bounds__(256) encode_e2m1_kernel(const float* __restric
     if (t < n / 2) out[t] = static_cast<uint8_t>(dt::e2m1x2_from_f32<RELU>(x[2 * t], x[2 * t + 1]));
 }
 
+// One group of four f32 -> four codes with stochastic rounding (quad_from_f32_stochastic,
+// narrow.rs:217-229): one byte each (FP8, FP6) or one nibble each (E2M1, 16 bits).
+template <int OP, bool RELU>
+__device__ __forceinline__ uint32_t encode_quad_rs(float x0, float x1, float x2, float x3,
+                                                   uint32_t rb) {
+    if constexpr (OP == kE4M3) return dt::e4m3x4_from_f32_rs<RELU>(x0, x1, x2, x3, rb);
+    else if constexpr (OP == kE5M2) return dt::e5m2x4_from_f32_rs<RELU>(x0, x1, x2, x3, rb);
+    else if constexpr (OP == kE2M3) return dt::e2m3x4_from_f32_rs<RELU>(x0, x1, x2, x3, rb);
+    else if constexpr (OP == kE3M2) return dt::e3m2x4_from_f32_rs<RELU>(x0, x1, x2, x3, rb);
+    else return dt::e2m1x4_from_f32_rs<RELU>(x0, x1, x2, x3, rb);
+}
+
+// f32 -> codes with stochastic rounding: group g = elements 4g .. 4g+3 with rbits[g]; one
+// 16-byte load and one 4-byte (2-byte for E2M1) store per group. A last group of fewer than four
+// is padded with zeros and only its real elements are written (narrow.rs:483-486).
+template <int OP, bool RELU>
+__global__ void __launch_bounds__(256) encode_rs_kernel(const float* __restrict__ x,
+                                                        const uint32_t* __restrict__ rbits,
+                                                        uint8_t* __restrict__ out, size_t n) {
+    const size_t n4 = n / 4;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (size_t i = tid; i < n4; i += stride) {
+        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        const uint32_t c = encode_quad_rs<OP, RELU>(v.x, v.y, v.z, v.w, rbits[i]);
+        if constexpr (OP == kE2M1) reinterpret_cast<uint16_t*>(out)[i] = static_cast<uint16_t>(c);
+        else reinterpret_cast<uint32_t*>(out)[i] = c;
+    }
+    const size_t rem = n - n4 * 4;
+    if (tid == 0 && rem != 0) {
+        const size_t b = n4 * 4;
+        const float x0 = x[b], x1 = rem > 1 ? x[b + 1] : 0.0f, x2 = rem > 2 ? x[b + 2] : 0.0f;
+        const uint32_t c = encode_quad_rs<OP, RELU>(x0, x1, x2, 0.0f, rbits[n4]);
+        if constexpr (OP == kE2M1) {
+            out[b / 2] = static_cast<uint8_t>(c);  // n is even: the two real elements
+        } else {
+            for (size_t j = 0; j < rem; ++j) out[b + j] = static_cast<uint8_t>(c >> (8 * j));
+        }
+    }
+}
+
+// f32 -> bf16 / f16 with stochastic rounding: pair p = elements 2p, 2p+1 with rbits[p]; an odd
+// last element is converted as a pair with a zero lane.
+template <bool BF16, bool RELU, bool SAT>
+__global__ void __launch_bounds__(256) encode_x2_rs_kernel(const float* __restrict__ x,
+                                                           const uint32_t* __restrict__ rbits,
+                                                           uint16_t* __restrict__ out, size_t n) {
+    const size_t n2 = n / 2;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (size_t i = tid; i < n2; i += stride) {
+        const float2 v = reinterpret_cast<const float2*>(x)[i];
+        reinterpret_cast<uint32_t*>(out)[i] =
+            BF16 ? dt::bf16x2_from_f32_rs<RELU, SAT>(v.x, v.y, rbits[i])
+                 : dt::f16x2_from_f32_rs<RELU, SAT>(v.x, v.y, rbits[i]);
+    }
+    if (tid == 0 && (n & 1)) {
+        const uint32_t c = BF16 ? dt::bf16x2_from_f32_rs<RELU, SAT>(x[n - 1], 0.0f, rbits[n2])
+                                : dt::f16x2_from_f32_rs<RELU, SAT>(x[n - 1], 0.0f, rbits[n2]);
+        out[n - 1] = static_cast<uint16_t>(c);
+    }
+}
+
 template <bool ROUND_UP, bool SAT>
 __global__ void __launch_bounds__(256) encode_ue8m0_kernel(const float* __restrict__ x,
                                                            uint8_t* __restrict__ out, size_t n) {
@@ -99,12 +164,84 @@ __global__ void __launch_bounds__(256) decode_kernel(const uint8_t* __restrict__
     }
 }
 
-// Converts the f32 bit patterns base + i, i < n, with variant v; one output byte per input.
+// Seed of the sweep's random bits: input pattern p takes group p / 4 (p / 2 for bf16/f16) of
+// the SplitMix64 stream below.
+constexpr uint64_t kSweepSeed = 0x2545F4914F6CDD1Dull;
+
+// Stochastic-rounding sweep variants 12..29: four inputs base + i .. +3 (i a multiple of 4) ->
+// four one-byte codes (12..21: e4m3, e5m2, e2m3, e3m2, e2m1 as nibbles, then the same with
+// .relu), or two 32-bit words of bf16/f16 pairs (22..29: bf16 plain, .relu, .satfinite, both;
+// then f16), written at out + i or out + 2 i.
+__device__ __forceinline__ void sweep_rs(int v, uint64_t p0, float x0, float x1, float x2,
+                                         float x3, uint8_t* out, uint64_t i, uint64_t valid) {
+    if (v < 22) {
+        const uint64_t h = dt::splitmix64(kSweepSeed, p0 >> 3);
+        const uint32_t rb = ((p0 >> 2) & 1) ? static_cast<uint32_t>(h >> 32)
+                                            : static_cast<uint32_t>(h);
+        uint32_t c;
+        switch (v) {
+        case 12: c = dt::e4m3x4_from_f32_rs<false>(x0, x1, x2, x3, rb); break;
+        case 13: c = dt::e5m2x4_from_f32_rs<false>(x0, x1, x2, x3, rb); break;
+        case 14: c = dt::e2m3x4_from_f32_rs<false>(x0, x1, x2, x3, rb); break;
+        case 15: c = dt::e3m2x4_from_f32_rs<false>(x0, x1, x2, x3, rb); break;
+        case 16: c = dt::e2m1x4_from_f32_rs<false>(x0, x1, x2, x3, rb); break;
+        case 17: c = dt::e4m3x4_from_f32_rs<true>(x0, x1, x2, x3, rb); break;
+        case 18: c = dt::e5m2x4_from_f32_rs<true>(x0, x1, x2, x3, rb); break;
+        case 19: c = dt::e2m3x4_from_f32_rs<true>(x0, x1, x2, x3, rb); break;
+        case 20: c = dt::e3m2x4_from_f32_rs<true>(x0, x1, x2, x3, rb); break;
+        default: c = dt::e2m1x4_from_f32_rs<true>(x0, x1, x2, x3, rb); break;
+        }
+        if (v == 16 || v == 21)  // nibbles -> one per byte
+            c = (c & 0xFu) | ((c & 0xF0u) << 4) | ((c & 0xF00u) << 8) | ((c & 0xF000u) << 12);
+        if (valid == 4) {
+            *reinterpret_cast<uint32_t*>(out + i) = c;
+        } else {
+            for (uint64_t j = 0; j < valid; ++j) out[i + j] = static_cast<uint8_t>(c >> (8 * j));
+        }
+        return;
+    }
+    // pairs (p0, p0 + 1) and (p0 + 2, p0 + 3): groups p0 / 2 (even) and p0 / 2 + 1
+    const uint64_t h = dt::splitmix64(kSweepSeed, p0 >> 2);
+    const uint32_t r0 = static_cast<uint32_t>(h), r1 = static_cast<uint32_t>(h >> 32);
+    uint32_t c0, c1;
+    switch (v) {
+    case 22: c0 = dt::bf16x2_from_f32_rs<false, false>(x0, x1, r0); c1 = dt::bf16x2_from_f32_rs<false, false>(x2, x3, r1); break;
+    case 23: c0 = dt::bf16x2_from_f32_rs<true, false>(x0, x1, r0); c1 = dt::bf16x2_from_f32_rs<true, false>(x2, x3, r1); break;
+    case 24: c0 = dt::bf16x2_from_f32_rs<false, true>(x0, x1, r0); c1 = dt::bf16x2_from_f32_rs<false, true>(x2, x3, r1); break;
+    case 25: c0 = dt::bf16x2_from_f32_rs<true, true>(x0, x1, r0); c1 = dt::bf16x2_from_f32_rs<true, true>(x2, x3, r1); break;
+    case 26: c0 = dt::f16x2_from_f32_rs<false, false>(x0, x1, r0); c1 = dt::f16x2_from_f32_rs<false, false>(x2, x3, r1); break;
+    case 27: c0 = dt::f16x2_from_f32_rs<true, false>(x0, x1, r0); c1 = dt::f16x2_from_f32_rs<true, false>(x2, x3, r1); break;
+    case 28: c0 = dt::f16x2_from_f32_rs<false, true>(x0, x1, r0); c1 = dt::f16x2_from_f32_rs<false, true>(x2, x3, r1); break;
+    default: c0 = dt::f16x2_from_f32_rs<true, true>(x0, x1, r0); c1 = dt::f16x2_from_f32_rs<true, true>(x2, x3, r1); break;
+    }
+    uint16_t* o = reinterpret_cast<uint16_t*>(out) + i;
+    const uint16_t codes[4] = {static_cast<uint16_t>(c0), static_cast<uint16_t>(c0 >> 16),
+                               static_cast<uint16_t>(c1), static_cast<uint16_t>(c1 >> 16)};
+    if (valid == 4) {
+        reinterpret_cast<uint32_t*>(o)[0] = c0;
+        reinterpret_cast<uint32_t*>(o)[1] = c1;
+    } else {
+        for (uint64_t j = 0; j < valid; ++j) o[j] = codes[j];
+    }
+}
+
+// Converts the f32 bit patterns base + i, i < n, with variant v; one output byte per input
+// (two for variants 22..29).
 __global__ void __launch_bounds__(256) sweep_kernel(int v, uint64_t base, uint64_t n,
                                                     uint8_t* __restrict__ out) {
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
     for (uint64_t i = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < n;
          i += stride * 4) {
+        if (v >= 12) {
+            const uint64_t p = base + i;
+            const uint64_t valid = n - i < 4 ? n - i : 4;
+            const float x0 = __uint_as_float(static_cast<uint32_t>(p));
+            const float x1 = valid > 1 ? __uint_as_float(static_cast<uint32_t>(p + 1)) : 0.0f;
+            const float x2 = valid > 2 ? __uint_as_float(static_cast<uint32_t>(p + 2)) : 0.0f;
+            const float x3 = valid > 3 ? __uint_as_float(static_cast<uint32_t>(p + 3)) : 0.0f;
+            sweep_rs(v, p, x0, x1, x2, x3, out, i, valid);
+            continue;
+        }
         uint32_t codes = 0;
         for (int j = 0; j < 4; ++j) {
             const float f = __uint_as_float(static_cast<uint32_t>(base + i + j));
@@ -143,6 +280,44 @@ template <typename F>
 int launch(F f) {
     f();
     return ptxstd::launch_status();
+}
+
+template <int OP>
+int launch_rs(const float* d_x, const uint32_t* d_rbits, uint8_t* d_out, size_t n, int relu,
+              ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    const uintptr_t out_align = OP == kE2M1 ? 1 : 3;
+    if (!d_x || !d_rbits || !d_out || !ptxstd::aligned16(d_x) ||
+        (reinterpret_cast<uintptr_t>(d_rbits) & 3) ||
+        (reinterpret_cast<uintptr_t>(d_out) & out_align))
+        return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int g = grid_for(n / 4 + 1);
+    return launch([&] {
+        if (relu) encode_rs_kernel<OP, true><<<g, 256, 0, s>>>(d_x, d_rbits, d_out, n);
+        else encode_rs_kernel<OP, false><<<g, 256, 0, s>>>(d_x, d_rbits, d_out, n);
+    });
+}
+
+template <bool BF16>
+int launch_x2_rs(const float* d_x, const uint32_t* d_rbits, uint16_t* d_out, size_t n, int relu,
+                 int satfinite, ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_x || !d_rbits || !d_out || (reinterpret_cast<uintptr_t>(d_x) & 7) ||
+        (reinterpret_cast<uintptr_t>(d_rbits) & 3) || (reinterpret_cast<uintptr_t>(d_out) & 3))
+        return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int g = grid_for(n / 2 + 1);
+    return launch([&] {
+        if (relu && satfinite)
+            encode_x2_rs_kernel<BF16, true, true><<<g, 256, 0, s>>>(d_x, d_rbits, d_out, n);
+        else if (relu)
+            encode_x2_rs_kernel<BF16, true, false><<<g, 256, 0, s>>>(d_x, d_rbits, d_out, n);
+        else if (satfinite)
+            encode_x2_rs_kernel<BF16, false, true><<<g, 256, 0, s>>>(d_x, d_rbits, d_out, n);
+        else
+            encode_x2_rs_kernel<BF16, false, false><<<g, 256, 0, s>>>(d_x, d_rbits, d_out, n);
+    });
 }
 
 }  // namespace
@@ -278,11 +453,41 @@ int ptxstd_cvt_ue8m0_to_f32(const uint8_t* d_codes, float* d_out, size_t n,
     return launch([&] { decode_kernel<3><<<grid_for(n), 256, 0, s>>>(d_codes, d_out, n); });
 }
 
+int ptxstd_cvt_f32_to_e4m3_rs(const float* d_x, const uint32_t* d_rbits, uint8_t* d_out, size_t n,
+                              int relu, ptxstd_stream stream) {
+    return launch_rs<kE4M3>(d_x, d_rbits, d_out, n, relu, stream);
+}
+int ptxstd_cvt_f32_to_e5m2_rs(const float* d_x, const uint32_t* d_rbits, uint8_t* d_out, size_t n,
+                              int relu, ptxstd_stream stream) {
+    return launch_rs<kE5M2>(d_x, d_rbits, d_out, n, relu, stream);
+}
+int ptxstd_cvt_f32_to_e2m3_rs(const float* d_x, const uint32_t* d_rbits, uint8_t* d_out, size_t n,
+                              int relu, ptxstd_stream stream) {
+    return launch_rs<kE2M3>(d_x, d_rbits, d_out, n, relu, stream);
+}
+int ptxstd_cvt_f32_to_e3m2_rs(const float* d_x, const uint32_t* d_rbits, uint8_t* d_out, size_t n,
+                              int relu, ptxstd_stream stream) {
+    return launch_rs<kE3M2>(d_x, d_rbits, d_out, n, relu, stream);
+}
+int ptxstd_cvt_f32_to_e2m1x2_rs(const float* d_x, const uint32_t* d_rbits, uint8_t* d_out,
+                                size_t n, int relu, ptxstd_stream stream) {
+    if (n & 1) return PTXSTD_EINVAL;
+    return launch_rs<kE2M1>(d_x, d_rbits, d_out, n, relu, stream);
+}
+int ptxstd_cvt_f32_to_bf16_rs(const float* d_x, const uint32_t* d_rbits, uint16_t* d_out,
+                              size_t n, int relu, int satfinite, ptxstd_stream stream) {
+    return launch_x2_rs<true>(d_x, d_rbits, d_out, n, relu, satfinite, stream);
+}
+int ptxstd_cvt_f32_to_f16_rs(const float* d_x, const uint32_t* d_rbits, uint16_t* d_out,
+                             size_t n, int relu, int satfinite, ptxstd_stream stream) {
+    return launch_x2_rs<false>(d_x, d_rbits, d_out, n, relu, satfinite, stream);
+}
+
 int ptxstd_cvt_sweep(int variant, uint64_t base, uint64_t n, uint8_t* d_out,
                      ptxstd_stream stream) {
     if (n == 0) return PTXSTD_OK;
-    if (!d_out || variant < 0 || variant > 11 || base + n > (1ull << 32) ||
-        (reinterpret_cast<uintptr_t>(d_out) & 3))
+    if (!d_out || variant < 0 || variant > 29 || base + n > (1ull << 32) ||
+        (reinterpret_cast<uintptr_t>(d_out) & 3) || (variant >= 12 && (base & 3)))
         return PTXSTD_EINVAL;
     auto s = static_cast<cudaStream_t>(stream);
     return launch([&] { sweep_kernel<<<grid_for(n / 4 + 1), 256, 0, s>>>(variant, base, n, d_out); });

@@ -74,6 +74,68 @@ __device__ __forceinline__ uint32_t e2m1x4_from_f32(float x0, float x1, float x2
     return e2m1x2_from_f32(x0, x1) | (e2m1x2_from_f32(x2, x3) << 8);
 }
 
+// ---- f32 -> narrow, stochastic rounding (.rs, sm_100a) -----------------------------------------
+// quad_from_f32_stochastic (narrow.rs:217-229): cvt.rs.satfinite{.relu}.<fmt>x4.f32 d,
+// {x3, x2, x1, x0}, rbits -- element 0 in the least significant bits of d. Each element is
+// truncated toward zero unless its random value plus the discarded mantissa bits carries; the
+// random bits of the four elements come from rbits as the reference documents per format
+// (float8.rs:59, float6.rs:61, float4.rs:60).
+#define PTXSTD_RS_X4(NAME, TY, RES, CONS)                                                        \
+    template <bool RELU = false>                                                                 \
+    __device__ __forceinline__ uint32_t NAME(float x0, float x1, float x2, float x3,             \
+                                             uint32_t rbits) {                                   \
+        RES r;                                                                                   \
+        if constexpr (RELU)                                                                      \
+            asm("cvt.rs.relu.satfinite." TY ".f32 %0, {%1, %2, %3, %4}, %5;"                     \
+                : "=" CONS(r)                                                                    \
+                : "f"(x3), "f"(x2), "f"(x1), "f"(x0), "r"(rbits));                               \
+        else                                                                                     \
+            asm("cvt.rs.satfinite." TY ".f32 %0, {%1, %2, %3, %4}, %5;"                          \
+                : "=" CONS(r)                                                                    \
+                : "f"(x3), "f"(x2), "f"(x1), "f"(x0), "r"(rbits));                               \
+        return static_cast<uint32_t>(r);                                                         \
+    }
+PTXSTD_RS_X4(e4m3x4_from_f32_rs, "e4m3x4", uint32_t, "r")
+PTXSTD_RS_X4(e5m2x4_from_f32_rs, "e5m2x4", uint32_t, "r")
+PTXSTD_RS_X4(e2m3x4_from_f32_rs, "e2m3x4", uint32_t, "r")
+PTXSTD_RS_X4(e3m2x4_from_f32_rs, "e3m2x4", uint32_t, "r")
+PTXSTD_RS_X4(e2m1x4_from_f32_rs, "e2m1x4", uint16_t, "h")  // 16 bits, element 0 in bits 0..3
+#undef PTXSTD_RS_X4
+
+// bf16x2 / f16x2::pair_from_f32_stochastic::<R, O> (bfloat16.rs:456-462, float16.rs:589-595):
+// cvt.rs{.relu}{.satfinite}.{bf16x2,f16x2}.f32 d, x1, x0, rbits; the low half of rbits serves
+// element 0.
+#define PTXSTD_RS_X2(NAME, TY)                                                                   \
+    template <bool RELU, bool SAT>                                                               \
+    __device__ __forceinline__ uint32_t NAME(float x0, float x1, uint32_t rbits) {               \
+        uint32_t r;                                                                              \
+        if constexpr (RELU && SAT)                                                               \
+            asm("cvt.rs.relu.satfinite." TY ".f32 %0, %1, %2, %3;"                               \
+                : "=r"(r) : "f"(x1), "f"(x0), "r"(rbits));                                       \
+        else if constexpr (RELU)                                                                 \
+            asm("cvt.rs.relu." TY ".f32 %0, %1, %2, %3;" : "=r"(r) : "f"(x1), "f"(x0), "r"(rbits)); \
+        else if constexpr (SAT)                                                                  \
+            asm("cvt.rs.satfinite." TY ".f32 %0, %1, %2, %3;"                                    \
+                : "=r"(r) : "f"(x1), "f"(x0), "r"(rbits));                                       \
+        else                                                                                     \
+            asm("cvt.rs." TY ".f32 %0, %1, %2, %3;" : "=r"(r) : "f"(x1), "f"(x0), "r"(rbits));    \
+        return r;                                                                                \
+    }
+PTXSTD_RS_X2(bf16x2_from_f32_rs, "bf16x2")
+PTXSTD_RS_X2(f16x2_from_f32_rs, "f16x2")
+#undef PTXSTD_RS_X2
+
+// Counter-based random bits for the seeded stochastic-rounding quantisers: output i of SplitMix64
+// (Steele, Lea and Flood, "Fast splittable pseudorandom number generators", OOPSLA 2014) started
+// at `seed`. Group g of four consecutive elements takes the low (g even) or high (g odd) word of
+// output g / 2, so an 8-element vector takes both words of one output.
+__device__ __forceinline__ uint64_t splitmix64(uint64_t seed, uint64_t i) {
+    uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
 // f8e8m0x2::pair_from_f32::<RND, OVERFLOW> (narrow.rs:600-617): RZ or RP, optional .satfinite.
 template <bool ROUND_UP, bool SATFINITE>
 __device__ __forceinline__ uint16_t ue8m0x2_from_f32(float x0, float x1) {

@@ -14,6 +14,11 @@
 //     (MXFP8) or 4-byte (NVFP4) stores, so a warp store covers 256 / 128 contiguous bytes;
 //   - consumers release a stage with one arrive per warp on its `empty` barrier.
 //
+// The stochastic-rounding forms (Mxfp8Rs, Nvfp4Rs) keep the scale recipe and round the elements
+// with cvt.rs (narrow.rs:217-229); the random bits of vector v (elements 8 v .. 8 v + 7, two
+// groups of four) are both words of SplitMix64 output v of the caller's seed, so no random bits
+// are read from memory.
+//
 // Every wait is bounded; a timeout records PTXSTD_ETIMEOUT, and the producer drains its copies
 // before the CTA exits.
 #include "common.cuh"
@@ -116,6 +121,67 @@ struct Nvfp4 {
                       << (8 * k);
         if (valid) {
             reinterpret_cast<uint32_t*>(q)[gv] = packed;
+            if ((lane & 1u) == 0) store_scale<BLOCKED>(sf, gv >> 1, sf_cols, code);
+        }
+    }
+};
+
+// Stochastic-rounding MXFP8: the same scale; elements 8 gv .. 8 gv + 3 with the low word of
+// splitmix64(seed, gv), elements + 4 .. + 7 with the high word.
+template <bool BLOCKED>
+struct Mxfp8Rs {
+    static constexpr uint32_t kLanesPerBlock = 4;
+    uint64_t seed;
+    __device__ __forceinline__ void operator()(const uint4 v, bool valid, size_t gv, uint32_t lane,
+                                               uint8_t* q, uint8_t* sf, size_t sf_cols) const {
+        uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                              dt::bf16x2_absmax_bits(v.z, v.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        const uint32_t code = dt::mxfp8_scale_code(__uint_as_float(m << 16));
+        const float inv = dt::ue8m0_inverse(code);
+        const uint64_t h = dt::splitmix64(seed, gv);
+        const uint32_t lo = dt::e4m3x4_from_f32_rs<false>(
+            __fmul_rn(dt::bf16_lo(v.x), inv), __fmul_rn(dt::bf16_hi(v.x), inv),
+            __fmul_rn(dt::bf16_lo(v.y), inv), __fmul_rn(dt::bf16_hi(v.y), inv),
+            static_cast<uint32_t>(h));
+        const uint32_t hi = dt::e4m3x4_from_f32_rs<false>(
+            __fmul_rn(dt::bf16_lo(v.z), inv), __fmul_rn(dt::bf16_hi(v.z), inv),
+            __fmul_rn(dt::bf16_lo(v.w), inv), __fmul_rn(dt::bf16_hi(v.w), inv),
+            static_cast<uint32_t>(h >> 32));
+        if (valid) {
+            reinterpret_cast<uint2*>(q)[gv] = make_uint2(lo, hi);
+            if ((lane & 3u) == 0) store_scale<BLOCKED>(sf, gv >> 2, sf_cols, code);
+        }
+    }
+};
+
+// Stochastic-rounding NVFP4: the same scale and reciprocal; elements with cvt.rs e2m1x4.
+template <bool BLOCKED>
+struct Nvfp4Rs {
+    static constexpr uint32_t kLanesPerBlock = 2;
+    float g, six_g;
+    uint64_t seed;
+    __device__ __forceinline__ void operator()(const uint4 v, bool valid, size_t gv, uint32_t lane,
+                                               uint8_t* q, uint8_t* sf, size_t sf_cols) const {
+        uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                              dt::bf16x2_absmax_bits(v.z, v.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        const float s = __fdiv_rn(__uint_as_float(m << 16), six_g);
+        const uint32_t code = dt::e4m3x2_from_f32<false>(s, 0.0f) & 0xFFu;
+        const float t = __fmul_rn(dt::e4m3_to_f32(code), g);
+        const float r = (t == 0.0f) ? 0.0f : __frcp_rn(t);
+        const uint64_t h = dt::splitmix64(seed, gv);
+        const uint32_t lo = dt::e2m1x4_from_f32_rs<false>(
+            __fmul_rn(dt::bf16_lo(v.x), r), __fmul_rn(dt::bf16_hi(v.x), r),
+            __fmul_rn(dt::bf16_lo(v.y), r), __fmul_rn(dt::bf16_hi(v.y), r),
+            static_cast<uint32_t>(h));
+        const uint32_t hi = dt::e2m1x4_from_f32_rs<false>(
+            __fmul_rn(dt::bf16_lo(v.z), r), __fmul_rn(dt::bf16_hi(v.z), r),
+            __fmul_rn(dt::bf16_lo(v.w), r), __fmul_rn(dt::bf16_hi(v.w), r),
+            static_cast<uint32_t>(h >> 32));
+        if (valid) {
+            reinterpret_cast<uint32_t*>(q)[gv] = lo | (hi << 16);
             if ((lane & 1u) == 0) store_scale<BLOCKED>(sf, gv >> 1, sf_cols, code);
         }
     }
@@ -274,6 +340,40 @@ int ptxstd_quantize_nvfp4_layout(const uint16_t* d_x, int64_t rows, int64_t cols
 int ptxstd_quantize_nvfp4(const uint16_t* d_x, int64_t rows, int64_t cols, float global_scale,
                           uint8_t* d_q, uint8_t* d_sf, ptxstd_stream stream) {
     return ptxstd_quantize_nvfp4_layout(d_x, rows, cols, global_scale, d_q, d_sf, 0, stream);
+}
+
+int ptxstd_quantize_mxfp8_rs(const uint16_t* d_x, int64_t rows, int64_t cols, uint8_t* d_q,
+                             uint8_t* d_sf, int sf_layout, uint64_t seed, ptxstd_stream stream) {
+    if (rows <= 0 || cols <= 0 || cols % 32 != 0) return PTXSTD_EINVAL;
+    if (!d_x || !d_q || !d_sf || !ptxstd::aligned16(d_x) || !ptxstd::aligned16(d_q))
+        return PTXSTD_EINVAL;
+    if (sf_layout != 0 && sf_layout != 1) return PTXSTD_EINVAL;
+    if (sf_layout == 1 && (rows % 128 != 0 || cols % 128 != 0)) return PTXSTD_EINVAL;
+    const size_t n = static_cast<size_t>(rows) * static_cast<size_t>(cols);
+    const size_t sf_cols = static_cast<size_t>(cols) / 32;
+    auto s = static_cast<cudaStream_t>(stream);
+    if (sf_layout == 1) return launch<DefaultCfg>(d_x, n, Mxfp8Rs<true>{seed}, d_q, d_sf, sf_cols, s);
+    return launch<DefaultCfg>(d_x, n, Mxfp8Rs<false>{seed}, d_q, d_sf, sf_cols, s);
+}
+
+int ptxstd_quantize_nvfp4_rs(const uint16_t* d_x, int64_t rows, int64_t cols, float global_scale,
+                             uint8_t* d_q, uint8_t* d_sf, int sf_layout, uint64_t seed,
+                             ptxstd_stream stream) {
+    if (rows <= 0 || cols <= 0 || cols % 16 != 0) return PTXSTD_EINVAL;
+    if (!(global_scale > 0.0f) || global_scale == __builtin_huge_valf()) return PTXSTD_EINVAL;
+    if (!d_x || !d_q || !d_sf || !ptxstd::aligned16(d_x) || !ptxstd::aligned16(d_q))
+        return PTXSTD_EINVAL;
+    if (sf_layout != 0 && sf_layout != 1) return PTXSTD_EINVAL;
+    if (sf_layout == 1 && (rows % 128 != 0 || cols % 64 != 0)) return PTXSTD_EINVAL;
+    const size_t n = static_cast<size_t>(rows) * static_cast<size_t>(cols);
+    const size_t sf_cols = static_cast<size_t>(cols) / 16;
+    auto s = static_cast<cudaStream_t>(stream);
+    const float six_g = 6.0f * global_scale;
+    if (sf_layout == 1)
+        return launch<DefaultCfg>(d_x, n, Nvfp4Rs<true>{global_scale, six_g, seed}, d_q, d_sf,
+                                  sf_cols, s);
+    return launch<DefaultCfg>(d_x, n, Nvfp4Rs<false>{global_scale, six_g, seed}, d_q, d_sf,
+                              sf_cols, s);
 }
 
 }  // extern "C"

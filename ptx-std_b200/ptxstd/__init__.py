@@ -53,6 +53,20 @@ _SIGS = {
     "ptxstd_cvt_e2m3_to_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "ptxstd_cvt_e3m2_to_f32": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "ptxstd_cvt_sweep": (C.c_int, [C.c_int, C.c_uint64, C.c_uint64, C.c_void_p, C.c_void_p]),
+    "ptxstd_cvt_f32_to_e4m3_rs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                            C.c_int, C.c_void_p]),
+    "ptxstd_cvt_f32_to_e5m2_rs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                            C.c_int, C.c_void_p]),
+    "ptxstd_cvt_f32_to_e2m3_rs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                            C.c_int, C.c_void_p]),
+    "ptxstd_cvt_f32_to_e3m2_rs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                            C.c_int, C.c_void_p]),
+    "ptxstd_cvt_f32_to_e2m1x2_rs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                              C.c_int, C.c_void_p]),
+    "ptxstd_cvt_f32_to_bf16_rs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                            C.c_int, C.c_int, C.c_void_p]),
+    "ptxstd_cvt_f32_to_f16_rs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                           C.c_int, C.c_int, C.c_void_p]),
     "ptxstd_quantize_mxfp8": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p,
                                         C.c_void_p, C.c_void_p]),
     "ptxstd_quantize_nvfp4": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_float, C.c_void_p,
@@ -61,6 +75,11 @@ _SIGS = {
                                                C.c_void_p, C.c_int, C.c_void_p]),
     "ptxstd_quantize_nvfp4_layout": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_float,
                                                C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
+    "ptxstd_quantize_mxfp8_rs": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p,
+                                           C.c_void_p, C.c_int, C.c_uint64, C.c_void_p]),
+    "ptxstd_quantize_nvfp4_rs": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_float,
+                                           C.c_void_p, C.c_void_p, C.c_int, C.c_uint64,
+                                           C.c_void_p]),
     "ptxstd_gemm_fp8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_float, C.c_float, C.c_void_p,
                                   C.c_int64, C.c_int64, C.c_int64, C.c_void_p]),
     "ptxstd_gemm_nvfp4": (C.c_int, [C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p,

@@ -9,6 +9,10 @@ kernels with the same `cvt` instructions the reference's pair methods wrap:
 - ``to_f32(fmt, codes)``: exact decode through f16 (narrow.rs:292-299).
 - ``ue8m0_from_f32(x, round_up, satfinite)``: f8e8m0::from_f32::<RND, OVERFLOW>
   (narrow.rs:600-617); ``ue8m0_to_f32``: through bf16 (narrow.rs:683-690).
+- ``from_f32_stochastic(fmt, x, rbits, relu)``: Vector<fmt, N>::from_f32_stochastic::<RELU>
+  (narrow.rs:494-505), one rbits word per group of four elements; ``bf16_from_f32_stochastic``
+  and ``f16_from_f32_stochastic``: bf16xN / f16xN::from_f32_stochastic::<R, O>
+  (bfloat16.rs:572-598, float16.rs:740-766), one word per pair.
 """
 
 from __future__ import annotations
@@ -54,6 +58,56 @@ def to_f32(fmt: str, codes, stream=None):
     return out
 
 
+_ENC_RS = {E4M3: "ptxstd_cvt_f32_to_e4m3_rs", E5M2: "ptxstd_cvt_f32_to_e5m2_rs",
+           E2M1: "ptxstd_cvt_f32_to_e2m1x2_rs", E2M3: "ptxstd_cvt_f32_to_e2m3_rs",
+           E3M2: "ptxstd_cvt_f32_to_e3m2_rs"}
+
+
+def _rbits(rbits, need: int):
+    torch = _torch()
+    if rbits.dtype not in (torch.int32, torch.uint32) or rbits.numel() < need:
+        raise ValueError(f"rbits must be 32-bit words, at least {need} of them")
+    return rbits.contiguous()
+
+
+def from_f32_stochastic(fmt: str, x, rbits, relu: bool = False, stream=None):
+    """Stochastic rounding: elements 4g .. 4g+3 of x with rbits[g] (32-bit words)."""
+    torch = _torch()
+    if x.dtype != torch.float32:
+        raise TypeError("expected float32")
+    x = x.contiguous()
+    n = x.numel()
+    rb = _rbits(rbits, (n + 3) // 4)
+    out = torch.empty(n // 2 if fmt == E2M1 else n, dtype=torch.uint8, device=x.device)
+    check(getattr(lib(), _ENC_RS[fmt])(_dev(x), _dev(rb), _dev(out), n, int(relu),
+                                       _stream(stream)), f"from_f32_stochastic({fmt})")
+    return out
+
+
+def _x2_stochastic(name, x, rbits, relu, satfinite, stream):
+    torch = _torch()
+    if x.dtype != torch.float32:
+        raise TypeError("expected float32")
+    x = x.contiguous()
+    n = x.numel()
+    rb = _rbits(rbits, (n + 1) // 2)
+    out = torch.empty(n, dtype=torch.int16, device=x.device)
+    check(getattr(lib(), name)(_dev(x), _dev(rb), _dev(out), n, int(relu), int(satfinite),
+                               _stream(stream)), name)
+    return out
+
+
+def bf16_from_f32_stochastic(x, rbits, relu: bool = False, satfinite: bool = False,
+                             stream=None):
+    """bf16 bit patterns (int16) of x rounded stochastically, elements 2p, 2p+1 with rbits[p]."""
+    return _x2_stochastic("ptxstd_cvt_f32_to_bf16_rs", x, rbits, relu, satfinite, stream)
+
+
+def f16_from_f32_stochastic(x, rbits, relu: bool = False, satfinite: bool = False, stream=None):
+    """f16 bit patterns (int16) of x rounded stochastically, elements 2p, 2p+1 with rbits[p]."""
+    return _x2_stochastic("ptxstd_cvt_f32_to_f16_rs", x, rbits, relu, satfinite, stream)
+
+
 def ue8m0_from_f32(x, round_up: bool = False, satfinite: bool = True, stream=None):
     torch = _torch()
     x = x.contiguous()
@@ -72,10 +126,17 @@ def ue8m0_to_f32(codes, stream=None):
     return out
 
 
+def sweep_width(variant: int) -> int:
+    """Bytes per input of a sweep variant: 2 for the bf16/f16 stochastic forms (22..29)."""
+    return 2 if variant >= 22 else 1
+
+
 def sweep(variant: int, base: int, n: int, out=None, stream=None):
     """Codes of the f32 bit patterns base .. base+n-1 (see ptxstd_cvt_sweep)."""
     torch = _torch()
     if out is None:
-        out = torch.empty(n, dtype=torch.uint8, device="cuda")
+        out = torch.empty(n * sweep_width(variant), dtype=torch.uint8, device="cuda")
+    elif out.numel() < n * sweep_width(variant):
+        raise ValueError("sweep output too small")
     check(lib().ptxstd_cvt_sweep(variant, base, n, _dev(out), _stream(stream)), "sweep")
     return out

@@ -7,10 +7,12 @@ from . import _dev, _stream, _torch, check, lib
 SF_ROWMAJOR, SF_BLOCKED = 0, 1
 
 
-def quantize_mxfp8(x, sf_layout: int = SF_ROWMAJOR, out=None, stream=None):
+def quantize_mxfp8(x, sf_layout: int = SF_ROWMAJOR, out=None, stream=None, seed=None):
     """bf16 [rows, cols] -> (E4M3 [rows, cols] uint8, UE8M0 scales uint8).
 
     Scales are [rows, cols/32] row-major (sf_layout 0) or the blocked 128x4 GEMM layout (1).
+    With a `seed`, the elements are rounded stochastically (ptxstd_quantize_mxfp8_rs: random bits
+    from SplitMix64 started at the seed, group of four elements i // 4).
     """
     torch = _torch()
     if x.dtype != torch.bfloat16 or x.dim() != 2:
@@ -21,8 +23,13 @@ def quantize_mxfp8(x, sf_layout: int = SF_ROWMAJOR, out=None, stream=None):
         sf = torch.empty((rows, cols // 32), dtype=torch.uint8, device=x.device)
     else:
         q, sf = out
-    check(lib().ptxstd_quantize_mxfp8_layout(_dev(x), rows, cols, _dev(q), _dev(sf), sf_layout,
-                                             _stream(stream)), "quantize_mxfp8")
+    if seed is None:
+        check(lib().ptxstd_quantize_mxfp8_layout(_dev(x), rows, cols, _dev(q), _dev(sf),
+                                                 sf_layout, _stream(stream)), "quantize_mxfp8")
+    else:
+        check(lib().ptxstd_quantize_mxfp8_rs(_dev(x), rows, cols, _dev(q), _dev(sf), sf_layout,
+                                             int(seed) & (2**64 - 1), _stream(stream)),
+              "quantize_mxfp8(seed)")
     return q, sf
 
 
@@ -113,8 +120,10 @@ def gemm_decode(x, w, sfw, gw: float, out=None, workspace=None, stream=None):
 
 
 def quantize_nvfp4(x, global_scale: float, sf_layout: int = SF_ROWMAJOR, out=None,
-                   stream=None):
-    """bf16 [rows, cols] -> (E2M1x2 [rows, cols/2] uint8, E4M3 scales per 16 uint8)."""
+                   stream=None, seed=None):
+    """bf16 [rows, cols] -> (E2M1x2 [rows, cols/2] uint8, E4M3 scales per 16 uint8).
+
+    With a `seed`, the elements are rounded stochastically (ptxstd_quantize_nvfp4_rs)."""
     torch = _torch()
     if x.dtype != torch.bfloat16 or x.dim() != 2:
         raise TypeError("expected a 2-D bfloat16 tensor")
@@ -124,7 +133,12 @@ def quantize_nvfp4(x, global_scale: float, sf_layout: int = SF_ROWMAJOR, out=Non
         sf = torch.empty((rows, cols // 16), dtype=torch.uint8, device=x.device)
     else:
         q, sf = out
-    check(lib().ptxstd_quantize_nvfp4_layout(_dev(x), rows, cols, float(global_scale), _dev(q),
-                                             _dev(sf), sf_layout, _stream(stream)),
-          "quantize_nvfp4")
+    if seed is None:
+        check(lib().ptxstd_quantize_nvfp4_layout(_dev(x), rows, cols, float(global_scale),
+                                                 _dev(q), _dev(sf), sf_layout, _stream(stream)),
+              "quantize_nvfp4")
+    else:
+        check(lib().ptxstd_quantize_nvfp4_rs(_dev(x), rows, cols, float(global_scale), _dev(q),
+                                             _dev(sf), sf_layout, int(seed) & (2**64 - 1),
+                                             _stream(stream)), "quantize_nvfp4(seed)")
     return q, sf

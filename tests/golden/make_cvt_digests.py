@@ -5,9 +5,10 @@ The reference's encoders are the hardware `cvt` instructions (src/data_types/nar
 tests/test_oracle.py recomputes the oracle's digests and compares.
 
 For each variant (e4m3, e5m2, e2m1 as one nibble per byte, the three .relu forms, ue8m0 RZ and
-RP with .satfinite, the FP6 formats e2m3 and e3m2 with and without .relu), the codes of inputs
-[i * 2^24, (i + 1) * 2^24) are hashed as: FNV-1a 64 of every 2^16-byte piece, then FNV-1a 64 over
-those 256 digests (little-endian).
+RP with .satfinite, the FP6 formats e2m3 and e3m2 with and without .relu, and the
+stochastic-rounding forms of ptxstd_cvt_sweep 12..29, bf16/f16 with two bytes per input), the
+codes of inputs [i * 2^24, (i + 1) * 2^24) are hashed as: FNV-1a 64 of every 2^16-byte piece,
+then FNV-1a 64 over those digests (little-endian).
 
     python tests/golden/make_cvt_digests.py --out tests/golden/cvt_sweep_digests.json
     python tests/golden/make_cvt_digests.py --variants e2m3 e3m2   # add to an existing file
@@ -39,8 +40,8 @@ def main() -> int:
 
     chunk = 1 << 24
     step = 1 << 28
-    dev = torch.empty(step, dtype=torch.uint8, device="cuda")
-    host = torch.empty(step, dtype=torch.uint8, pin_memory=True)
+    dev = torch.empty(2 * step, dtype=torch.uint8, device="cuda")
+    host = torch.empty(2 * step, dtype=torch.uint8, pin_memory=True)
     out = {"chunk": chunk, "scheme": "fnv1a64 of 2^16-byte pieces, then fnv1a64 of the digests",
            "device": torch.cuda.get_device_name(), "variants": {}}
     if a.variants and os.path.exists(a.out):
@@ -50,12 +51,13 @@ def main() -> int:
         if a.variants and name not in a.variants:
             continue
         digs = []
+        w = O.sweep_width(v)
         for base in range(0, 1 << 32, step):
             dt.sweep(v, base, step, out=dev)
             host.copy_(dev)
-            h = host.numpy()
+            h = host.numpy()[: w * step]
             for k in range(step // chunk):
-                digs.append(f"{O.digest_bytes(h[k * chunk:(k + 1) * chunk]):016x}")
+                digs.append(f"{O.digest_bytes(h[k * chunk * w:(k + 1) * chunk * w]):016x}")
         out["variants"][name] = digs
         print(name, digs[0], f"{time.time() - t0:.1f}s", flush=True)
     with open(a.out, "w") as f:

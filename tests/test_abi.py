@@ -55,5 +55,11 @@ def test_host_validation_without_gpu(ptxstd_lib):
     assert L.ptxstd_quantize_nvfp4(None, 128, 64, 0.0, None, None, None) == EINVAL
     assert L.ptxstd_quantize_nvfp4_layout(16, 128, 64, 1.0, 16, 16, 2, None) == EINVAL
     assert L.ptxstd_cvt_f32_to_e2m1x2(16, 16, 3, 0, None) == EINVAL
-    assert L.ptxstd_cvt_sweep(12, 0, 16, 16, None) == EINVAL
+    assert L.ptxstd_cvt_sweep(30, 0, 16, 16, None) == EINVAL
+    assert L.ptxstd_cvt_sweep(12, 2, 16, 16, None) == EINVAL      # stochastic: base % 4
+    assert L.ptxstd_cvt_f32_to_e2m1x2_rs(16, 16, 16, 3, 0, None) == EINVAL   # odd n
+    assert L.ptxstd_cvt_f32_to_e4m3_rs(8, 16, 16, 4, 0, None) == EINVAL      # x not 16-aligned
+    assert L.ptxstd_cvt_f32_to_bf16_rs(16, 2, 16, 4, 0, 0, None) == EINVAL   # rbits misaligned
+    assert L.ptxstd_quantize_mxfp8_rs(16, 128, 96 + 1, 16, 16, 0, 1, None) == EINVAL
+    assert L.ptxstd_quantize_nvfp4_rs(16, 128, 64, 0.0, 16, 16, 0, 1, None) == EINVAL
     assert L.ptxstd_cvt_sweep(0, (1 << 32) - 8, 16, 16, None) == EINVAL

@@ -4,8 +4,11 @@
 - the narrow-float round-trip set (2^24 seeded values with specials) encoded to E4M3, E5M2,
   E2M1x2, E2M3 and E3M2 (RN .satfinite, with and without .relu) and decoded back matches the
   oracle bit for bit;
-- all 2^32 f32 bit patterns, through the device's `cvt` for the twelve encode variants, match the
-  oracle (the exhaustive pin of the oracle against the instructions the reference wraps).
+- all 2^32 f32 bit patterns, through the device's `cvt` for the twelve round-to-nearest variants
+  and the eighteen stochastic-rounding forms (cvt.rs with SplitMix64 bits per group), match the
+  oracle (the exhaustive pin of the oracle against the instructions the reference wraps);
+- the element-wise stochastic entry points (caller-supplied rbits, ragged lengths whose last
+  group is zero-padded, .relu, .satfinite) match the oracle bit for bit.
 """
 
 import numpy as np
@@ -81,22 +84,90 @@ def test_ue8m0_set(cuda, oracle):
 
 
 def test_exhaustive_all_f32(cuda, oracle):
-    """All 2^32 inputs, 12 variants, in 2^28 chunks: zero mismatches."""
+    """All 2^32 inputs, 30 variants, in 2^28 chunks: zero mismatches."""
     import ptxstd.data_types as dt
     torch = cuda
     chunk = 1 << 28
-    dev = torch.empty(chunk, dtype=torch.uint8, device="cuda")
-    host = torch.empty(chunk, dtype=torch.uint8, pin_memory=True)
+    dev = torch.empty(2 * chunk, dtype=torch.uint8, device="cuda")
+    host = torch.empty(2 * chunk, dtype=torch.uint8, pin_memory=True)
     total_bad = {}
     for v in range(len(oracle.VARIANT_NAMES)):
         bad = 0
         report = []
+        w = oracle.sweep_width(v)
         for base in range(0, 1 << 32, chunk):
             dt.sweep(v, base, chunk, out=dev)
             host.copy_(dev)
-            n, rep = oracle.sweep_compare(v, base, host.numpy(), max_report=8)
+            n, rep = oracle.sweep_compare(v, base, host.numpy()[: w * chunk], max_report=8)
             bad += n
             report += [tuple(int(t) for t in r) for r in rep[:4]]
         total_bad[oracle.VARIANT_NAMES[v]] = (bad, [(hex(a), hex(b), hex(c))
                                                     for a, b, c in report[:8]])
     assert all(b == 0 for b, _ in total_bad.values()), total_bad
+
+
+# ---- stochastic rounding through the element-wise entry points -----------------------------------
+
+def _rs_inputs(n, seed):
+    rng = np.random.default_rng(seed)
+    e = rng.integers(-30, 20, n)
+    m = rng.integers(0, 1 << 23, n)
+    bits = ((rng.integers(0, 2, n) << 31) | ((e + 127) << 23) | m).astype(np.uint32)
+    sp = np.array([0, 0x80000000, 0x7F800000, 0xFF800000, 0x7FC00000, 3], dtype=np.uint32)
+    bits[: min(n, sp.size)] = sp[:n]
+    rb = rng.integers(0, 1 << 32, (n + 3) // 4, dtype=np.uint64).astype(np.uint32)
+    return bits.view(np.float32), rb
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2", "e2m3", "e3m2", "e2m1"])
+@pytest.mark.parametrize("relu", [False, True])
+def test_stochastic_vs_oracle(cuda, oracle, fmt, relu):
+    import ptxstd.data_types as dt
+    torch = cuda
+    ofmt = {"e4m3": oracle.E4M3, "e5m2": oracle.E5M2, "e2m3": oracle.E2M3, "e3m2": oracle.E3M2,
+            "e2m1": oracle.E2M1}[fmt]
+    for n in ((1 << 20), (1 << 20) + 2) + (() if fmt == "e2m1" else ((1 << 20) + 1, 7, 1)):
+        x, rb = _rs_inputs(n, n)
+        got = _to_np(dt.from_f32_stochastic(fmt, torch.from_numpy(x).cuda(),
+                                            torch.from_numpy(rb.view(np.int32)).cuda(), relu))
+        want = oracle.encode_rs(ofmt, x, rb, relu)
+        bad = np.nonzero(got != want)[0]
+        assert bad.size == 0, (n, bad[:4], got[bad[:4]], want[bad[:4]])
+
+
+@pytest.mark.parametrize("kind", ["bf16", "f16"])
+@pytest.mark.parametrize("relu", [False, True])
+@pytest.mark.parametrize("sat", [False, True])
+def test_stochastic_x2_vs_oracle(cuda, oracle, kind, relu, sat):
+    import ptxstd.data_types as dt
+    torch = cuda
+    dev_fn = dt.bf16_from_f32_stochastic if kind == "bf16" else dt.f16_from_f32_stochastic
+    ora_fn = oracle.bf16_rs if kind == "bf16" else oracle.f16_rs
+    for n in ((1 << 20), (1 << 20) + 1, 3):
+        x, rb = _rs_inputs(n, 7 * n)
+        rb = np.concatenate([rb, rb])[: (n + 1) // 2]
+        got = _to_np(dev_fn(torch.from_numpy(x).cuda(), torch.from_numpy(rb.view(np.int32)).cuda(),
+                            relu, sat)).view(np.uint16)
+        want = ora_fn(x, rb, relu, sat)
+        bad = np.nonzero(got != want)[0]
+        assert bad.size == 0, (n, bad[:4], got[bad[:4]], want[bad[:4]])
+
+
+def test_stochastic_unbiased_on_device(cuda):
+    """Mean of the device's stochastic E4M3 codes of one value over 2^22 random words equals the
+    value within 5 standard errors, while RN is biased by its rounding error."""
+    import ptxstd.data_types as dt
+    torch = cuda
+    n = 1 << 24
+    v = 1.1  # between the E4M3 codes 1.0 and 1.125
+    x = torch.full((n,), v, dtype=torch.float32, device="cuda")
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    rb = torch.randint(-(2 ** 31), 2 ** 31 - 1, (n // 4,), dtype=torch.int32, device="cuda",
+                       generator=g)
+    q = dt.to_f32("e4m3", dt.from_f32_stochastic("e4m3", x, rb)).double()
+    mean, se = q.mean().item(), q.std().item() / n ** 0.5
+    exact = float(np.float32(v))
+    assert abs(mean - exact) < 5 * se
+    rn = dt.to_f32("e4m3", dt.from_f32("e4m3", x[:4])).double()[0].item()
+    assert abs(rn - exact) > 50 * se

@@ -6,7 +6,11 @@
 - encode rounding: hand-computed ties and .satfinite boundaries, a second independent (float64)
   formulation of RN, decode->encode round trips;
 - the hardware pin: digests of the B200's own `cvt` outputs over all 2^32 f32 patterns
-  (tests/golden/cvt_sweep_digests.json, written by tests/golden/make_cvt_digests.py on a B200).
+  (tests/golden/cvt_sweep_digests.json, written by tests/golden/make_cvt_digests.py on a B200);
+- stochastic rounding (cvt.rs): the random-bit assignment the reference documents, the carry
+  rule's limits (all-zero bits truncate, all-one bits round up anything inexact), unbiasedness,
+  SplitMix64's published outputs, and the B200's own codes for 18 forms
+  (tests/golden/cvt_rs_vectors.json, written by tests/golden/make_cvt_rs_vectors.py).
 """
 
 import json
@@ -285,7 +289,7 @@ DIGESTS = os.path.join(GOLDEN, "cvt_sweep_digests.json")
 
 
 @pytest.mark.skipif(not os.path.exists(DIGESTS), reason="no hardware digests recorded yet")
-@pytest.mark.parametrize("variant", range(12))
+@pytest.mark.parametrize("variant", range(30))
 def test_oracle_matches_hardware_digests(oracle, variant):
     """The oracle's codes for all 2^32 f32 inputs hash to the digests of the B200's own `cvt`
     outputs (the reference's encoders are those instructions). A few chunks are checked by
@@ -301,3 +305,140 @@ def test_oracle_matches_hardware_digests(oracle, variant):
     for i in idx:
         got = oracle.sweep_digest(variant, i * chunk, chunk)
         assert f"{got:016x}" == digs[i], (variant, i)
+
+
+# ---- stochastic rounding -------------------------------------------------------------------------
+
+RS_FORMATS = {"e4m3": 0, "e5m2": 1, "e2m1": 2, "e2m3": 3, "e3m2": 4}
+
+
+def test_rs_random_bit_assignment(oracle):
+    """Which rbits bits feed which element (float8.rs:59, float6.rs:61, float4.rs:60,
+    bfloat16.rs:576-579, float16.rs:742-746). FP8/FP6: a bit of the lower half reaches elements 0
+    and 1 (the even one reads the half most significant bit first, the odd one bit-reversed), a
+    bit of the upper half elements 2 and 3; E2M1: the low bytes of both halves feed 0 and 1, the
+    high bytes 2 and 3; bf16: one element per half."""
+    L = oracle.lib()
+    for kind, per, owners in [
+        (oracle.RS_X4, 4, lambda b: [0, 1] if b < 16 else [2, 3]),
+        (oracle.RS_E2M1, 4, lambda b: [0, 1] if (b % 16) < 8 else [2, 3]),
+        (oracle.RS_BF16, 2, lambda b: [0] if b < 16 else [1]),
+    ]:
+        for b in range(32):
+            hit = [k for k in range(per) if L.ptxo_rs_random(kind, 1 << b, k) != 0]
+            assert hit == owners(b), (kind, b, hit)
+    # the even element weights bit 15 (bit 31) most, the odd one bit 0 (bit 16)
+    assert L.ptxo_rs_random(oracle.RS_X4, 1 << 15, 0) == 0x8000
+    assert L.ptxo_rs_random(oracle.RS_X4, 1, 1) == 0x8000
+    assert L.ptxo_rs_random(oracle.RS_X4, 1 << 16, 3) == 0x8000
+    # f16 uses only the 13 low bits of each half
+    for b in range(32):
+        hit = [k for k in range(2) if L.ptxo_rs_random(oracle.RS_F16, 1 << b, k) != 0]
+        assert hit == ([0] if b < 13 else [1] if 16 <= b < 29 else []), (b, hit)
+
+
+# (mantissa bits, minimum normal exponent, largest finite value) of the narrow formats
+RS_PARAMS = {"e4m3": (3, -6, 448.0), "e5m2": (2, -14, 57344.0), "e2m1": (1, 0, 6.0),
+             "e2m3": (3, 0, 7.5), "e3m2": (2, -2, 28.0)}
+
+
+def _rs_f64(fmt, x, r):
+    """Second, float64 formulation of the stochastic rounding of finite x with w = 16 random
+    bits r: quantum 2^(max(e, emin) - M); up when floor(frac * 2^16) + r >= 2^16; .satfinite."""
+    M, emin, mx = RS_PARAMS[fmt]
+    a = np.abs(x.astype(np.float64))
+    _, ex = np.frexp(np.where(a > 0, a, 1.0))
+    q = np.ldexp(1.0, np.maximum(ex - 1, emin) - M)
+    t = np.floor(a / q)
+    up = np.floor((a / q - t) * 65536.0) + r >= 65536
+    v = np.minimum((t + up) * q, mx)
+    return np.where(np.signbit(x), -v, v)
+
+
+@pytest.mark.parametrize("fmt", list(RS_FORMATS))
+def test_rs_matches_float64_formulation(oracle, fmt):
+    """The integer restatement equals an independent float64 one on random finite inputs and
+    random bits; with all-zero bits it truncates toward zero."""
+    f = RS_FORMATS[fmt]
+    rng = np.random.default_rng(5)
+    n = 1 << 14
+    x = (rng.standard_normal(n) * np.exp2(rng.integers(-12, 8, n))).astype(np.float32)
+    rb = rng.integers(0, 1 << 32, n // 4, dtype=np.uint64).astype(np.uint32)
+    kind = oracle.RS_E2M1 if f == oracle.E2M1 else oracle.RS_X4
+    L = oracle.lib()
+    r = np.array([L.ptxo_rs_random(kind, int(rb[i // 4]), i % 4) for i in range(n)])
+    got = oracle.decode(f, oracle.encode_rs(f, x, rb)).astype(np.float64)
+    assert np.array_equal(got, _rs_f64(fmt, x, r))
+    zero = oracle.decode(f, oracle.encode_rs(f, x, np.zeros(n // 4, np.uint32))).astype(np.float64)
+    assert np.all(np.abs(zero) <= np.abs(x.astype(np.float64)))
+    assert np.array_equal(zero, _rs_f64(fmt, x, np.zeros(n)))
+
+
+def test_rs_unbiased(oracle):
+    """The mean of the stochastic E4M3 and bf16 roundings of one value over random bits is the
+    value (the point of .rs), within 5 standard errors."""
+    rng = np.random.default_rng(7)
+    n = 1 << 16
+    rb = rng.integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32)
+    for v in (1.1, -3.3, 0.0123, 300.7):
+        x = np.full(4 * n, v, np.float32)
+        q = oracle.decode(0, oracle.encode_rs(0, x, rb)).astype(np.float64)
+        assert abs(q.mean() - float(np.float32(v))) < 5 * q.std() / math.sqrt(q.size) + 1e-12, v
+        h = oracle.bf16_rs(x[: 2 * n], rb)
+        qb = oracle.bf16_to_f32(h).astype(np.float64)
+        assert abs(qb.mean() - float(np.float32(v))) < 5 * qb.std() / math.sqrt(qb.size) + 1e-12
+
+
+def test_splitmix64_published_outputs(oracle):
+    """SplitMix64 seeded with 0 (Steele, Lea and Flood 2014; the reference generator's first
+    outputs), and the vectorised numpy copy used by the tests."""
+    L = oracle.lib()
+    assert L.ptxo_splitmix64(0, 0) == 0xE220A8397B1DCDAF
+    assert L.ptxo_splitmix64(0, 1) == 0x6E789E6AA1B965F4
+    words = oracle.sr_rbits(0x1234, 10)
+    for g in range(10):
+        assert int(words[g]) == L.ptxo_sr_rbits(0x1234, g)
+
+
+RS_VECTORS = os.path.join(GOLDEN, "cvt_rs_vectors.json")
+
+
+@pytest.mark.skipif(not os.path.exists(RS_VECTORS), reason="no hardware vectors recorded yet")
+def test_rs_hardware_vectors(oracle):
+    """The oracle reproduces the B200's cvt.rs codes for every recorded form."""
+    d = json.load(open(RS_VECTORS))["forms"]
+    assert len(d) == 18
+    for key, rec in d.items():
+        x = np.array([int(v, 16) for v in rec["x"]], dtype=np.uint32).view(np.float32)
+        rb = np.array([int(v, 16) for v in rec["rbits"]], dtype=np.uint32)
+        relu, sat = "_relu" in key, key.endswith("_sat")
+        name = key.split("_")[0]
+        hw = bytes.fromhex(rec["codes"])
+        if name in ("bf16", "f16"):
+            got = (oracle.bf16_rs if name == "bf16" else oracle.f16_rs)(x, rb, relu, sat)
+            want = np.frombuffer(hw, dtype=np.uint16)
+        else:
+            got = oracle.encode_rs(RS_FORMATS[name], x, rb, relu)
+            want = np.frombuffer(hw, dtype=np.uint8)
+        bad = np.nonzero(got != want)[0]
+        assert bad.size == 0, (key, bad[:4], got[bad[:4]], want[bad[:4]])
+
+
+def test_rs_quantize_keeps_scales(oracle):
+    """The stochastic quantisers keep the round-to-nearest scales; every element is within one
+    code step of the RN element, and one seed always gives the same codes."""
+    from ptxstd import workloads
+    xb = workloads.normal_bf16(64, 512, std=1.0, seed=3)
+    q0, s0 = oracle.quantize_mxfp8(xb)
+    q1, s1 = oracle.quantize_mxfp8_rs(xb, 99)
+    q2, _ = oracle.quantize_mxfp8_rs(xb, 99)
+    q3, _ = oracle.quantize_mxfp8_rs(xb, 100)
+    assert np.array_equal(s0, s1) and np.array_equal(q1, q2) and not np.array_equal(q1, q3)
+    d0 = oracle.decode(0, q0.ravel()).astype(np.float64)
+    d1 = oracle.decode(0, q1.ravel()).astype(np.float64)
+    step = np.maximum(np.abs(d0) * 2.0 ** -3, 2.0 ** -9) * 1.0001  # E4M3 spacing
+    assert np.all(np.abs(d1 - d0) <= step)
+    g = 0.01
+    n0, t0 = oracle.quantize_nvfp4(xb, g)
+    n1, t1 = oracle.quantize_nvfp4_rs(xb, g, 5)
+    assert np.array_equal(t0, t1)

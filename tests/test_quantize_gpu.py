@@ -106,6 +106,48 @@ def test_nvfp4_edges(cuda, oracle, shape):
         _check_nvfp4(cuda, oracle, xb, g, 0)
 
 
+def _check_rs(torch, oracle, xb, layout, seed, fmt, g=None):
+    import ptxstd
+    rows, cols = xb.shape
+    xt = torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16)
+    if fmt == "mxfp8":
+        q, sf = ptxstd.quantize_mxfp8(xt, sf_layout=layout, seed=seed)
+        wq, wsf = oracle.quantize_mxfp8_rs(xb, seed)
+        per = 32
+    else:
+        q, sf = ptxstd.quantize_nvfp4(xt, g, sf_layout=layout, seed=seed)
+        wq, wsf = oracle.quantize_nvfp4_rs(xb, g, seed)
+        per = 16
+    gq, gsf = q.cpu().numpy(), sf.cpu().numpy()
+    if layout == 1:
+        gsf = _blocked_to_rowmajor(gsf, rows, cols // per)
+    bad = np.argwhere(gq != wq)
+    assert bad.shape[0] == 0, (seed, bad[:8])
+    assert np.array_equal(gsf, wsf)
+    return gq
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+def test_stochastic_quantize_vs_oracle(cuda, oracle, layout):
+    """Seeded stochastic rounding (SplitMix64 bits per group of four): payload and scales
+    bit-exact against the oracle, for edge-case matrices and several seeds; the scales equal the
+    round-to-nearest scales; another seed changes the codes."""
+    torch = cuda
+    xb = _edge_matrix(256, 1024, 21)
+    a = _check_rs(torch, oracle, xb, layout, 0, "mxfp8")
+    b = _check_rs(torch, oracle, xb, layout, 2 ** 64 - 1, "mxfp8")
+    assert not np.array_equal(a, b)
+    _check_rs(torch, oracle, xb, layout, 12345, "nvfp4", g=0.05)
+    _check_rs(torch, oracle, xb, layout, 7, "nvfp4", g=3.0e-4)
+
+
+def test_stochastic_quantize_full_size(cuda, oracle):
+    """The MXFP8 workload (8192 x 8192) with stochastic rounding, bit-exact."""
+    from ptxstd import workloads
+    xb = workloads.mxfp8_activation(8192, 8192)
+    _check_rs(cuda, oracle, xb, 1, 0xC0FFEE, "mxfp8")
+
+
 def test_invalid_arguments(cuda):
     import ptxstd
     torch = cuda
