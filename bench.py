@@ -388,6 +388,70 @@ class Mxfp8Gemm(Fp8Gemm):
         return 1
 
 
+class Mxfp8SparseGemm(Fp8Gemm):
+    """2:4-sparse MXFP8: A [8192, 8192] pruned to 2:4 (vals [8192, 4096] + metadata [8192, 1024]) x
+    dense B [8192, 8192], UE8M0 scales per 64 logical K -> bf16 C. TFLOP/s count the logical
+    (dense-equivalent) 2 M N K; the roofline peak is 2x the dense MXFP8 figure (2:4 sparsity
+    halves the tensor-core work per logical FLOP)."""
+
+    name = "mxfp8_gemm_sparse"
+    dtype = "2:4 e4m3 x e4m3 (ue8m0/64 scales) -> f32 acc -> bf16"
+    kernel = "gemm_mxfp8_sparse_pair_kernel"
+    peak_ratio_to_bf16 = 4.0
+    peak_note = "2:4-sparse MXFP8 = 2x dense MXFP8 = 4x bf16, logical FLOPs"
+
+    def __init__(self, world: int = 1):
+        super().__init__(world)
+        self.in_bytes = self.M * self.K // 2 + self.M * self.K // 8 + self.N * self.K + \
+            (self.M + self.N) * self.K // 64
+        self.bytes = self.in_bytes + self.out_bytes
+        self.config = {"workload": "mxfp8_gemm_sparse 2:4 e4m3 x e4m3, ue8m0/64, "
+                       "8192x8192x8192 (logical K) -> bf16", "M": self.M, "N": self.N,
+                       "K": self.K, "l2": "operands 104 MiB + output 128 MiB per step (> L2)"}
+
+    def host_input(self):
+        if getattr(self, "_sp", None) is None:
+            import numpy as np
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            a, b = super().host_input()
+            rng = np.random.default_rng(34)
+            self._sp = (a, b, rng.integers(122, 133, self.M * self.K // 64, dtype=np.uint8),
+                        rng.integers(122, 133, self.N * self.K // 64, dtype=np.uint8))
+        return self._sp
+
+    def setup(self, torch, sp):
+        import ptxstd
+        super().setup(torch, sp[:2])
+        # prune A on the device (the library's own 2:4 pruning)
+        self.vals, self.meta = ptxstd.prune_24(self.a)
+        self.vals_host = self.vals.cpu().pin_memory()
+        self.meta_host = self.meta.cpu().pin_memory()
+        self.sfa_host = torch.from_numpy(sp[2]).pin_memory()
+        self.sfb_host = torch.from_numpy(sp[3]).pin_memory()
+        self.sfa = self.sfa_host.cuda()
+        self.sfb = self.sfb_host.cuda()
+
+    def step(self, i):
+        import ptxstd
+        ptxstd.gemm_mxfp8_sparse(self.vals, self.meta, self.sfa, self.b, self.sfb, out=self.c)
+        return 1
+
+    def e2e_step(self, i):
+        import ptxstd
+        for dst, src in ((self.vals, self.vals_host), (self.meta, self.meta_host),
+                         (self.b, self.b_host), (self.sfa, self.sfa_host),
+                         (self.sfb, self.sfb_host)):
+            dst.copy_(src, non_blocking=True)
+        ptxstd.gemm_mxfp8_sparse(self.vals, self.meta, self.sfa, self.b, self.sfb, out=self.c)
+        self.c_host.copy_(self.c, non_blocking=True)
+        return 1
+
+    def cpu_sample(self, threads: int, budget_s: float):
+        """The same f32 blocked GEMM as the dense workloads over the decompressed A (a CPU has no
+        2:4 sparse unit), on a 256-row block, scaled to the logical FLOPs."""
+        return super().cpu_sample(threads, budget_s)
+
+
 class Nvfp4Gemm:
     """NVFP4 MLP up-projection: A [8192, 8192] x B [28672, 8192] (E2M1 + E4M3/16 + f32 global)
     -> bf16 [8192, 28672]; B is sharded along N across ranks (no communication)."""
@@ -612,7 +676,7 @@ class MxFp8QuantizeSR(MxFp8Quantize):
 
 WORKLOADS = {"mxfp8_quantize": MxFp8Quantize, "fp8_gemm": Fp8Gemm, "nvfp4_gemm": Nvfp4Gemm,
              "decode_gemm": DecodeGemm, "mxfp8_gemm": Mxfp8Gemm,
-             "mxfp8_quantize_sr": MxFp8QuantizeSR}
+             "mxfp8_quantize_sr": MxFp8QuantizeSR, "mxfp8_gemm_sparse": Mxfp8SparseGemm}
 
 
 # ---- arms -----------------------------------------------------------------------------------

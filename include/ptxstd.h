@@ -196,6 +196,25 @@ PTXSTD_API int ptxstd_gemm_nvfp4(const uint8_t* d_a, const uint8_t* d_sfa, float
 PTXSTD_API int ptxstd_gemm_mxfp8(const uint8_t* d_a, const uint8_t* d_sfa, const uint8_t* d_b,
                                  const uint8_t* d_sfb, uint16_t* d_c, int64_t M, int64_t N,
                                  int64_t K, ptxstd_stream stream);
+/* 2:4 structured sparsity (the A operand of tcgen05.mma.sp, src/tcgen05/mma.rs:725-777): in each
+ * group of four consecutive elements of a row of E4M3 codes [rows, cols], the two of largest
+ * magnitude (code & 0x7F, ties to the lower index) are kept, in index order, in vals
+ * [rows, cols/2]; meta [rows, cols/8] holds one nibble per group, i0 | i1 << 2 (i0 < i1 the kept
+ * positions), group g in the low nibble of byte g/2 for even g. cols % 8 == 0; d_codes 8-byte
+ * and d_vals 4-byte aligned. */
+PTXSTD_API int ptxstd_prune_24_e4m3(const uint8_t* d_codes, int64_t rows, int64_t cols, uint8_t* d_vals,
+                         uint8_t* d_meta, ptxstd_stream stream);
+/* 2:4-sparse MXFP8 GEMM: C[M,N] bf16 = sum_k A[m,k] 2^(sfa[m,k/64]-127) * B[n,k] 2^(sfb[n,k/64]-127)
+ * with A given as (vals [M,K/2], meta [M,K/8]) of ptxstd_prune_24_e4m3, B [N,K] E4M3 (K
+ * contiguous), and ONE UE8M0 scale per 64 logical K for each operand (the sparse K = 64 MMA takes
+ * a single scale: 32 stored elements of A), in the blocked 128x4 layout (one 512-byte tile per
+ * 128 rows and 256 K). tcgen05.mma.sp.cta_group::2.kind::mxf8f6f4.block_scale.block32, metadata
+ * moved to Tensor Memory with tcgen05.cp.128x128b (mma_block_scaled_sparse, src/tcgen05/mma.rs:
+ * 725-777; InstrDescriptor::with_sparsity, src/tcgen05/descriptor.rs:500-506). M % 256 == 0,
+ * N % 256 == 0, K % 256 == 0; all pointers 16-byte aligned. */
+PTXSTD_API int ptxstd_gemm_mxfp8_sparse(const uint8_t* d_vals, const uint8_t* d_meta, const uint8_t* d_sfa,
+                             const uint8_t* d_b, const uint8_t* d_sfb, uint16_t* d_c, int64_t M,
+                             int64_t N, int64_t K, ptxstd_stream stream);
 
 /* Decode-shape GEMM: y[M,N] bf16 = MXFP8(x)[M,K] * NVFP4(W)[N,K]^T * gw, M <= 16 tokens.
  * x: bf16 [M,K] row-major, quantised inside the call with the recipe of ptxstd_quantize_mxfp8

@@ -886,6 +886,101 @@ void ptxo_gemm_mxfp8_ref(const uint8_t* A, const uint8_t* sfA, const uint8_t* B,
     parallel_for((uint64_t)n_samples, threads, mxfp8_samples, &c);
 }
 
+/* 2:4 pruning (one row per job step): magnitude = code & 0x7F (E4M3 codes order like their
+ * magnitudes; the NaN code 0x7F sorts highest), ties to the lower index. */
+typedef struct { const uint8_t* codes; int64_t cols; uint8_t *vals, *meta; } prune_ctx;
+
+static void prune_rows(void* p, uint64_t lo, uint64_t hi) {
+    prune_ctx* c = (prune_ctx*)p;
+    for (uint64_t r = lo; r < hi; ++r) {
+        const uint8_t* x = c->codes + r * c->cols;
+        uint8_t* v = c->vals + r * (c->cols / 2);
+        uint8_t* m = c->meta + r * (c->cols / 8);
+        for (int64_t g = 0; g < c->cols / 4; ++g) {
+            const uint8_t* q = x + 4 * g;
+            int best = 0;
+            for (int i = 1; i < 4; ++i) if ((q[i] & 0x7F) > (q[best] & 0x7F)) best = i;
+            int second = -1;
+            for (int i = 0; i < 4; ++i) {
+                if (i == best) continue;
+                if (second < 0 || (q[i] & 0x7F) > (q[second] & 0x7F)) second = i;
+            }
+            int i0 = best < second ? best : second, i1 = best < second ? second : best;
+            v[2 * g] = q[i0];
+            v[2 * g + 1] = q[i1];
+            uint8_t nib = (uint8_t)(i0 | (i1 << 2));
+            if (g % 2 == 0) m[g / 2] = nib;
+            else m[g / 2] |= (uint8_t)(nib << 4);
+        }
+    }
+}
+
+void ptxo_prune_24(const uint8_t* codes, int64_t rows, int64_t cols, uint8_t* vals, uint8_t* meta,
+                   int threads) {
+    prune_ctx c = {codes, cols, vals, meta};
+    parallel_for((uint64_t)rows, threads, prune_rows, &c);
+}
+
+typedef struct { const uint8_t *vals, *meta; int64_t cols; uint8_t* codes; } dec24_ctx;
+
+static void decompress_rows(void* p, uint64_t lo, uint64_t hi) {
+    dec24_ctx* c = (dec24_ctx*)p;
+    for (uint64_t r = lo; r < hi; ++r) {
+        uint8_t* x = c->codes + r * c->cols;
+        const uint8_t* v = c->vals + r * (c->cols / 2);
+        const uint8_t* m = c->meta + r * (c->cols / 8);
+        memset(x, 0, (size_t)c->cols);
+        for (int64_t g = 0; g < c->cols / 4; ++g) {
+            uint8_t nib = (uint8_t)((m[g / 2] >> (4 * (g % 2))) & 0xF);
+            x[4 * g + (nib & 3)] = v[2 * g];
+            x[4 * g + (nib >> 2)] = v[2 * g + 1];
+        }
+    }
+}
+
+void ptxo_decompress_24(const uint8_t* vals, const uint8_t* meta, int64_t rows, int64_t cols,
+                        uint8_t* codes, int threads) {
+    dec24_ctx c = {vals, meta, cols, codes};
+    parallel_for((uint64_t)rows, threads, decompress_rows, &c);
+}
+
+static void mxfp8_sparse_samples(void* p, uint64_t lo, uint64_t hi) {
+    gemm_ctx* c = (gemm_ctx*)p;
+    double lut[256];
+    for (int i = 0; i < 256; ++i) lut[i] = ptxo_e4m3_to_f32((uint8_t)i);
+    const int64_t K = c->K;
+    for (uint64_t s = lo; s < hi; ++s) {
+        /* c->A holds vals, c->W holds meta */
+        const uint8_t* v = c->A + c->rows[s] * (K / 2);
+        const uint8_t* m = c->W + c->rows[s] * (K / 8);
+        const uint8_t* sa = c->sfA + c->rows[s] * (K / 64);
+        const uint8_t* b = c->B + c->cols[s] * K;
+        const uint8_t* sb = c->sfB + c->cols[s] * (K / 64);
+        double acc = 0, mag = 0;
+        for (int64_t g = 0; g < K / 4; ++g) {
+            uint8_t nib = (uint8_t)((m[g / 2] >> (4 * (g % 2))) & 0xF);
+            double scale = (double)ptxo_ue8m0_to_f32(sa[(4 * g) >> 6]) *
+                           (double)ptxo_ue8m0_to_f32(sb[(4 * g) >> 6]);
+            for (int h = 0; h < 2; ++h) {
+                int64_t k = 4 * g + (h ? (nib >> 2) : (nib & 3));
+                double t = lut[v[2 * g + h]] * lut[b[k]] * scale;
+                acc += t; mag += fabs(t);
+            }
+        }
+        c->ref[s] = acc; c->mag[s] = mag;
+    }
+}
+
+void ptxo_gemm_mxfp8_sparse_ref(const uint8_t* vals, const uint8_t* meta, const uint8_t* sfA,
+                                const uint8_t* B, const uint8_t* sfB, int64_t M, int64_t N,
+                                int64_t K, const int64_t* rows, const int64_t* cols,
+                                int64_t n_samples, double* ref, double* mag, int threads) {
+    gemm_ctx c; memset(&c, 0, sizeof c);
+    c.A = vals; c.W = meta; c.sfA = sfA; c.B = B; c.sfB = sfB;
+    c.M = M; c.N = N; c.K = K; c.rows = rows; c.cols = cols; c.ref = ref; c.mag = mag;
+    parallel_for((uint64_t)n_samples, threads, mxfp8_sparse_samples, &c);
+}
+
 static void decode_samples(void* p, uint64_t lo, uint64_t hi) {
     gemm_ctx* c = (gemm_ctx*)p;
     int64_t K = c->K;

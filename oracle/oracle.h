@@ -181,6 +181,25 @@ void ptxo_gemm_mxfp8_ref(const uint8_t* A, const uint8_t* sfA, const uint8_t* B,
                          const uint8_t* sfB, int64_t M, int64_t N, int64_t K,
                          const int64_t* rows, const int64_t* cols, int64_t n_samples, double* ref,
                          double* mag, int threads);
+/* 2:4 structured sparsity of E4M3 codes [rows, cols] (cols % 8 == 0): in every group of four
+ * consecutive elements of a row, the two with the largest magnitude (code & 0x7F; ties go to the
+ * lower index) are kept, in index order, in vals [rows, cols/2]; meta [rows, cols/8] holds one
+ * nibble per group, i0 | i1 << 2 (i0 < i1, the kept positions), group g in the low nibble of byte
+ * g/2 when g is even. This is the metadata of tcgen05.mma.sp for 8-bit kinds
+ * (src/tcgen05/mma.rs:725-777): a row's nibbles in order are its lane's bits in Tensor Memory. */
+void ptxo_prune_24(const uint8_t* codes, int64_t rows, int64_t cols, uint8_t* vals, uint8_t* meta,
+                   int threads);
+/* The dense E4M3 matrix [rows, cols] of (vals, meta): kept codes at their positions, 0 elsewhere. */
+void ptxo_decompress_24(const uint8_t* vals, const uint8_t* meta, int64_t rows, int64_t cols,
+                        uint8_t* codes, int threads);
+/* 2:4-sparse MXFP8 GEMM (tcgen05.mma.sp kind::mxf8f6f4 .block_scale): A given as (vals [M,K/2],
+ * meta [M,K/8]), B [N,K] E4M3, and ONE UE8M0 scale per 64 logical K for both operands (the
+ * sparse MMA of K = 64 takes a single scale of each operand: 32 stored A elements), sfA [M,K/64],
+ * sfB [N,K/64] row-major; C[i,j] = sum_k A[i,k] 2^(sfA[i,k/64]-127) B[j,k] 2^(sfB[j,k/64]-127). */
+void ptxo_gemm_mxfp8_sparse_ref(const uint8_t* vals, const uint8_t* meta, const uint8_t* sfA,
+                                const uint8_t* B, const uint8_t* sfB, int64_t M, int64_t N,
+                                int64_t K, const int64_t* rows, const int64_t* cols,
+                                int64_t n_samples, double* ref, double* mag, int threads);
 /* Decode: x bf16 [M,K] is MXFP8-quantised (32-blocks) by the recipe above, W NVFP4 [N,K/2] with
  * sfW [N,K/16] and gw; C[i,j] = sum_k xq[i,k] 2^(sx-127) * w[j,k] sfW gw. */
 void ptxo_gemm_decode_ref(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float gw,

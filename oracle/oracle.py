@@ -109,6 +109,10 @@ def _declare(L: C.CDLL) -> None:
         "ptxo_sweep_code": (u32, [i32, u64]),
         "ptxo_sweep_width": (i32, [i32]),
         "ptxo_quantize_mxfp8_rs": (None, [p, i64, i64, u64, p, p, i32]),
+        "ptxo_prune_24": (None, [p, i64, i64, p, p, i32]),
+        "ptxo_decompress_24": (None, [p, p, i64, i64, p, i32]),
+        "ptxo_gemm_mxfp8_sparse_ref": (None, [p, p, p, p, p, i64, i64, i64, p, p, i64, p, p,
+                                              i32]),
         "ptxo_quantize_nvfp4_rs": (i32, [p, i64, i64, f32, u64, p, p, i32]),
     }
     for name, (res, args) in sigs.items():
@@ -202,6 +206,37 @@ def gemm_mxfp8_ref(A, sfA, B, sfB, rows, cols, threads=0):
     r, c, ref, mag = _samples(rows, cols)
     lib().ptxo_gemm_mxfp8_ref(_ptr(A), _ptr(sfA), _ptr(B), _ptr(sfB), M, N, K, _ptr(r), _ptr(c),
                               r.size, _ptr(ref), _ptr(mag), threads)
+    return ref, mag
+
+
+def prune_24(codes: np.ndarray, threads: int = 0):
+    """2:4 magnitude pruning of E4M3 codes [rows, cols] -> (vals [rows, cols/2], meta [rows, cols/8])."""
+    x = np.ascontiguousarray(codes, dtype=np.uint8)
+    rows, cols = x.shape
+    vals = np.empty((rows, cols // 2), dtype=np.uint8)
+    meta = np.empty((rows, cols // 8), dtype=np.uint8)
+    lib().ptxo_prune_24(_ptr(x), rows, cols, _ptr(vals), _ptr(meta), threads)
+    return vals, meta
+
+
+def decompress_24(vals: np.ndarray, meta: np.ndarray, threads: int = 0) -> np.ndarray:
+    v = np.ascontiguousarray(vals, dtype=np.uint8)
+    m = np.ascontiguousarray(meta, dtype=np.uint8)
+    rows, cols = v.shape[0], v.shape[1] * 2
+    out = np.empty((rows, cols), dtype=np.uint8)
+    lib().ptxo_decompress_24(_ptr(v), _ptr(m), rows, cols, _ptr(out), threads)
+    return out
+
+
+def gemm_mxfp8_sparse_ref(vals, meta, sfA, B, sfB, rows, cols, threads=0):
+    """2:4-sparse MXFP8 GEMM reference at sampled outputs; scales row-major [rows, K/64]."""
+    vals, meta, sfA, B, sfB = (np.ascontiguousarray(t, dtype=np.uint8)
+                               for t in (vals, meta, sfA, B, sfB))
+    M, K = vals.shape[0], vals.shape[1] * 2
+    N = B.shape[0]
+    r, c, ref, mag = _samples(rows, cols)
+    lib().ptxo_gemm_mxfp8_sparse_ref(_ptr(vals), _ptr(meta), _ptr(sfA), _ptr(B), _ptr(sfB), M, N,
+                                     K, _ptr(r), _ptr(c), r.size, _ptr(ref), _ptr(mag), threads)
     return ref, mag
 
 

@@ -339,6 +339,28 @@ __device__ __forceinline__ void cp_32x128b_warpx4_pair(uint32_t taddr, uint64_t 
     asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc)
                  : "memory");
 }
+// copy::<Two, S128x128b> (src/tcgen05/copy.rs): 128 rows x 16 bytes of each CTA's smem -> 4
+// columns of that CTA's 128 lanes (row i to lane i).
+__device__ __forceinline__ void cp_128x128b_pair(uint32_t taddr, uint64_t src_desc) {
+    asm volatile("tcgen05.cp.cta_group::2.128x128b [%0], %1;" ::"r"(taddr), "l"(src_desc)
+                 : "memory");
+}
+// mma_block_scaled_sparse::<Two, _, Block32, Mxf8f6f4> (src/tcgen05/mma.rs:725-777): A is 2:4
+// sparse (the descriptor addresses the compressed K/2 values), its metadata at [meta] in TMEM;
+// one MMA covers K = 64 logical elements and takes one scale byte of each operand.
+__device__ __forceinline__ void mma_sp_mxf8f6f4_block32_pair(uint32_t d_tmem, uint64_t a_desc,
+                                                             uint64_t b_desc, uint32_t meta_tmem,
+                                                             uint32_t idesc, uint32_t sfa_tmem,
+                                                             uint32_t sfb_tmem,
+                                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %7, 0;\n\t"
+        "tcgen05.mma.sp.cta_group::2.kind::mxf8f6f4.block_scale.block32 [%0], %1, %2, [%3], %4, "
+        "[%5], [%6], p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(meta_tmem), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem),
+        "r"(accumulate)
+        : "memory");
+}
 
 // load::<S32x32b, x32> (src/tcgen05/ld_st.rs:252-300): lane (32 * (warp % 4) + laneid), 32
 // consecutive columns -> 32 registers.

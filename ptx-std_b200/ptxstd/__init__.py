@@ -87,6 +87,11 @@ _SIGS = {
                                     C.c_void_p]),
     "ptxstd_gemm_mxfp8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_int64, C.c_int64, C.c_int64, C.c_void_p]),
+    "ptxstd_prune_24_e4m3": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p,
+                                       C.c_void_p]),
+    "ptxstd_gemm_mxfp8_sparse": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                           C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
+                                           C.c_int64, C.c_void_p]),
     "ptxstd_gemm_decode_workspace_bytes": (C.c_size_t, [C.c_int64, C.c_int64, C.c_int64]),
     "ptxstd_gemm_decode": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_void_p,
                                      C.c_int64, C.c_int64, C.c_int64, C.c_void_p, C.c_size_t,
@@ -173,9 +178,9 @@ def last_device_error(clear: bool = True, stream=None) -> tuple[int, int]:
 
 
 from . import data_types, tcgen05  # noqa: E402
-from .kernels import (gemm_decode, gemm_fp8, gemm_mxfp8, gemm_nvfp4,  # noqa: E402
-                      quantize_mxfp8, quantize_nvfp4)
+from .kernels import (gemm_decode, gemm_fp8, gemm_mxfp8, gemm_mxfp8_sparse,  # noqa: E402
+                      gemm_nvfp4, prune_24, quantize_mxfp8, quantize_nvfp4)
 
 __all__ = ["lib", "check", "PtxStdError", "status_string", "last_device_error", "data_types",
            "tcgen05", "quantize_mxfp8", "quantize_nvfp4", "gemm_fp8", "gemm_mxfp8",
-           "gemm_nvfp4", "gemm_decode"]
+           "gemm_nvfp4", "gemm_decode", "gemm_mxfp8_sparse", "prune_24"]

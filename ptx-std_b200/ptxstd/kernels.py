@@ -63,6 +63,38 @@ def gemm_mxfp8(a, sfa, b, sfb, out=None, stream=None):
     return c
 
 
+def prune_24(codes, stream=None):
+    """2:4 pruning of E4M3 codes [rows, cols] (uint8) -> (vals [rows, cols/2], meta [rows, cols/8])
+    (ptxstd_prune_24_e4m3: the two largest magnitudes of each group of four are kept)."""
+    torch = _torch()
+    if codes.dtype != torch.uint8 or codes.dim() != 2:
+        raise TypeError("expected 2-D uint8 E4M3 codes")
+    rows, cols = codes.shape
+    codes = codes.contiguous()
+    vals = torch.empty((rows, cols // 2), dtype=torch.uint8, device=codes.device)
+    meta = torch.empty((rows, cols // 8), dtype=torch.uint8, device=codes.device)
+    check(lib().ptxstd_prune_24_e4m3(_dev(codes), rows, cols, _dev(vals), _dev(meta),
+                                     _stream(stream)), "prune_24")
+    return vals, meta
+
+
+def gemm_mxfp8_sparse(vals, meta, sfa, b, sfb, out=None, stream=None):
+    """2:4-sparse MXFP8: A as (vals [M, K/2], meta [M, K/8]) from prune_24, b [N, K] E4M3, blocked
+    UE8M0 scales per 64 logical K for both operands -> bf16 [M, N]."""
+    torch = _torch()
+    M, Kh = vals.shape
+    K = 2 * Kh
+    N = b.shape[0]
+    if b.shape[1] != K or meta.shape != (M, K // 8):
+        raise ValueError("shape mismatch")
+    if sfa.numel() != M * K // 64 or sfb.numel() != N * K // 64:
+        raise ValueError("scale tensors must hold one UE8M0 per 64 logical elements")
+    c = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=vals.device)
+    check(lib().ptxstd_gemm_mxfp8_sparse(_dev(vals), _dev(meta), _dev(sfa), _dev(b), _dev(sfb),
+                                         _dev(c), M, N, K, _stream(stream)), "gemm_mxfp8_sparse")
+    return c
+
+
 def gemm_nvfp4(a, sfa, ga: float, b, sfb, gb: float, out=None, stream=None):
     """NVFP4 a [M, K/2], b [N, K/2] (uint8, E2M1x2) with blocked E4M3 scales -> bf16 [M, N]."""
     torch = _torch()

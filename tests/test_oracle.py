@@ -442,3 +442,37 @@ def test_rs_quantize_keeps_scales(oracle):
     n0, t0 = oracle.quantize_nvfp4(xb, g)
     n1, t1 = oracle.quantize_nvfp4_rs(xb, g, 5)
     assert np.array_equal(t0, t1)
+
+
+# ---- 2:4 structured sparsity ---------------------------------------------------------------------
+
+def test_prune_24_rules(oracle):
+    """The two largest magnitudes of each group of four stay, in index order, ties to the lower
+    index; the NaN code sorts highest; metadata nibble = i0 | i1 << 2, even groups low."""
+    A = np.array([[0x38, 0x40, 0x30, 0x48,   0x05, 0x05, 0x05, 0x05],
+                  [0xC8, 0x01, 0x7F, 0x00,   0x80, 0x00, 0x81, 0x02]], dtype=np.uint8)
+    v, m = oracle.prune_24(A)
+    assert v.tolist() == [[0x40, 0x48, 0x05, 0x05], [0xC8, 0x7F, 0x81, 0x02]]
+    # row 0: group 0 keeps (1, 3) -> 0b1101, group 1 ties keep (0, 1) -> 0b0100
+    # row 1: group 0 keeps (0, 2) -> 0b1000, group 1 keeps (2, 3) -> 0b1110
+    assert m.tolist() == [[0x4D], [0xE8]]
+    d = oracle.decompress_24(v, m)
+    assert d.tolist() == [[0, 0x40, 0, 0x48, 0x05, 0x05, 0, 0], [0xC8, 0, 0x7F, 0, 0, 0, 0x81, 0x02]]
+
+
+def test_sparse_ref_equals_dense_ref(oracle):
+    """The sparse reference over (vals, meta) equals the dense MXFP8 reference over the
+    decompressed A with each 64-scale repeated for both 32-blocks."""
+    rng = np.random.default_rng(8)
+    M, N, K = 8, 6, 256
+    A = rng.integers(0, 0x7E, (M, K)).astype(np.uint8)
+    B = rng.integers(0, 0x7E, (N, K)).astype(np.uint8)
+    v, m = oracle.prune_24(A)
+    sfA = rng.integers(120, 134, (M, K // 64)).astype(np.uint8)
+    sfB = rng.integers(120, 134, (N, K // 64)).astype(np.uint8)
+    r, c = np.meshgrid(np.arange(M), np.arange(N), indexing="ij")
+    r, c = r.ravel(), c.ravel()
+    s_ref, s_mag = oracle.gemm_mxfp8_sparse_ref(v, m, sfA, B, sfB, r, c)
+    d_ref, d_mag = oracle.gemm_mxfp8_ref(oracle.decompress_24(v, m), np.repeat(sfA, 2, axis=1), B,
+                                         np.repeat(sfB, 2, axis=1), r, c)
+    assert np.allclose(s_ref, d_ref, rtol=1e-12, atol=0) and np.allclose(s_mag, d_mag, rtol=1e-12)
