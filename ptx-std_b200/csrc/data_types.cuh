@@ -212,6 +212,18 @@ __device__ __forceinline__ uint32_t bf16x2_from_f32(float x0, float x1) {
     return r;
 }
 
+// Both bf16 halves of a word, widened exactly to f32 and multiplied by `s` with round-to-nearest:
+// one mul.rn.f32x2 (sm_100's packed f32 multiply, two IEEE products; the same results as two
+// __fmul_rn). .x is the low half (element 0).
+__device__ __forceinline__ float2 bf16x2_mul_f32(uint32_t w, float s) {
+    const uint64_t a = (static_cast<uint64_t>(w & 0xFFFF0000u) << 32) | (w << 16);
+    const uint64_t b = (static_cast<uint64_t>(__float_as_uint(s)) << 32) | __float_as_uint(s);
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return make_float2(__uint_as_float(static_cast<uint32_t>(r)),
+                       __uint_as_float(static_cast<uint32_t>(r >> 32)));
+}
+
 // ---- block-scale helpers -------------------------------------------------------------------
 // NaN-propagating amax of the |bf16| values in a word pair: for non-negative bf16 patterns the
 // integer order is the float order, and every NaN pattern sorts above infinity, so an unsigned

@@ -88,9 +88,10 @@ struct Mxfp8 {
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         uint32_t p[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-            p[k] = dt::e4m3x2_from_f32<false>(__fmul_rn(dt::bf16_lo(w[k]), inv),
-                                              __fmul_rn(dt::bf16_hi(w[k]), inv));
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = dt::bf16x2_mul_f32(w[k], inv);
+            p[k] = dt::e4m3x2_from_f32<false>(f.x, f.y);
+        }
         if (valid) {
             reinterpret_cast<uint2*>(q)[gv] = make_uint2(p[0] | (p[1] << 16), p[2] | (p[3] << 16));
             if ((lane & 3u) == 0) store_scale<BLOCKED>(sf, gv >> 2, sf_cols, code);
@@ -115,10 +116,10 @@ struct Nvfp4 {
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         uint32_t packed = 0;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-            packed |= dt::e2m1x2_from_f32<false>(__fmul_rn(dt::bf16_lo(w[k]), r),
-                                                 __fmul_rn(dt::bf16_hi(w[k]), r))
-                      << (8 * k);
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = dt::bf16x2_mul_f32(w[k], r);
+            packed |= dt::e2m1x2_from_f32<false>(f.x, f.y) << (8 * k);
+        }
         if (valid) {
             reinterpret_cast<uint32_t*>(q)[gv] = packed;
             if ((lane & 1u) == 0) store_scale<BLOCKED>(sf, gv >> 1, sf_cols, code);
@@ -141,14 +142,12 @@ struct Mxfp8Rs {
         const uint32_t code = dt::mxfp8_scale_code(__uint_as_float(m << 16));
         const float inv = dt::ue8m0_inverse(code);
         const uint64_t h = dt::splitmix64(seed, gv);
-        const uint32_t lo = dt::e4m3x4_from_f32_rs<false>(
-            __fmul_rn(dt::bf16_lo(v.x), inv), __fmul_rn(dt::bf16_hi(v.x), inv),
-            __fmul_rn(dt::bf16_lo(v.y), inv), __fmul_rn(dt::bf16_hi(v.y), inv),
-            static_cast<uint32_t>(h));
-        const uint32_t hi = dt::e4m3x4_from_f32_rs<false>(
-            __fmul_rn(dt::bf16_lo(v.z), inv), __fmul_rn(dt::bf16_hi(v.z), inv),
-            __fmul_rn(dt::bf16_lo(v.w), inv), __fmul_rn(dt::bf16_hi(v.w), inv),
-            static_cast<uint32_t>(h >> 32));
+        const float2 a = dt::bf16x2_mul_f32(v.x, inv), b = dt::bf16x2_mul_f32(v.y, inv);
+        const float2 c = dt::bf16x2_mul_f32(v.z, inv), d = dt::bf16x2_mul_f32(v.w, inv);
+        const uint32_t lo =
+            dt::e4m3x4_from_f32_rs<false>(a.x, a.y, b.x, b.y, static_cast<uint32_t>(h));
+        const uint32_t hi =
+            dt::e4m3x4_from_f32_rs<false>(c.x, c.y, d.x, d.y, static_cast<uint32_t>(h >> 32));
         if (valid) {
             reinterpret_cast<uint2*>(q)[gv] = make_uint2(lo, hi);
             if ((lane & 3u) == 0) store_scale<BLOCKED>(sf, gv >> 2, sf_cols, code);
@@ -172,14 +171,12 @@ struct Nvfp4Rs {
         const float t = __fmul_rn(dt::e4m3_to_f32(code), g);
         const float r = (t == 0.0f) ? 0.0f : __frcp_rn(t);
         const uint64_t h = dt::splitmix64(seed, gv);
-        const uint32_t lo = dt::e2m1x4_from_f32_rs<false>(
-            __fmul_rn(dt::bf16_lo(v.x), r), __fmul_rn(dt::bf16_hi(v.x), r),
-            __fmul_rn(dt::bf16_lo(v.y), r), __fmul_rn(dt::bf16_hi(v.y), r),
-            static_cast<uint32_t>(h));
-        const uint32_t hi = dt::e2m1x4_from_f32_rs<false>(
-            __fmul_rn(dt::bf16_lo(v.z), r), __fmul_rn(dt::bf16_hi(v.z), r),
-            __fmul_rn(dt::bf16_lo(v.w), r), __fmul_rn(dt::bf16_hi(v.w), r),
-            static_cast<uint32_t>(h >> 32));
+        const float2 a = dt::bf16x2_mul_f32(v.x, r), b = dt::bf16x2_mul_f32(v.y, r);
+        const float2 c = dt::bf16x2_mul_f32(v.z, r), d = dt::bf16x2_mul_f32(v.w, r);
+        const uint32_t lo =
+            dt::e2m1x4_from_f32_rs<false>(a.x, a.y, b.x, b.y, static_cast<uint32_t>(h));
+        const uint32_t hi =
+            dt::e2m1x4_from_f32_rs<false>(c.x, c.y, d.x, d.y, static_cast<uint32_t>(h >> 32));
         if (valid) {
             reinterpret_cast<uint32_t*>(q)[gv] = lo | (hi << 16);
             if ((lane & 1u) == 0) store_scale<BLOCKED>(sf, gv >> 1, sf_cols, code);
