@@ -90,6 +90,29 @@ PTXSTD_API int ptxstd_cvt_f32_to_e3m2(const float* d_x, uint8_t* d_out, size_t n
  * of each code byte are significant (float6.rs:1-8: the two top bits must be zero). */
 PTXSTD_API int ptxstd_cvt_e2m3_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
 PTXSTD_API int ptxstd_cvt_e3m2_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
+/* Vector<E, N>::to_bf16_scaled::<RELU, OVERFLOW> (src/data_types/narrow.rs:314-330, :444-465):
+ * element i times the UE8M0 scale d_scales[i / block] (2^(s-127); 0xff is NaN), rounded to bf16
+ * (RN). relu clamps negative results to +0; satfinite clamps results outside the finite range to
+ * the largest finite bf16 of matching sign, otherwise they become infinity. block = 1 is the
+ * reference's form (one scale per element); block = 32 dequantises MXFP8 rows. The reference
+ * lowers this to cvt.rn...bf16x2.<fmt>x2.scale::n2::ue8m0, which the CUDA 12.9 ptxas of this
+ * build does not accept; the result is computed exactly instead (exact decode, exact f32 product,
+ * one cvt.rn{.relu}{.satfinite}.bf16x2.f32). e2m1x2 codes are packed two per byte (n even). */
+PTXSTD_API int ptxstd_cvt_e4m3_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scales,
+                                   uint16_t* d_out, size_t n, size_t block, int relu,
+                                   int satfinite, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_e5m2_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scales,
+                                   uint16_t* d_out, size_t n, size_t block, int relu,
+                                   int satfinite, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_e2m1x2_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scales,
+                                     uint16_t* d_out, size_t n, size_t block, int relu,
+                                     int satfinite, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_e2m3_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scales,
+                                   uint16_t* d_out, size_t n, size_t block, int relu,
+                                   int satfinite, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_e3m2_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scales,
+                                   uint16_t* d_out, size_t n, size_t block, int relu,
+                                   int satfinite, ptxstd_stream stream);
 /* Stochastic rounding: Vector<E, N>::from_f32_stochastic::<RELU> (src/data_types/narrow.rs:494-505;
  * core quad_from_f32_stochastic = cvt.rs.satfinite{.relu}.<fmt>x4.f32, :217-229). Elements
  * 4g .. 4g+3 are converted together with the random bits d_rbits[g] (ceil(n/4) words); a last

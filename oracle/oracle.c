@@ -239,6 +239,61 @@ uint16_t ptxo_f32_to_bf16(float x) {
 float ptxo_bf16_to_f32(uint16_t h) { return u2f((uint32_t)h << 16); }
 
 /* ------------------------------------------------------------------------------------------ */
+/* scaled up-conversion to bf16                                                               */
+/* ------------------------------------------------------------------------------------------ */
+
+static float narrow_value(int format, uint8_t code) {
+    switch (format) {
+    case PTXO_E4M3: return ptxo_e4m3_to_f32(code);
+    case PTXO_E5M2: return ptxo_e5m2_to_f32(code);
+    case PTXO_E2M3: return ptxo_e2m3_to_f32(code);
+    case PTXO_E3M2: return ptxo_e3m2_to_f32(code);
+    default: return ptxo_e2m1_to_f32(code);
+    }
+}
+
+uint16_t ptxo_to_bf16_scaled(int format, uint8_t code, uint8_t scale, int relu, int satfinite) {
+    float v = narrow_value(format, code);
+    if (v != v || scale == 0xFF) return 0x7FFF;
+    double p = (double)v * ldexp(1.0, (int)scale - 127); /* exact: <= 4 significant bits */
+    int neg = signbit(p) != 0;
+    if (relu && neg) return 0;
+    double a = fabs(p);
+    uint16_t sign = neg ? 0x8000 : 0;
+    if (isinf(a)) return (uint16_t)(sign | (satfinite ? 0x7F7F : 0x7F80));
+    if (a == 0.0) return sign;
+    /* quantum: 2^(e-7) in the normal range, 2^-133 below 2^-126 */
+    int e;
+    frexp(a, &e);
+    e -= 1;
+    double q = ldexp(1.0, e < -126 ? -133 : e - 7);
+    double m = a / q, r = nearbyint(m); /* round half to even (default rounding mode) */
+    double b = r * q;
+    if (b >= ldexp(1.0, 128)) return (uint16_t)(sign | (satfinite ? 0x7F7F : 0x7F80));
+    return (uint16_t)(sign | (f2u((float)b) >> 16));
+}
+
+typedef struct {
+    int format, relu, sat; const uint8_t *codes, *scales; uint16_t* out; size_t block;
+} scaled_ctx;
+
+static void scaled_range(void* p, uint64_t lo, uint64_t hi) {
+    scaled_ctx* c = (scaled_ctx*)p;
+    for (uint64_t i = lo; i < hi; ++i) {
+        uint8_t code = c->format == PTXO_E2M1 ? (uint8_t)((c->codes[i / 2] >> (4 * (i % 2))) & 0xF)
+                                              : c->codes[i];
+        c->out[i] = ptxo_to_bf16_scaled(c->format, code, c->scales[i / c->block], c->relu, c->sat);
+    }
+}
+
+void ptxo_to_bf16_scaled_array(int format, const uint8_t* codes, const uint8_t* scales,
+                               uint16_t* out, size_t n, size_t block, int relu, int satfinite,
+                               int threads) {
+    scaled_ctx c = {format, relu, satfinite, codes, scales, out, block};
+    parallel_for(n, threads, scaled_range, &c);
+}
+
+/* ------------------------------------------------------------------------------------------ */
 /* stochastic rounding                                                                        */
 /* ------------------------------------------------------------------------------------------ */
 

@@ -65,6 +65,17 @@ uint8_t ptxo_f32_to_ue8m0(float x, int rnd_up, int satfinite);
 uint16_t ptxo_f32_to_bf16(float x);
 float ptxo_bf16_to_f32(uint16_t h);
 
+/* to_bf16_scaled::<RELU, OVERFLOW> (src/data_types/narrow.rs:314-330, :444-465): the exact
+ * value of a narrow code (format PTXO_E4M3 .. PTXO_E3M2; E2M1 as a nibble) times 2^(scale-127),
+ * rounded to bf16 (RN, subnormals kept); relu maps negative results (and -0) to +0; satfinite
+ * clamps results past the finite range to the largest finite bf16 of matching sign, otherwise
+ * they become infinity; a NaN code or the NaN scale 0xff gives 0x7FFF. */
+uint16_t ptxo_to_bf16_scaled(int format, uint8_t code, uint8_t scale, int relu, int satfinite);
+/* Element i of codes (E2M1: nibble i % 2 of byte i / 2) with scales[i / block]. */
+void ptxo_to_bf16_scaled_array(int format, const uint8_t* codes, const uint8_t* scales,
+                               uint16_t* out, size_t n, size_t block, int relu, int satfinite,
+                               int threads);
+
 /* ---- stochastic rounding (cvt.rs; src/data_types/narrow.rs:217-229, :494-505; bf16
  * src/data_types/bfloat16.rs:456-462, :572-598; f16 src/data_types/float16.rs:589-595, :740-766).
  * One rbits word serves a group of four elements (FP8, FP6, E2M1) or a pair (bf16, f16). Element

@@ -110,6 +110,8 @@ def _declare(L: C.CDLL) -> None:
         "ptxo_sweep_width": (i32, [i32]),
         "ptxo_quantize_mxfp8_rs": (None, [p, i64, i64, u64, p, p, i32]),
         "ptxo_prune_24": (None, [p, i64, i64, p, p, i32]),
+        "ptxo_to_bf16_scaled": (u16, [i32, u8, u8, i32, i32]),
+        "ptxo_to_bf16_scaled_array": (None, [i32, p, p, p, C.c_size_t, C.c_size_t, i32, i32, i32]),
         "ptxo_decompress_24": (None, [p, p, i64, i64, p, i32]),
         "ptxo_gemm_mxfp8_sparse_ref": (None, [p, p, p, p, p, i64, i64, i64, p, p, i64, p, p,
                                               i32]),
@@ -207,6 +209,17 @@ def gemm_mxfp8_ref(A, sfA, B, sfB, rows, cols, threads=0):
     lib().ptxo_gemm_mxfp8_ref(_ptr(A), _ptr(sfA), _ptr(B), _ptr(sfB), M, N, K, _ptr(r), _ptr(c),
                               r.size, _ptr(ref), _ptr(mag), threads)
     return ref, mag
+
+
+def to_bf16_scaled(fmt: int, codes: np.ndarray, scales: np.ndarray, n: int, block: int = 1,
+                   relu: bool = False, satfinite: bool = False, threads: int = 0) -> np.ndarray:
+    """bf16 bit patterns of n narrow codes times their UE8M0 scales (scales[i // block])."""
+    c = np.ascontiguousarray(codes, dtype=np.uint8)
+    sc = np.ascontiguousarray(scales, dtype=np.uint8)
+    out = np.empty(n, dtype=np.uint16)
+    lib().ptxo_to_bf16_scaled_array(fmt, _ptr(c), _ptr(sc), _ptr(out), n, block, int(relu),
+                                    int(satfinite), threads)
+    return out
 
 
 def prune_24(codes: np.ndarray, threads: int = 0):

@@ -126,6 +126,58 @@ __global__ void __launch_bounds__(256) encode_x2_rs_kernel(const float* __restri
     }
 }
 
+// Exact f32 value of one narrow code (FMT as decode_kernel: 0 e4m3, 1 e5m2, 2 e2m1 nibble,
+// 4 e2m3, 5 e3m2).
+template <int FMT>
+__device__ __forceinline__ float narrow_to_f32(uint32_t c) {
+    if constexpr (FMT == 0) return dt::e4m3x2_to_f32(static_cast<uint16_t>(c)).x;
+    else if constexpr (FMT == 1) return dt::e5m2x2_to_f32(static_cast<uint16_t>(c)).x;
+    else if constexpr (FMT == 2) return dt::e2m1x2_to_f32(c).x;
+    else if constexpr (FMT == 4) return dt::e2m3x2_to_f32(static_cast<uint16_t>(c)).x;
+    else return dt::e3m2x2_to_f32(static_cast<uint16_t>(c)).x;
+}
+
+// 2^(s - 127) as an f32 (2^-127 is an f32 subnormal); NaN for the NaN code 0xff.
+__device__ __forceinline__ float ue8m0_value(uint32_t s) {
+    return s == 0xFFu ? __uint_as_float(0x7FC00000u)
+           : s != 0u  ? __uint_as_float(s << 23)
+                      : __uint_as_float(0x00400000u);
+}
+
+// to_bf16_scaled::<RELU, OVERFLOW> (narrow.rs:314-330, :444-465): element i times the UE8M0 scale
+// scales[i / block], rounded once to bf16 (RN; .relu clamps negatives to +0; .satfinite clamps
+// overflow to the largest finite bf16). The narrow value has at most 4 significant bits, so the
+// f32 product is exact (or infinite past 2^128) and the single cvt.rn...bf16x2.f32 is the only
+// rounding, which matters only below 2^-126.
+template <int FMT, bool RELU, bool SAT>
+__global__ void __launch_bounds__(256) to_bf16_scaled_kernel(const uint8_t* __restrict__ codes,
+                                                             const uint8_t* __restrict__ scales,
+                                                             uint16_t* __restrict__ out, size_t n,
+                                                             size_t block) {
+    const size_t n2 = (n + 1) / 2;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t p = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; p < n2;
+         p += stride) {
+        const size_t i = 2 * p;
+        uint32_t c0, c1 = 0;
+        if constexpr (FMT == 2) {
+            const uint32_t b = codes[p];
+            c0 = b & 0xFu;
+            c1 = b >> 4;
+        } else {
+            c0 = codes[i];
+            if (i + 1 < n) c1 = codes[i + 1];
+        }
+        const float v0 = __fmul_rn(narrow_to_f32<FMT>(c0), ue8m0_value(scales[i / block]));
+        const float v1 =
+            i + 1 < n ? __fmul_rn(narrow_to_f32<FMT>(c1), ue8m0_value(scales[(i + 1) / block]))
+                      : 0.0f;
+        const uint32_t r = dt::bf16x2_from_f32_mode<RELU, SAT>(v0, v1);
+        out[i] = static_cast<uint16_t>(r);
+        if (i + 1 < n) out[i + 1] = static_cast<uint16_t>(r >> 16);
+    }
+}
+
 template <bool ROUND_UP, bool SAT>
 __global__ void __launch_bounds__(256) encode_ue8m0_kernel(const float* __restrict__ x,
                                                            uint8_t* __restrict__ out, size_t n) {
@@ -280,6 +332,26 @@ template <typename F>
 int launch(F f) {
     f();
     return ptxstd::launch_status();
+}
+
+template <int FMT>
+int launch_scaled(const uint8_t* d_codes, const uint8_t* d_scales, uint16_t* d_out, size_t n,
+                  size_t block, int relu, int satfinite, ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_codes || !d_scales || !d_out || block == 0 || (FMT == 2 && (n & 1)))
+        return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int g = grid_for((n + 1) / 2);
+    return launch([&] {
+        if (relu && satfinite)
+            to_bf16_scaled_kernel<FMT, true, true><<<g, 256, 0, s>>>(d_codes, d_scales, d_out, n, block);
+        else if (relu)
+            to_bf16_scaled_kernel<FMT, true, false><<<g, 256, 0, s>>>(d_codes, d_scales, d_out, n, block);
+        else if (satfinite)
+            to_bf16_scaled_kernel<FMT, false, true><<<g, 256, 0, s>>>(d_codes, d_scales, d_out, n, block);
+        else
+            to_bf16_scaled_kernel<FMT, false, false><<<g, 256, 0, s>>>(d_codes, d_scales, d_out, n, block);
+    });
 }
 
 template <int OP>
@@ -481,6 +553,32 @@ int ptxstd_cvt_f32_to_bf16_rs(const float* d_x, const uint32_t* d_rbits, uint16_
 int ptxstd_cvt_f32_to_f16_rs(const float* d_x, const uint32_t* d_rbits, uint16_t* d_out,
                              size_t n, int relu, int satfinite, ptxstd_stream stream) {
     return launch_x2_rs<false>(d_x, d_rbits, d_out, n, relu, satfinite, stream);
+}
+
+int ptxstd_cvt_e4m3_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scales,
+                                   uint16_t* d_out, size_t n, size_t block, int relu,
+                                   int satfinite, ptxstd_stream stream) {
+    return launch_scaled<0>(d_codes, d_scales, d_out, n, block, relu, satfinite, stream);
+}
+int ptxstd_cvt_e5m2_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scales,
+                                   uint16_t* d_out, size_t n, size_t block, int relu,
+                                   int satfinite, ptxstd_stream stream) {
+    return launch_scaled<1>(d_codes, d_scales, d_out, n, block, relu, satfinite, stream);
+}
+int ptxstd_cvt_e2m1x2_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scales,
+                                     uint16_t* d_out, size_t n, size_t block, int relu,
+                                     int satfinite, ptxstd_stream stream) {
+    return launch_scaled<2>(d_codes, d_scales, d_out, n, block, relu, satfinite, stream);
+}
+int ptxstd_cvt_e2m3_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scales,
+                                   uint16_t* d_out, size_t n, size_t block, int relu,
+                                   int satfinite, ptxstd_stream stream) {
+    return launch_scaled<4>(d_codes, d_scales, d_out, n, block, relu, satfinite, stream);
+}
+int ptxstd_cvt_e3m2_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scales,
+                                   uint16_t* d_out, size_t n, size_t block, int relu,
+                                   int satfinite, ptxstd_stream stream) {
+    return launch_scaled<5>(d_codes, d_scales, d_out, n, block, relu, satfinite, stream);
 }
 
 int ptxstd_cvt_sweep(int variant, uint64_t base, uint64_t n, uint8_t* d_out,

@@ -224,6 +224,22 @@ __device__ __forceinline__ float2 bf16x2_mul_f32(uint32_t w, float s) {
                        __uint_as_float(static_cast<uint32_t>(r >> 32)));
 }
 
+// bf16x2::pair_from_f32_with::<Rn, R, O> (bfloat16.rs:446-454): cvt.rn{.relu}{.satfinite}.bf16x2.f32,
+// x0 in the low half.
+template <bool RELU, bool SAT>
+__device__ __forceinline__ uint32_t bf16x2_from_f32_mode(float x0, float x1) {
+    uint32_t r;
+    if constexpr (RELU && SAT)
+        asm("cvt.rn.relu.satfinite.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
+    else if constexpr (RELU)
+        asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
+    else if constexpr (SAT)
+        asm("cvt.rn.satfinite.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
+    else
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
+    return r;
+}
+
 // ---- block-scale helpers -------------------------------------------------------------------
 // NaN-propagating amax of the |bf16| values in a word pair: for non-negative bf16 patterns the
 // integer order is the float order, and every NaN pattern sorts above infinity, so an unsigned

@@ -108,6 +108,27 @@ def f16_from_f32_stochastic(x, rbits, relu: bool = False, satfinite: bool = Fals
     return _x2_stochastic("ptxstd_cvt_f32_to_f16_rs", x, rbits, relu, satfinite, stream)
 
 
+_SCALED = {E4M3: "ptxstd_cvt_e4m3_to_bf16_scaled", E5M2: "ptxstd_cvt_e5m2_to_bf16_scaled",
+           E2M1: "ptxstd_cvt_e2m1x2_to_bf16_scaled", E2M3: "ptxstd_cvt_e2m3_to_bf16_scaled",
+           E3M2: "ptxstd_cvt_e3m2_to_bf16_scaled"}
+
+
+def to_bf16_scaled(fmt: str, codes, scales, block: int = 1, relu: bool = False,
+                   satfinite: bool = False, stream=None):
+    """Vector<fmt, N>::to_bf16_scaled (narrow.rs:444-465): bf16 bit patterns (int16) of each code
+    times its UE8M0 scale scales[i // block]. E2M1 codes are packed two per byte."""
+    torch = _torch()
+    codes = codes.contiguous()
+    scales = scales.contiguous()
+    n = 2 * codes.numel() if fmt == E2M1 else codes.numel()
+    if scales.numel() < (n + block - 1) // block:
+        raise ValueError("too few scales")
+    out = torch.empty(n, dtype=torch.int16, device=codes.device)
+    check(getattr(lib(), _SCALED[fmt])(_dev(codes), _dev(scales), _dev(out), n, block, int(relu),
+                                       int(satfinite), _stream(stream)), f"to_bf16_scaled({fmt})")
+    return out
+
+
 def ue8m0_from_f32(x, round_up: bool = False, satfinite: bool = True, stream=None):
     torch = _torch()
     x = x.contiguous()

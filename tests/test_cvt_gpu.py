@@ -171,3 +171,37 @@ def test_stochastic_unbiased_on_device(cuda):
     assert abs(mean - exact) < 5 * se
     rn = dt.to_f32("e4m3", dt.from_f32("e4m3", x[:4])).double()[0].item()
     assert abs(rn - exact) > 50 * se
+
+
+# ---- scaled up-conversion to bf16 ------------------------------------------------------------------
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2", "e2m3", "e3m2", "e2m1"])
+def test_to_bf16_scaled_exhaustive(cuda, oracle, fmt):
+    """Every code times every UE8M0 scale (0x00 .. 0xff), with and without .relu / .satfinite,
+    bit for bit against the oracle; then MX dequantisation of random rows with one scale per 32."""
+    import ptxstd.data_types as dt
+    torch = cuda
+    ofmt = {"e4m3": oracle.E4M3, "e5m2": oracle.E5M2, "e2m3": oracle.E2M3, "e3m2": oracle.E3M2,
+            "e2m1": oracle.E2M1}[fmt]
+    ncodes = {"e4m3": 256, "e5m2": 256, "e2m3": 64, "e3m2": 64, "e2m1": 16}[fmt]
+    codes = np.repeat(np.arange(ncodes, dtype=np.uint8), 256)
+    scales = np.tile(np.arange(256, dtype=np.uint8), ncodes)
+    n = codes.size
+    packed = (codes[0::2] | (codes[1::2] << 4)).astype(np.uint8) if fmt == "e2m1" else codes
+    cd, sd = torch.from_numpy(packed).cuda(), torch.from_numpy(scales).cuda()
+    for relu in (False, True):
+        for sat in (False, True):
+            got = _to_np(dt.to_bf16_scaled(fmt, cd, sd, 1, relu, sat)).view(np.uint16)
+            want = oracle.to_bf16_scaled(ofmt, packed, scales, n, 1, relu, sat)
+            bad = np.nonzero(got != want)[0]
+            assert bad.size == 0, (relu, sat, [(int(codes[i]), int(scales[i]), hex(got[i]),
+                                                hex(want[i])) for i in bad[:6]])
+    rng = np.random.default_rng(11)
+    m = 1 << 16
+    rc = rng.integers(0, 256, m // 2 if fmt == "e2m1" else m).astype(np.uint8)
+    if fmt in ("e2m3", "e3m2"):
+        rc &= 0x3F
+    rs = rng.integers(100, 150, m // 32).astype(np.uint8)
+    got = _to_np(dt.to_bf16_scaled(fmt, torch.from_numpy(rc).cuda(), torch.from_numpy(rs).cuda(),
+                                   32)).view(np.uint16)
+    assert np.array_equal(got, oracle.to_bf16_scaled(ofmt, rc, rs, m, 32))

@@ -476,3 +476,33 @@ def test_sparse_ref_equals_dense_ref(oracle):
     d_ref, d_mag = oracle.gemm_mxfp8_ref(oracle.decompress_24(v, m), np.repeat(sfA, 2, axis=1), B,
                                          np.repeat(sfB, 2, axis=1), r, c)
     assert np.allclose(s_ref, d_ref, rtol=1e-12, atol=0) and np.allclose(s_mag, d_mag, rtol=1e-12)
+
+
+# ---- scaled up-conversion to bf16 --------------------------------------------------------------
+
+def test_to_bf16_scaled_rules(oracle):
+    """Known answers of the exact scaled conversion: an exact power-of-two product, overflow to
+    infinity or (with .satfinite) to the largest finite bf16, rounding below 2^-126, .relu, NaN."""
+    L = oracle.lib()
+    E4 = oracle.E4M3
+    assert L.ptxo_to_bf16_scaled(E4, 0x38, 130, 0, 0) == 0x4100          # 1.0 * 2^3
+    assert L.ptxo_to_bf16_scaled(E4, 0x7E, 254, 0, 0) == 0x7F80          # 448 * 2^127 -> inf
+    assert L.ptxo_to_bf16_scaled(E4, 0xFE, 254, 0, 1) == 0xFF7F          # -> -max finite
+    assert L.ptxo_to_bf16_scaled(E4, 0x01, 0, 0, 0) == 0x0000            # 2^-136 -> +0
+    assert L.ptxo_to_bf16_scaled(E4, 0x06, 0, 0, 0) == 0x0001            # 0.75 * 2^-133 -> 2^-133
+    assert L.ptxo_to_bf16_scaled(E4, 0xB8, 127, 1, 0) == 0x0000          # relu(-1) = +0
+    assert L.ptxo_to_bf16_scaled(E4, 0x7F, 127, 0, 0) == 0x7FFF          # NaN code
+    assert L.ptxo_to_bf16_scaled(E4, 0x38, 255, 0, 0) == 0x7FFF          # NaN scale
+    assert L.ptxo_to_bf16_scaled(oracle.E5M2, 0x7C, 127, 0, 1) == 0x7F7F  # inf, satfinite
+
+
+def test_to_bf16_scaled_exact_in_range(oracle):
+    """Where the product is a normal bf16, the result is exactly code value * 2^(scale - 127)."""
+    for fmt, ncodes in [(oracle.E4M3, 256), (oracle.E5M2, 256), (oracle.E2M3, 64)]:
+        codes = np.repeat(np.arange(ncodes, dtype=np.uint8), 100)
+        scales = np.tile(np.arange(90, 190, dtype=np.uint8), ncodes)
+        got = oracle.to_bf16_scaled(fmt, codes, scales, codes.size)
+        v = oracle.decode(fmt, codes).astype(np.float64) * np.exp2(scales.astype(np.float64) - 127)
+        ok = np.isfinite(v) & ((np.abs(v) >= 2.0 ** -126) | (v == 0)) & (np.abs(v) < 2.0 ** 127)
+        want = (v[ok].astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+        assert np.array_equal(got[ok], want)
