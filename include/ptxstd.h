@@ -90,6 +90,27 @@ PTXSTD_API int ptxstd_cvt_f32_to_e3m2(const float* d_x, uint8_t* d_out, size_t n
  * of each code byte are significant (float6.rs:1-8: the two top bits must be zero). */
 PTXSTD_API int ptxstd_cvt_e2m3_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
 PTXSTD_API int ptxstd_cvt_e3m2_to_f32(const uint8_t* d_codes, float* d_out, size_t n, ptxstd_stream stream);
+/* Vector<E, N>::from_f16::<RELU> (src/data_types/narrow.rs:164-172, :363-395): f16 bit patterns ->
+ * narrow codes, RN .satfinite, the same rules as from_f32 (f16 widens to f32 exactly). FP8 uses
+ * cvt.rn.satfinite{.relu}.<fmt>x2.f16x2; FP6 and FP4, whose f16x2 forms this toolchain's ptxas
+ * does not accept, convert the exactly widened f32. E2M1 output packed two per byte (n even). */
+PTXSTD_API int ptxstd_cvt_f16_to_e4m3(const uint16_t* d_x, uint8_t* d_out, size_t n, int relu, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_f16_to_e5m2(const uint16_t* d_x, uint8_t* d_out, size_t n, int relu, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_f16_to_e2m1x2(const uint16_t* d_x, uint8_t* d_out, size_t n, int relu, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_f16_to_e2m3(const uint16_t* d_x, uint8_t* d_out, size_t n, int relu, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_f16_to_e3m2(const uint16_t* d_x, uint8_t* d_out, size_t n, int relu, ptxstd_stream stream);
+/* Vector<E, N>::to_f16 (narrow.rs:275-291): exact f16 bit patterns via cvt.rn.f16x2.<fmt>x2 (e2m1x2
+ * decodes 2 * n_bytes values). */
+PTXSTD_API int ptxstd_cvt_e4m3_to_f16(const uint8_t* d_codes, uint16_t* d_out, size_t n, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_e5m2_to_f16(const uint8_t* d_codes, uint16_t* d_out, size_t n, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_e2m1x2_to_f16(const uint8_t* d_codes, uint16_t* d_out, size_t n_bytes, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_e2m3_to_f16(const uint8_t* d_codes, uint16_t* d_out, size_t n, ptxstd_stream stream);
+PTXSTD_API int ptxstd_cvt_e3m2_to_f16(const uint8_t* d_codes, uint16_t* d_out, size_t n, ptxstd_stream stream);
+/* bf16xN::from_f32::<R, O> (src/data_types/bfloat16.rs:104-118, :446-454): RN, relu clamps negative
+ * results (and -0) to +0, satfinite clamps overflow to the largest finite bf16 (else infinity);
+ * every NaN becomes 0x7FFF. */
+PTXSTD_API int ptxstd_cvt_f32_to_bf16(const float* d_x, uint16_t* d_out, size_t n, int relu, int satfinite,
+                           ptxstd_stream stream);
 /* Vector<E, N>::to_bf16_scaled::<RELU, OVERFLOW> (src/data_types/narrow.rs:314-330, :444-465):
  * element i times the UE8M0 scale d_scales[i / block] (2^(s-127); 0xff is NaN), rounded to bf16
  * (RN). relu clamps negative results to +0; satfinite clamps results outside the finite range to
@@ -147,7 +168,8 @@ PTXSTD_API int ptxstd_cvt_f32_to_f16_rs(const float* d_x, const uint32_t* d_rbit
  * 6 ue8m0 RZ satfinite, 7 ue8m0 RP satfinite, 8 e2m3, 9 e3m2, 10-11 the same with .relu;
  * stochastic rounding: 12 e4m3, 13 e5m2, 14 e2m3, 15 e3m2, 16 e2m1 (nibble per byte), 17-21 the
  * same with .relu, then two bytes per input: 22 bf16, 23 .relu, 24 .satfinite, 25 both, 26-29
- * the same for f16. Pattern p of a stochastic variant takes the random bits of group p / 4
+ * the same for f16; 30-33 bf16 round-to-nearest: plain, .relu, .satfinite, both (two bytes per
+ * input). Pattern p of a stochastic variant takes the random bits of group p / 4
  * (p / 2 for bf16/f16): word (group % 2) of SplitMix64 output group / 2 from the seed
  * 0x2545F4914F6CDD1D (the generator of ptxstd_quantize_mxfp8_rs). base + n <= 2^32; base % 4 == 0
  * for the stochastic variants. */

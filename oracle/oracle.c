@@ -238,6 +238,17 @@ uint16_t ptxo_f32_to_bf16(float x) {
 }
 float ptxo_bf16_to_f32(uint16_t h) { return u2f((uint32_t)h << 16); }
 
+uint16_t ptxo_f32_to_bf16_mode(float x, int relu, int satfinite) {
+    uint32_t u = f2u(x);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0x7FFF;
+    if (relu && (u >> 31)) return 0;
+    uint32_t lsb = (u >> 16) & 1;
+    uint32_t r = (u & 0x7FFFFFFFu) == 0x7F800000u ? u : u + 0x7FFFu + lsb;
+    uint16_t h = (uint16_t)(r >> 16);
+    if (satfinite && (h & 0x7FFF) == 0x7F80) h = (uint16_t)((h & 0x8000) | 0x7F7F);
+    return h;
+}
+
 /* ------------------------------------------------------------------------------------------ */
 /* scaled up-conversion to bf16                                                               */
 /* ------------------------------------------------------------------------------------------ */
@@ -250,6 +261,19 @@ static float narrow_value(int format, uint8_t code) {
     case PTXO_E3M2: return ptxo_e3m2_to_f32(code);
     default: return ptxo_e2m1_to_f32(code);
     }
+}
+
+uint16_t ptxo_narrow_to_f16(int format, uint8_t code) {
+    float v = narrow_value(format, code);
+    if (v != v) return 0x7FFF;
+    uint32_t u = f2u(v), sign = (u >> 16) & 0x8000u, a = u & 0x7FFFFFFFu;
+    if (a == 0) return (uint16_t)sign;
+    if (a == 0x7F800000u) return (uint16_t)(sign | 0x7C00u);
+    int e = (int)(a >> 23) - 127;
+    uint32_t m = (a & 0x7FFFFFu) | 0x800000u;
+    if (e >= -14) /* normal f16: the narrow value has at most 4 significant bits, exact */
+        return (uint16_t)(sign | ((uint32_t)(e + 15) << 10) | ((m >> 13) & 0x3FFu));
+    return (uint16_t)(sign | (m >> (13 + (-14 - e)))); /* subnormal f16, exact (>= 2^-24) */
 }
 
 uint16_t ptxo_to_bf16_scaled(int format, uint8_t code, uint8_t scale, int relu, int satfinite) {
@@ -568,6 +592,10 @@ uint32_t ptxo_sweep_code(int variant, uint64_t p) {
         uint32_t rb = ptxo_sr_rbits(PTXO_SWEEP_SEED, p >> 2);
         uint32_t r = ptxo_rs_random(fmt == PTXO_E2M1 ? PTXO_RS_E2M1 : PTXO_RS_X4, rb, (int)(p & 3));
         return ptxo_f32_to_narrow_rs(fmt, x, r, relu);
+    }
+    if (variant >= PTXO_V_BF16_RN) {
+        int w = variant - PTXO_V_BF16_RN;
+        return ptxo_f32_to_bf16_mode(x, w & 1, (w >> 1) & 1);
     }
     int v = variant - PTXO_V_BF16_RS;
     int bf = v < 4, relu = v & 1, sat = (v >> 1) & 1;

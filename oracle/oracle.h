@@ -63,6 +63,12 @@ uint8_t ptxo_f32_to_ue8m0(float x, int rnd_up, int satfinite);
 
 /* bf16 helpers (src/data_types/bfloat16.rs:76-86): RNE f32 -> bf16 and the exact widening. */
 uint16_t ptxo_f32_to_bf16(float x);
+/* cvt.rn{.relu}{.satfinite}.bf16x2.f32 of one value (bfloat16.rs:446-454): RN; every NaN becomes
+ * 0x7FFF; relu maps negative results and -0 to +0; satfinite clamps overflow to 0x7F7F / 0xFF7F. */
+uint16_t ptxo_f32_to_bf16_mode(float x, int relu, int satfinite);
+/* Exact f16 bit pattern of a narrow code (format PTXO_E4M3 .. PTXO_E3M2; E2M1 as a nibble); NaN
+ * codes give 0x7FFF. */
+uint16_t ptxo_narrow_to_f16(int format, uint8_t code);
 float ptxo_bf16_to_f32(uint16_t h);
 
 /* to_bf16_scaled::<RELU, OVERFLOW> (src/data_types/narrow.rs:314-330, :444-465): the exact
@@ -136,7 +142,10 @@ enum ptxo_variant {
     PTXO_V_BF16_RS = 22, PTXO_V_BF16_RS_RELU = 23, PTXO_V_BF16_RS_SAT = 24,
     PTXO_V_BF16_RS_RELU_SAT = 25, PTXO_V_F16_RS = 26, PTXO_V_F16_RS_RELU = 27,
     PTXO_V_F16_RS_SAT = 28, PTXO_V_F16_RS_RELU_SAT = 29,
-    PTXO_NUM_VARIANTS = 30,
+    /* bf16 round-to-nearest (two bytes per input): plain, .relu, .satfinite, both */
+    PTXO_V_BF16_RN = 30, PTXO_V_BF16_RN_RELU = 31, PTXO_V_BF16_RN_SAT = 32,
+    PTXO_V_BF16_RN_RELU_SAT = 33,
+    PTXO_NUM_VARIANTS = 34,
 };
 #define PTXO_SWEEP_SEED 0x2545F4914F6CDD1Dull
 uint8_t ptxo_encode_variant(int variant, float x); /* the round-to-nearest variants 0..11 */

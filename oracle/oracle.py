@@ -24,7 +24,8 @@ VARIANT_NAMES = ["e4m3", "e5m2", "e2m1", "e4m3_relu", "e5m2_relu", "e2m1_relu", 
                  "e4m3_rs", "e5m2_rs", "e2m3_rs", "e3m2_rs", "e2m1_rs",
                  "e4m3_rs_relu", "e5m2_rs_relu", "e2m3_rs_relu", "e3m2_rs_relu", "e2m1_rs_relu",
                  "bf16_rs", "bf16_rs_relu", "bf16_rs_sat", "bf16_rs_relu_sat",
-                 "f16_rs", "f16_rs_relu", "f16_rs_sat", "f16_rs_relu_sat"]
+                 "f16_rs", "f16_rs_relu", "f16_rs_sat", "f16_rs_relu_sat",
+                 "bf16_rn", "bf16_rn_relu", "bf16_rn_sat", "bf16_rn_relu_sat"]
 # stochastic-rounding random-value kinds (ptxo_rs_random)
 RS_X4, RS_E2M1, RS_BF16, RS_F16 = 0, 1, 2, 3
 SWEEP_SEED = 0x2545F4914F6CDD1D
@@ -111,6 +112,8 @@ def _declare(L: C.CDLL) -> None:
         "ptxo_quantize_mxfp8_rs": (None, [p, i64, i64, u64, p, p, i32]),
         "ptxo_prune_24": (None, [p, i64, i64, p, p, i32]),
         "ptxo_to_bf16_scaled": (u16, [i32, u8, u8, i32, i32]),
+        "ptxo_f32_to_bf16_mode": (u16, [f32, i32, i32]),
+        "ptxo_narrow_to_f16": (u16, [i32, u8]),
         "ptxo_to_bf16_scaled_array": (None, [i32, p, p, p, C.c_size_t, C.c_size_t, i32, i32, i32]),
         "ptxo_decompress_24": (None, [p, p, i64, i64, p, i32]),
         "ptxo_gemm_mxfp8_sparse_ref": (None, [p, p, p, p, p, i64, i64, i64, p, p, i64, p, p,

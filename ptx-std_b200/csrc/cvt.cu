@@ -126,6 +126,77 @@ __global__ void __launch_bounds__(256) encode_x2_rs_kernel(const float* __restri
     }
 }
 
+// f16 -> narrow, one pair per thread step: the f16x2 instruction for FP8 (narrow.rs:164-172);
+// FP6 and FP4 through the exact f16 -> f32 widening and the f32 instruction (the same real value,
+// so the same round-to-nearest code; their f16x2 forms are not accepted by this ptxas).
+template <int OP, bool RELU>
+__device__ __forceinline__ uint32_t encode_pair_f16(uint32_t h2) {
+    if constexpr (OP == kE4M3) return dt::e4m3x2_from_f16x2<RELU>(h2);
+    else if constexpr (OP == kE5M2) return dt::e5m2x2_from_f16x2<RELU>(h2);
+    else {
+        const float2 f = dt::f16x2_to_f32(h2);
+        if constexpr (OP == kE2M1) return dt::e2m1x2_from_f32<RELU>(f.x, f.y);
+        else return encode_pair<OP, RELU>(f.x, f.y);
+    }
+}
+
+template <int OP, bool RELU>
+__global__ void __launch_bounds__(256) encode_f16_kernel(const uint16_t* __restrict__ x,
+                                                         uint8_t* __restrict__ out, size_t n) {
+    const size_t n2 = (n + 1) / 2;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t p = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; p < n2;
+         p += stride) {
+        const size_t i = 2 * p;
+        const uint32_t h2 = x[i] | (i + 1 < n ? static_cast<uint32_t>(x[i + 1]) << 16 : 0u);
+        const uint32_t c = encode_pair_f16<OP, RELU>(h2);
+        if constexpr (OP == kE2M1) {
+            out[p] = static_cast<uint8_t>(c);  // n even: two nibbles
+        } else {
+            out[i] = static_cast<uint8_t>(c);
+            if (i + 1 < n) out[i + 1] = static_cast<uint8_t>(c >> 8);
+        }
+    }
+}
+
+// narrow -> f16 bits (exact), FMT as decode_kernel.
+template <int FMT>
+__global__ void __launch_bounds__(256) to_f16_kernel(const uint8_t* __restrict__ c,
+                                                     uint16_t* __restrict__ out, size_t n) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += stride) {
+        const uint32_t b = c[i];
+        if constexpr (FMT == 2) {
+            const uint32_t h2 = dt::e2m1x2_to_f16x2(b);
+            out[2 * i] = static_cast<uint16_t>(h2);
+            out[2 * i + 1] = static_cast<uint16_t>(h2 >> 16);
+        } else {
+            uint32_t h2;
+            if constexpr (FMT == 0) h2 = dt::e4m3x2_to_f16x2(static_cast<uint16_t>(b));
+            else if constexpr (FMT == 1) h2 = dt::e5m2x2_to_f16x2(static_cast<uint16_t>(b));
+            else if constexpr (FMT == 4) h2 = dt::e2m3x2_to_f16x2(static_cast<uint16_t>(b));
+            else h2 = dt::e3m2x2_to_f16x2(static_cast<uint16_t>(b));
+            out[i] = static_cast<uint16_t>(h2);
+        }
+    }
+}
+
+// bf16::from_f32 with RELU / OVERFLOW (bfloat16.rs:104-118, :446-454), one pair per step.
+template <bool RELU, bool SAT>
+__global__ void __launch_bounds__(256) f32_to_bf16_kernel(const float* __restrict__ x,
+                                                          uint16_t* __restrict__ out, size_t n) {
+    const size_t n2 = (n + 1) / 2;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t p = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; p < n2;
+         p += stride) {
+        const size_t i = 2 * p;
+        const uint32_t r = dt::bf16x2_from_f32_mode<RELU, SAT>(x[i], i + 1 < n ? x[i + 1] : 0.0f);
+        out[i] = static_cast<uint16_t>(r);
+        if (i + 1 < n) out[i + 1] = static_cast<uint16_t>(r >> 16);
+    }
+}
+
 // Exact f32 value of one narrow code (FMT as decode_kernel: 0 e4m3, 1 e5m2, 2 e2m1 nibble,
 // 4 e2m3, 5 e3m2).
 template <int FMT>
@@ -249,6 +320,25 @@ __device__ __forceinline__ void sweep_rs(int v, uint64_t p0, float x0, float x1,
             *reinterpret_cast<uint32_t*>(out + i) = c;
         } else {
             for (uint64_t j = 0; j < valid; ++j) out[i + j] = static_cast<uint8_t>(c >> (8 * j));
+        }
+        return;
+    }
+    if (v >= 30) {  // bf16 round-to-nearest: plain, .relu, .satfinite, both
+        uint32_t c0, c1;
+        switch (v) {
+        case 30: c0 = dt::bf16x2_from_f32_mode<false, false>(x0, x1); c1 = dt::bf16x2_from_f32_mode<false, false>(x2, x3); break;
+        case 31: c0 = dt::bf16x2_from_f32_mode<true, false>(x0, x1); c1 = dt::bf16x2_from_f32_mode<true, false>(x2, x3); break;
+        case 32: c0 = dt::bf16x2_from_f32_mode<false, true>(x0, x1); c1 = dt::bf16x2_from_f32_mode<false, true>(x2, x3); break;
+        default: c0 = dt::bf16x2_from_f32_mode<true, true>(x0, x1); c1 = dt::bf16x2_from_f32_mode<true, true>(x2, x3); break;
+        }
+        uint16_t* o = reinterpret_cast<uint16_t*>(out) + i;
+        const uint16_t codes[4] = {static_cast<uint16_t>(c0), static_cast<uint16_t>(c0 >> 16),
+                                   static_cast<uint16_t>(c1), static_cast<uint16_t>(c1 >> 16)};
+        if (valid == 4) {
+            reinterpret_cast<uint32_t*>(o)[0] = c0;
+            reinterpret_cast<uint32_t*>(o)[1] = c1;
+        } else {
+            for (uint64_t j = 0; j < valid; ++j) o[j] = codes[j];
         }
         return;
     }
@@ -555,6 +645,105 @@ int ptxstd_cvt_f32_to_f16_rs(const float* d_x, const uint32_t* d_rbits, uint16_t
     return launch_x2_rs<false>(d_x, d_rbits, d_out, n, relu, satfinite, stream);
 }
 
+int ptxstd_cvt_f16_to_e4m3(const uint16_t* d_x, uint8_t* d_out, size_t n, int relu,
+                           ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_x || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int g = grid_for((n + 1) / 2);
+    return launch([&] {
+        if (relu) encode_f16_kernel<kE4M3, true><<<g, 256, 0, s>>>(d_x, d_out, n);
+        else encode_f16_kernel<kE4M3, false><<<g, 256, 0, s>>>(d_x, d_out, n);
+    });
+}
+int ptxstd_cvt_f16_to_e5m2(const uint16_t* d_x, uint8_t* d_out, size_t n, int relu,
+                           ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_x || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int g = grid_for((n + 1) / 2);
+    return launch([&] {
+        if (relu) encode_f16_kernel<kE5M2, true><<<g, 256, 0, s>>>(d_x, d_out, n);
+        else encode_f16_kernel<kE5M2, false><<<g, 256, 0, s>>>(d_x, d_out, n);
+    });
+}
+int ptxstd_cvt_f16_to_e2m1x2(const uint16_t* d_x, uint8_t* d_out, size_t n, int relu,
+                           ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_x || !d_out || (n & 1)) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int g = grid_for((n + 1) / 2);
+    return launch([&] {
+        if (relu) encode_f16_kernel<kE2M1, true><<<g, 256, 0, s>>>(d_x, d_out, n);
+        else encode_f16_kernel<kE2M1, false><<<g, 256, 0, s>>>(d_x, d_out, n);
+    });
+}
+int ptxstd_cvt_f16_to_e2m3(const uint16_t* d_x, uint8_t* d_out, size_t n, int relu,
+                           ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_x || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int g = grid_for((n + 1) / 2);
+    return launch([&] {
+        if (relu) encode_f16_kernel<kE2M3, true><<<g, 256, 0, s>>>(d_x, d_out, n);
+        else encode_f16_kernel<kE2M3, false><<<g, 256, 0, s>>>(d_x, d_out, n);
+    });
+}
+int ptxstd_cvt_f16_to_e3m2(const uint16_t* d_x, uint8_t* d_out, size_t n, int relu,
+                           ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_x || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int g = grid_for((n + 1) / 2);
+    return launch([&] {
+        if (relu) encode_f16_kernel<kE3M2, true><<<g, 256, 0, s>>>(d_x, d_out, n);
+        else encode_f16_kernel<kE3M2, false><<<g, 256, 0, s>>>(d_x, d_out, n);
+    });
+}
+int ptxstd_cvt_e4m3_to_f16(const uint8_t* d_codes, uint16_t* d_out, size_t n, ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_codes || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    return launch([&] { to_f16_kernel<0><<<grid_for(n), 256, 0, s>>>(d_codes, d_out, n); });
+}
+int ptxstd_cvt_e5m2_to_f16(const uint8_t* d_codes, uint16_t* d_out, size_t n, ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_codes || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    return launch([&] { to_f16_kernel<1><<<grid_for(n), 256, 0, s>>>(d_codes, d_out, n); });
+}
+int ptxstd_cvt_e2m1x2_to_f16(const uint8_t* d_codes, uint16_t* d_out, size_t n, ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_codes || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    return launch([&] { to_f16_kernel<2><<<grid_for(n), 256, 0, s>>>(d_codes, d_out, n); });
+}
+int ptxstd_cvt_e2m3_to_f16(const uint8_t* d_codes, uint16_t* d_out, size_t n, ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_codes || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    return launch([&] { to_f16_kernel<4><<<grid_for(n), 256, 0, s>>>(d_codes, d_out, n); });
+}
+int ptxstd_cvt_e3m2_to_f16(const uint8_t* d_codes, uint16_t* d_out, size_t n, ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_codes || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    return launch([&] { to_f16_kernel<5><<<grid_for(n), 256, 0, s>>>(d_codes, d_out, n); });
+}
+int ptxstd_cvt_f32_to_bf16(const float* d_x, uint16_t* d_out, size_t n, int relu, int satfinite,
+                           ptxstd_stream stream) {
+    if (n == 0) return PTXSTD_OK;
+    if (!d_x || !d_out) return PTXSTD_EINVAL;
+    auto s = static_cast<cudaStream_t>(stream);
+    const int g = grid_for((n + 1) / 2);
+    return launch([&] {
+        if (relu && satfinite) f32_to_bf16_kernel<true, true><<<g, 256, 0, s>>>(d_x, d_out, n);
+        else if (relu) f32_to_bf16_kernel<true, false><<<g, 256, 0, s>>>(d_x, d_out, n);
+        else if (satfinite) f32_to_bf16_kernel<false, true><<<g, 256, 0, s>>>(d_x, d_out, n);
+        else f32_to_bf16_kernel<false, false><<<g, 256, 0, s>>>(d_x, d_out, n);
+    });
+}
+
 int ptxstd_cvt_e4m3_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scales,
                                    uint16_t* d_out, size_t n, size_t block, int relu,
                                    int satfinite, ptxstd_stream stream) {
@@ -584,7 +773,7 @@ int ptxstd_cvt_e3m2_to_bf16_scaled(const uint8_t* d_codes, const uint8_t* d_scal
 int ptxstd_cvt_sweep(int variant, uint64_t base, uint64_t n, uint8_t* d_out,
                      ptxstd_stream stream) {
     if (n == 0) return PTXSTD_OK;
-    if (!d_out || variant < 0 || variant > 29 || base + n > (1ull << 32) ||
+    if (!d_out || variant < 0 || variant > 33 || base + n > (1ull << 32) ||
         (reinterpret_cast<uintptr_t>(d_out) & 3) || (variant >= 12 && (base & 3)))
         return PTXSTD_EINVAL;
     auto s = static_cast<cudaStream_t>(stream);

@@ -136,6 +136,29 @@ __device__ __forceinline__ uint64_t splitmix64(uint64_t seed, uint64_t i) {
     return z ^ (z >> 31);
 }
 
+// ---- f16 -> narrow ------------------------------------------------------------------------------
+// f8e4m3x2 / f8e5m2x2::pair_from_f16 (narrow.rs:164-172): cvt.rn.satfinite{.relu}.e4m3x2.f16x2,
+// element 0 in the low half of the f16x2 word and in the low byte of the result.
+template <bool RELU>
+__device__ __forceinline__ uint16_t e4m3x2_from_f16x2(uint32_t h2) {
+    uint16_t r;
+    if constexpr (RELU) asm("cvt.rn.satfinite.relu.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(h2));
+    else asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(h2));
+    return r;
+}
+template <bool RELU>
+__device__ __forceinline__ uint16_t e5m2x2_from_f16x2(uint32_t h2) {
+    uint16_t r;
+    if constexpr (RELU) asm("cvt.rn.satfinite.relu.e5m2x2.f16x2 %0, %1;" : "=h"(r) : "r"(h2));
+    else asm("cvt.rn.satfinite.e5m2x2.f16x2 %0, %1;" : "=h"(r) : "r"(h2));
+    return r;
+}
+// The exact f16 -> f32 widening of both halves (element 0 = low half).
+__device__ __forceinline__ float2 f16x2_to_f32(uint32_t h2) {
+    __half2 h = *reinterpret_cast<__half2*>(&h2);
+    return __half22float2(h);
+}
+
 // f8e8m0x2::pair_from_f32::<RND, OVERFLOW> (narrow.rs:600-617): RZ or RP, optional .satfinite.
 template <bool ROUND_UP, bool SATFINITE>
 __device__ __forceinline__ uint16_t ue8m0x2_from_f32(float x0, float x1) {
@@ -189,6 +212,32 @@ __device__ __forceinline__ float2 e3m2x2_to_f32(uint16_t codes) {
     uint32_t h2;
     asm("cvt.rn.f16x2.e3m2x2 %0, %1;" : "=r"(h2) : "h"(codes));
     return half2_bits_to_float2(h2);
+}
+// to_f16 (narrow.rs:275-291): the exact cvt.rn.f16x2.<fmt>x2 result itself.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t c) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(c));
+    return h2;
+}
+__device__ __forceinline__ uint32_t e5m2x2_to_f16x2(uint16_t c) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e5m2x2 %0, %1;" : "=r"(h2) : "h"(c));
+    return h2;
+}
+__device__ __forceinline__ uint32_t e2m3x2_to_f16x2(uint16_t c) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e2m3x2 %0, %1;" : "=r"(h2) : "h"(c));
+    return h2;
+}
+__device__ __forceinline__ uint32_t e3m2x2_to_f16x2(uint16_t c) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e3m2x2 %0, %1;" : "=r"(h2) : "h"(c));
+    return h2;
+}
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+    uint32_t h2;
+    asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h2) : "r"(byte));
+    return h2;
 }
 // ue8m0 to_f32 = to_bf16 then widening (narrow.rs:683-690): cvt.rn.bf16x2.ue8m0x2.
 __device__ __forceinline__ float2 ue8m0x2_to_f32(uint16_t codes) {

@@ -63,6 +63,23 @@ _SIGS = {
                                                  C.c_size_t, C.c_int, C.c_int, C.c_void_p]),
     "ptxstd_cvt_e3m2_to_bf16_scaled": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
                                                  C.c_size_t, C.c_int, C.c_int, C.c_void_p]),
+    "ptxstd_cvt_f16_to_e4m3": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
+                                          C.c_void_p]),
+    "ptxstd_cvt_e4m3_to_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ptxstd_cvt_f16_to_e5m2": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
+                                          C.c_void_p]),
+    "ptxstd_cvt_e5m2_to_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ptxstd_cvt_f16_to_e2m1x2": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
+                                          C.c_void_p]),
+    "ptxstd_cvt_e2m1x2_to_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ptxstd_cvt_f16_to_e2m3": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
+                                          C.c_void_p]),
+    "ptxstd_cvt_e2m3_to_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ptxstd_cvt_f16_to_e3m2": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
+                                          C.c_void_p]),
+    "ptxstd_cvt_e3m2_to_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ptxstd_cvt_f32_to_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_int,
+                                         C.c_void_p]),
     "ptxstd_cvt_f32_to_e4m3_rs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
                                             C.c_int, C.c_void_p]),
     "ptxstd_cvt_f32_to_e5m2_rs": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,

@@ -41,6 +41,45 @@ def from_f32(fmt: str, x, relu: bool = False, stream=None):
     return out
 
 
+_F16 = {E4M3: "e4m3", E5M2: "e5m2", E2M1: "e2m1x2", E2M3: "e2m3", E3M2: "e3m2"}
+
+
+def from_f16(fmt: str, x, relu: bool = False, stream=None):
+    """Vector<fmt, N>::from_f16 (narrow.rs:164-172): float16 tensor -> codes (RN .satfinite)."""
+    torch = _torch()
+    if x.dtype != torch.float16:
+        raise TypeError("expected float16")
+    x = x.contiguous()
+    n = x.numel()
+    out = torch.empty(n // 2 if fmt == E2M1 else n, dtype=torch.uint8, device=x.device)
+    check(getattr(lib(), f"ptxstd_cvt_f16_to_{_F16[fmt]}")(_dev(x), _dev(out), n, int(relu),
+                                                            _stream(stream)), f"from_f16({fmt})")
+    return out
+
+
+def to_f16(fmt: str, codes, stream=None):
+    """Vector<fmt, N>::to_f16 (narrow.rs:275-291): exact float16 values of the codes."""
+    torch = _torch()
+    codes = codes.contiguous()
+    n = codes.numel()
+    out = torch.empty(2 * n if fmt == E2M1 else n, dtype=torch.float16, device=codes.device)
+    check(getattr(lib(), f"ptxstd_cvt_{_F16[fmt]}_to_f16")(_dev(codes), _dev(out), n,
+                                                            _stream(stream)), f"to_f16({fmt})")
+    return out
+
+
+def bf16_from_f32(x, relu: bool = False, satfinite: bool = False, stream=None):
+    """bf16xN::from_f32::<R, O> (bfloat16.rs:104-118): bf16 bit patterns (int16), RN."""
+    torch = _torch()
+    if x.dtype != torch.float32:
+        raise TypeError("expected float32")
+    x = x.contiguous()
+    out = torch.empty(x.numel(), dtype=torch.int16, device=x.device)
+    check(lib().ptxstd_cvt_f32_to_bf16(_dev(x), _dev(out), x.numel(), int(relu), int(satfinite),
+                                       _stream(stream)), "bf16_from_f32")
+    return out
+
+
 def from_bf16(fmt: str, x, relu: bool = False, stream=None):
     """Vector<fmt, N>::from_bf16 (narrow.rs:363-395): bf16 widens to f32 exactly, so the RN
     conversion of the widened value is the same rounding of the same real number."""
@@ -148,7 +187,7 @@ def ue8m0_to_f32(codes, stream=None):
 
 
 def sweep_width(variant: int) -> int:
-    """Bytes per input of a sweep variant: 2 for the bf16/f16 stochastic forms (22..29)."""
+    """Bytes per input of a sweep variant: 2 for the bf16/f16 forms (22..33)."""
     return 2 if variant >= 22 else 1
 
 

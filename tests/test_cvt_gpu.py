@@ -205,3 +205,56 @@ def test_to_bf16_scaled_exhaustive(cuda, oracle, fmt):
     got = _to_np(dt.to_bf16_scaled(fmt, torch.from_numpy(rc).cuda(), torch.from_numpy(rs).cuda(),
                                    32)).view(np.uint16)
     assert np.array_equal(got, oracle.to_bf16_scaled(ofmt, rc, rs, m, 32))
+
+
+# ---- f16 sources, f16 results, bf16 round-to-nearest modes -----------------------------------------
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2", "e2m3", "e3m2", "e2m1"])
+def test_from_f16_all_patterns(cuda, oracle, fmt):
+    """All 65536 f16 bit patterns, with and without .relu: the device codes equal the oracle's
+    encoding of the exactly widened f32 value (FP8 through the hardware f16x2 instruction)."""
+    import ptxstd.data_types as dt
+    torch = cuda
+    ofmt = {"e4m3": oracle.E4M3, "e5m2": oracle.E5M2, "e2m3": oracle.E2M3, "e3m2": oracle.E3M2,
+            "e2m1": oracle.E2M1}[fmt]
+    h = np.arange(1 << 16, dtype=np.uint16)
+    xd = torch.from_numpy(h.view(np.int16)).cuda().view(torch.float16)
+    for relu in (False, True):
+        got = _to_np(dt.from_f16(fmt, xd, relu))
+        want = oracle.encode(ofmt, h.view(np.float16).astype(np.float32), relu)
+        bad = np.nonzero(got != want)[0]
+        assert bad.size == 0, (relu, [(hex(int(h[i])), hex(got[i]), hex(want[i])) for i in bad[:6]])
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2", "e2m3", "e3m2", "e2m1"])
+def test_to_f16_every_code(cuda, oracle, fmt):
+    import ptxstd.data_types as dt
+    torch = cuda
+    ofmt = {"e4m3": oracle.E4M3, "e5m2": oracle.E5M2, "e2m3": oracle.E2M3, "e3m2": oracle.E3M2,
+            "e2m1": oracle.E2M1}[fmt]
+    ncodes = {"e4m3": 256, "e5m2": 256, "e2m3": 64, "e3m2": 64, "e2m1": 16}[fmt]
+    codes = np.arange(ncodes, dtype=np.uint8)
+    dev = (codes[0::2] | (codes[1::2] << 4)).astype(np.uint8) if fmt == "e2m1" else codes
+    got = _to_np(dt.to_f16(fmt, torch.from_numpy(dev).cuda()).view(torch.int16)).view(np.uint16)
+    L = oracle.lib()
+    want = np.array([L.ptxo_narrow_to_f16(ofmt, int(c)) for c in codes], dtype=np.uint16)
+    assert np.array_equal(got, want), [(int(c), hex(g), hex(w)) for c, g, w in zip(codes, got, want)
+                                       if g != w][:6]
+
+
+def test_bf16_from_f32_modes(cuda, oracle):
+    """The element-wise bf16 conversion in its four modes on random bit patterns plus specials
+    (the exhaustive pin is the sweep's bf16_rn variants)."""
+    import ptxstd.data_types as dt
+    torch = cuda
+    rng = np.random.default_rng(12)
+    bits = rng.integers(0, 1 << 32, 1 << 20, dtype=np.uint64).astype(np.uint32)
+    bits[:8] = [0, 0x80000000, 0x7F800000, 0xFF800000, 0x7FC00001, 0x7F7FFFFF, 0xFF7FFFFF, 1]
+    x = bits.view(np.float32)
+    L = oracle.lib()
+    for relu in (False, True):
+        for sat in (False, True):
+            got = _to_np(dt.bf16_from_f32(torch.from_numpy(x).cuda(), relu, sat)).view(np.uint16)
+            want = np.array([L.ptxo_f32_to_bf16_mode(float(v), relu, sat) for v in x[:4096]],
+                            dtype=np.uint16)
+            assert np.array_equal(got[:4096], want), (relu, sat)

@@ -289,7 +289,7 @@ DIGESTS = os.path.join(GOLDEN, "cvt_sweep_digests.json")
 
 
 @pytest.mark.skipif(not os.path.exists(DIGESTS), reason="no hardware digests recorded yet")
-@pytest.mark.parametrize("variant", range(30))
+@pytest.mark.parametrize("variant", range(34))
 def test_oracle_matches_hardware_digests(oracle, variant):
     """The oracle's codes for all 2^32 f32 inputs hash to the digests of the B200's own `cvt`
     outputs (the reference's encoders are those instructions). A few chunks are checked by
@@ -506,3 +506,29 @@ def test_to_bf16_scaled_exact_in_range(oracle):
         ok = np.isfinite(v) & ((np.abs(v) >= 2.0 ** -126) | (v == 0)) & (np.abs(v) < 2.0 ** 127)
         want = (v[ok].astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
         assert np.array_equal(got[ok], want)
+
+
+def test_narrow_to_f16_exact(oracle):
+    """The f16 pattern of every code is the exact value (numpy's float16 of the decode)."""
+    L = oracle.lib()
+    for fmt, n in [(oracle.E4M3, 256), (oracle.E5M2, 256), (oracle.E2M3, 64), (oracle.E3M2, 64),
+                   (oracle.E2M1, 16)]:
+        for c in range(n):
+            v = oracle.decode(fmt, np.array([c if fmt != oracle.E2M1 else c], dtype=np.uint8))
+            v = v[0] if fmt != oracle.E2M1 else v[0]
+            got = L.ptxo_narrow_to_f16(fmt, c)
+            if np.isnan(v):
+                assert got == 0x7FFF
+            else:
+                assert got == int(np.float16(v).view(np.uint16)), (fmt, c)
+
+
+def test_bf16_mode_rules(oracle):
+    L = oracle.lib()
+    f = lambda bits, r=0, s=0: L.ptxo_f32_to_bf16_mode(float(np.uint32(bits).view(np.float32)), r, s)  # noqa: E731
+    assert f(0x3F800000) == 0x3F80                      # 1.0
+    assert f(0x3F808000) == 0x3F80                      # tie to even
+    assert f(0x3F818000) == 0x3F82                      # tie to even (up)
+    assert f(0x7F7FFFFF) == 0x7F80 and f(0x7F7FFFFF, 0, 1) == 0x7F7F   # rounds past max
+    assert f(0xFF800000, 0, 1) == 0xFF7F and f(0xFF800000, 1, 0) == 0
+    assert f(0x80000000, 1, 0) == 0 and f(0x7FC00001) == 0x7FFF
