@@ -55,7 +55,7 @@ def test_host_validation_without_gpu(ptxstd_lib):
     assert L.ptxstd_quantize_nvfp4(None, 128, 64, 0.0, None, None, None) == EINVAL
     assert L.ptxstd_quantize_nvfp4_layout(16, 128, 64, 1.0, 16, 16, 2, None) == EINVAL
     assert L.ptxstd_cvt_f32_to_e2m1x2(16, 16, 3, 0, None) == EINVAL
-    assert L.ptxstd_cvt_sweep(30, 0, 16, 16, None) == EINVAL
+    assert L.ptxstd_cvt_sweep(34, 0, 16, 16, None) == EINVAL
     assert L.ptxstd_cvt_sweep(12, 2, 16, 16, None) == EINVAL      # stochastic: base % 4
     assert L.ptxstd_cvt_f32_to_e2m1x2_rs(16, 16, 16, 3, 0, None) == EINVAL   # odd n
     assert L.ptxstd_cvt_f32_to_e4m3_rs(8, 16, 16, 4, 0, None) == EINVAL      # x not 16-aligned
