@@ -536,7 +536,9 @@ class Nvfp4Gemm:
 
 class DecodeGemm:
     """Decode step: x bf16 [16, 8192] (MXFP8 in the call) x NVFP4 W [57344, 8192] -> bf16
-    [16, 57344]; W is sharded along N across ranks and the output columns are all-gathered."""
+    [16, 57344]; W is sharded along N across ranks and every rank ends with all output columns:
+    with `gather` "p2p" (default) the decode epilogue stores them into every rank's output over
+    NVLink peer memory, with "nccl" an NCCL all-gather follows the GEMM."""
 
     name = "decode_gemm"
     unit = "GB/s"
@@ -548,6 +550,7 @@ class DecodeGemm:
 
     def __init__(self, world: int = 1):
         self.world = world
+        self.gather = "p2p"
         self.n_local = self.N // world
         w_bytes = self.n_local * self.K // 2 + self.n_local * self.K // 16
         self.bytes = w_bytes + self.M * self.K * 2 + self.M * self.n_local * 2
@@ -556,7 +559,7 @@ class DecodeGemm:
         self.gather_bytes = (world - 1) * self.M * self.n_local * 2  # NVLink bytes in per rank
         self.config = {"workload": "decode_gemm x[16,8192] bf16 -> mxfp8, W nvfp4 [57344,8192]",
                        "M": self.M, "N": self.N, "K": self.K, "n_per_gpu": self.n_local,
-                       "sharding": "W along N, NCCL all-gather of output columns",
+                       "sharding": "W along N, output columns gathered to every rank",
                        "l2": "weights 252 MiB per step (> L2), 2 rotating weight copies"}
 
     def host_input(self):
@@ -585,6 +588,12 @@ class DecodeGemm:
         if self.world > 1:
             from ptxstd.dist import Dist
             self.dist = Dist.from_torch()
+            self.config["sharding"] = (
+                "W along N; the decode epilogue stores each rank's columns into every rank's "
+                "output over NVLink (CUDA IPC peer memory), no collective" if self.gather == "p2p"
+                else "W along N, NCCL all-gather of output columns + device unshard permute")
+            if self.gather == "p2p":
+                self.y = self.dist.decode_p2p_output(self.N)
 
     def _decode(self, i):
         import ptxstd
@@ -592,6 +601,10 @@ class DecodeGemm:
         if self.dist is None:
             ptxstd.gemm_decode(self.x, w, sfw, gw, out=self.y)
             return 2
+        if self.gather == "p2p":
+            # prep, decode with peer stores into every rank's y, completion wait
+            self.dist.gemm_decode_p2p(self.x, w, sfw, gw, self.N)
+            return 3
         # local shard, in-place NCCL all-gather over NVLink, device-side unshard permute
         self.dist.gemm_decode(self.x, w, sfw, gw, self.N, out=self.y)
         return 3
@@ -833,10 +846,15 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the timed steps eagerly instead of replaying a CUDA graph")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+                    help="decode_gemm on several GPUs: output columns stored into every rank "
+                         "over NVLink peer memory by the GEMM itself, or NCCL all-gather")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     wl = WORKLOADS[args.workload](int(os.environ.get("WORLD_SIZE", "1")))
+    if hasattr(wl, "gather"):
+        wl.gather = args.gather
     res = run_reference(args, wl) if args.impl == "reference" else run_ours(args, wl)
     if res is not None:
         print(json.dumps(res), flush=True)

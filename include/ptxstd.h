@@ -324,6 +324,23 @@ PTXSTD_API int ptxstd_gemm_decode_sharded(const ptxstd_dist* dist, const uint16_
                                           int64_t K, void* d_workspace, size_t workspace_bytes,
                                           ptxstd_stream stream);
 
+/* The decode GEMM with the all-gather fused into it: every rank's epilogue stores each finished
+ * [M, 128] output block straight into every rank's y over NVLink (CUDA IPC peer mappings), with
+ * monotonic counters and bounded waits in place of a collective, so a step is two kernels plus a
+ * one-block completion wait and can be captured in a CUDA graph. Setup, once per communicator
+ * and N (collective: every rank calls it): this rank's y [16, N] bf16 row-major, owned by the
+ * library until ptxstd_dist_free, is returned in *d_y. A step (collective): rows 0..M-1 of that y
+ * hold the full product when the stream reaches the end of the call; with d_y_copy non-null they
+ * are also copied there. Steps of one communicator must be issued in the same order on every
+ * rank. N % (128 * world) == 0; at most 8 ranks; workspace as ptxstd_gemm_decode_workspace_bytes
+ * (M, N / world, K). */
+PTXSTD_API int ptxstd_dist_decode_p2p_init(ptxstd_dist* dist, int64_t N, uint16_t** d_y);
+PTXSTD_API int ptxstd_gemm_decode_sharded_p2p(const ptxstd_dist* dist, const uint16_t* d_x,
+                                              const uint8_t* d_w_shard, const uint8_t* d_sfw_shard,
+                                              float gw, uint16_t* d_y_copy, int64_t M, int64_t N,
+                                              int64_t K, void* d_workspace, size_t workspace_bytes,
+                                              ptxstd_stream stream);
+
 /* ---- tcgen05 descriptors (src/tcgen05/descriptor.rs) ---------------------------------------- */
 /* InstrDescriptor::<KIND>::new for each kind. Element types use the reference's discriminants:
  * F16ElementType F16 0 / Bf16 1; FloatAccumulator F16 0 / F32 1; F8f6f4ElementType E4m3 0,

@@ -138,6 +138,15 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Release/acquire fences (the lighter alternative fence.rs:33-40 points to beside fence_seq_cst):
+// order this thread's earlier accesses before its later ones for threads of the GPU / system,
+// without joining the total order of fence.sc.
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
 
 // ---- TMA (src/tma/tensor.rs) -----------------------------------------------------------------
 // tma_load_tile::<2> (:214-236): 2-D tile global -> this CTA's smem, completing on `bar`.

@@ -7,6 +7,10 @@
 //     writing its [M, N/world] output block into its slot of a rank-major gather buffer, NCCL
 //     all-gathers that buffer in place over NVLink, and a small kernel permutes the rank-major
 //     blocks [world][M][N/world] into row-major y [M, N].
+//   - ptxstd_gemm_decode_sharded_p2p: the same product with the gather fused into the GEMM: the
+//     epilogue that finalises an output block stores it straight into every rank's y over NVLink
+//     (CUDA IPC peer mappings of a buffer each rank allocates once), with the counters and bounded
+//     waits of decode_out.h in place of a collective.
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2; the copy a host process such as torch has
 // already loaded is reused), so the library itself loads on machines without NCCL. The reference
@@ -17,14 +21,20 @@
 #include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
+#include "decode_out.h"
 
 struct ptxstd_dist {
     ncclComm_t comm;
     int nranks;
     int rank;
     int device;
+    // peer-to-peer decode output (ptxstd_dist_decode_p2p_init)
+    uint8_t* p2p_local = nullptr;                       // this rank's y [16][N] + signal words
+    uint8_t* p2p_peer[ptxstd::decode::kMaxRanks] = {};  // every rank's buffer, mapped here
+    int64_t p2p_n = 0;
 };
 
 namespace {
@@ -104,6 +114,25 @@ int ptxstd_dist_free(ptxstd_dist* d) {
     if (!d) return PTXSTD_OK;
     Nccl& n = nccl();
     int st = PTXSTD_OK;
+    if (d->p2p_local) {
+        // every rank unmaps the peers' buffers, then all ranks meet before any buffer is freed
+        if (cudaDeviceSynchronize() != cudaSuccess) st = PTXSTD_ECUDA;
+        for (int r = 0; r < d->nranks; ++r)
+            if (r != d->rank && d->p2p_peer[r] && cudaIpcCloseMemHandle(d->p2p_peer[r]) != cudaSuccess)
+                st = PTXSTD_ECUDA;
+        if (n.ok && d->comm) {
+            uint8_t* tmp = nullptr;
+            if (cudaMalloc(&tmp, 16 * static_cast<size_t>(d->nranks)) != cudaSuccess) {
+                st = PTXSTD_ECUDA;
+            } else {
+                if (n.all_gather(tmp + 16 * d->rank, tmp, 16, ncclUint8, d->comm, 0) != ncclSuccess)
+                    st = PTXSTD_ENCCL;
+                if (cudaDeviceSynchronize() != cudaSuccess) st = PTXSTD_ECUDA;
+                cudaFree(tmp);
+            }
+        }
+        if (cudaFree(d->p2p_local) != cudaSuccess) st = PTXSTD_ECUDA;
+    }
     if (n.ok && d->comm && n.comm_destroy(d->comm) != ncclSuccess) st = PTXSTD_ENCCL;
     delete d;
     return st;
@@ -167,6 +196,103 @@ int ptxstd_gemm_decode_sharded(const ptxstd_dist* d, const uint16_t* d_x, const 
                                                 static_cast<uint32_t>(d->nranks),
                                                 static_cast<uint32_t>(M), ns8);
     return ptxstd::launch_status();
+}
+
+namespace {
+constexpr int64_t kP2pRows = 16;
+size_t p2p_y_bytes(int64_t N) {
+    return (static_cast<size_t>(kP2pRows) * static_cast<size_t>(N) * 2 + 255) &
+           ~static_cast<size_t>(255);
+}
+}  // namespace
+
+int ptxstd_dist_decode_p2p_init(ptxstd_dist* d, int64_t N, uint16_t** d_y) {
+    namespace pd = ptxstd::decode;
+    if (!d || !d_y || N <= 0 || N % d->nranks != 0 || d->nranks > static_cast<int>(pd::kMaxRanks))
+        return PTXSTD_EINVAL;
+    if (d->p2p_local) return PTXSTD_EINVAL;  // once per communicator
+    Nccl& n = nccl();
+    if (!n.ok) return PTXSTD_ENCCL;
+    const size_t bytes = p2p_y_bytes(N) + pd::kSigWords * sizeof(uint32_t);
+    uint8_t* buf = nullptr;
+    if (cudaMalloc(&buf, bytes) != cudaSuccess) return PTXSTD_ECUDA;
+    // zeroed (counters at 0) before any peer can learn the handle
+    if (cudaMemset(buf, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(buf);
+        return PTXSTD_ECUDA;
+    }
+    cudaIpcMemHandle_t h;
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    if (cudaIpcGetMemHandle(&h, buf) != cudaSuccess) {
+        cudaFree(buf);
+        return PTXSTD_ECUDA;
+    }
+    // every rank's handle, gathered with one NCCL all-gather through a device staging buffer
+    uint8_t* stage = nullptr;
+    std::vector<uint8_t> all(64 * static_cast<size_t>(d->nranks));
+    int st = PTXSTD_OK;
+    if (cudaMalloc(&stage, all.size()) != cudaSuccess) st = PTXSTD_ECUDA;
+    if (!st && cudaMemcpy(stage + 64 * d->rank, &h, 64, cudaMemcpyHostToDevice) != cudaSuccess)
+        st = PTXSTD_ECUDA;
+    if (!st && n.all_gather(stage + 64 * d->rank, stage, 64, ncclUint8, d->comm, 0) != ncclSuccess)
+        st = PTXSTD_ENCCL;
+    if (!st && (cudaMemcpy(all.data(), stage, all.size(), cudaMemcpyDeviceToHost) != cudaSuccess))
+        st = PTXSTD_ECUDA;
+    if (stage) cudaFree(stage);
+    for (int r = 0; !st && r < d->nranks; ++r) {
+        if (r == d->rank) {
+            d->p2p_peer[r] = buf;
+            continue;
+        }
+        cudaIpcMemHandle_t hr;
+        memcpy(&hr, all.data() + 64 * r, 64);
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+            st = PTXSTD_ECUDA;
+        d->p2p_peer[r] = static_cast<uint8_t*>(p);
+    }
+    if (st) {
+        for (int r = 0; r < d->nranks; ++r)
+            if (r != d->rank && d->p2p_peer[r]) cudaIpcCloseMemHandle(d->p2p_peer[r]);
+        memset(d->p2p_peer, 0, sizeof(d->p2p_peer));
+        cudaFree(buf);
+        return st;
+    }
+    d->p2p_local = buf;
+    d->p2p_n = N;
+    *d_y = reinterpret_cast<uint16_t*>(buf);
+    return PTXSTD_OK;
+}
+
+int ptxstd_gemm_decode_sharded_p2p(const ptxstd_dist* d, const uint16_t* d_x,
+                                   const uint8_t* d_w_shard, const uint8_t* d_sfw_shard, float gw,
+                                   uint16_t* d_y, int64_t M, int64_t N, int64_t K,
+                                   void* d_workspace, size_t workspace_bytes,
+                                   ptxstd_stream stream) {
+    namespace pd = ptxstd::decode;
+    if (!d || !d->p2p_local || N != d->p2p_n || M <= 0 || M > kP2pRows || !d_workspace)
+        return PTXSTD_EINVAL;
+    const int64_t ns = N / d->nranks;
+    if (ns % 128 != 0) return PTXSTD_EINVAL;
+    const size_t dec = ptxstd_gemm_decode_workspace_bytes(M, ns, K);
+    if (dec == 0 || workspace_bytes < dec) return PTXSTD_EINVAL;
+    pd::Out out = {};
+    for (int r = 0; r < d->nranks; ++r) {
+        out.y[r] = reinterpret_cast<uint16_t*>(d->p2p_peer[r]);
+        out.sig[r] = reinterpret_cast<uint32_t*>(d->p2p_peer[r] + p2p_y_bytes(N));
+    }
+    out.nranks = static_cast<uint32_t>(d->nranks);
+    out.rank = static_cast<uint32_t>(d->rank);
+    out.ldy = static_cast<uint64_t>(N);
+    out.col0 = static_cast<uint64_t>(d->rank) * static_cast<uint64_t>(ns);
+    auto s = static_cast<cudaStream_t>(stream);
+    int st = pd::launch(d_x, d_w_shard, d_sfw_shard, gw, out, M, ns, K,
+                        static_cast<uint8_t*>(d_workspace), s);
+    if (st || !d_y) return st;
+    if (cudaMemcpyAsync(d_y, d->p2p_local, static_cast<size_t>(M) * N * 2,
+                        cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+        return PTXSTD_ECUDA;
+    return PTXSTD_OK;
 }
 
 }  // extern "C"

@@ -33,11 +33,16 @@
 //           drain the accumulator and reduce the 128 x 16 fp32 partial into the scratch with
 //           red.global.add.v4.f32, off the dequant / MMA path (the MMA already fills the other
 //           accumulator). A per-block counter of finished K stages elects the CTA that completes a
-//           block; its epilogue warps convert the block to bf16 and write y (transposed).
+//           block; its epilogue warps convert the block to bf16, transpose it through shared
+//           memory and write y in 16-byte row chunks.
+// Output routing (decode_out.h): one local y, or, for the N-sharded multi-GPU path, the y of every
+// rank over NVLink (the epilogue's stores go to each rank's copy; counters and bounded waits order
+// the steps; kernel 3, decode_done, waits until every rank's pieces have arrived).
 #include <mutex>
 
 #include "common.cuh"
 #include "data_types.cuh"
+#include "decode_out.h"
 #include "tcgen05.cuh"
 #include "tma_host.h"
 
@@ -88,6 +93,7 @@ struct alignas(1024) Smem {
     uint8_t w[WST][kWStageBytes];
     uint8_t x[XST][kXStageBytes];
     uint8_t sf[WST][kSfStageBytes];
+    uint16_t ytile[4][kTok][32];  // per epilogue warp: its 32 block columns x 16 tokens, bf16
     uint64_t wfull[WST];
     uint64_t wempty[WST];
     uint64_t xfull[XST];
@@ -140,8 +146,14 @@ __device__ __forceinline__ uint32_t ximg_offset(uint32_t r, uint32_t k) {
 // Blocks 0..15 handle token rows (rows >= M write zeros); the rest clear the scratch.
 __global__ void __launch_bounds__(kPrepThreads)
     decode_prep_kernel(const uint16_t* __restrict__ x, uint32_t M, uint32_t K, uint8_t* ws,
-                       uint32_t N) {
+                       uint32_t N, const ptxstd::decode::Out out) {
     asm volatile("griddepcontrol.launch_dependents;");
+    if (out.nranks != 0 && blockIdx.x == 0 && threadIdx.x < out.nranks) {
+        // peer-to-peer output: this rank starts a step (see decode_out.h)
+        namespace pd = ptxstd::decode;
+        if (threadIdx.x == 0) out.sig[out.rank][pd::kSigStep] += 1u;
+        atomicAdd_system(out.sig[threadIdx.x] + pd::kSigReady + out.rank, 1u);
+    }
     Workspace w{reinterpret_cast<float*>(ws),
                 reinterpret_cast<uint32_t*>(ws + ws_counters_off(N)), ws + ws_ximg_off(N),
                 reinterpret_cast<float*>(ws + ws_factors_off(N, K))};
@@ -289,6 +301,17 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
                  : "memory");
 }
 
+// Bounded wait until a peer-written counter reaches `target` (wrap-safe), acquire at system scope.
+__device__ __forceinline__ bool wait_counter(const uint32_t* p, uint32_t target) {
+    const uint64_t t0 = ptxstd::global_timer();
+    while (true) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if (static_cast<int32_t>(v - target) >= 0) return true;
+        if (ptxstd::global_timer() - t0 > ptxstd::kWaitLimitNs) return false;
+    }
+}
+
 // Unit u of U = nblocks * S is (block u / S, stage u % S); CTA c owns [c U / G, (c+1) U / G).
 __device__ __forceinline__ void unit_range(uint64_t U, uint32_t& u0, uint32_t& u1) {
     u0 = static_cast<uint32_t>(U * blockIdx.x / gridDim.x);
@@ -297,8 +320,8 @@ __device__ __forceinline__ void unit_range(uint64_t U, uint32_t& u0, uint32_t& u
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmW, const uint8_t* __restrict__ sfW,
-                       uint8_t* ws, uint16_t* __restrict__ y, uint32_t M, uint32_t N, uint32_t K,
-                       float gw, uint32_t* err) {
+                       uint8_t* ws, const __grid_constant__ ptxstd::decode::Out out, uint32_t M,
+                       uint32_t N, uint32_t K, float gw, uint32_t* err) {
     extern __shared__ uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~static_cast<uintptr_t>(1023));
@@ -534,7 +557,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         float fac[kTok];
 #pragma unroll
         for (uint32_t t = 0; t < kTok; ++t) fac[t] = __ldcg(wsp.factors + t) * gw;
+        namespace pd = ptxstd::decode;
+        if (out.nranks != 0) {
+            // Peer-to-peer output: every rank's stream has passed its readers of the previous
+            // step before any of this step's stores reach its y. Waited here, long before the
+            // first accumulator is ready, so the wait hides behind the pipeline.
+            const uint32_t step = __ldcg(out.sig[out.rank] + pd::kSigStep);
+            bool okr = lane >= out.nranks ||
+                       wait_counter(out.sig[out.rank] + pd::kSigReady + lane, step);
+            okr = __all_sync(0xffffffffu, okr);
+            if (!okr) {
+                if (lane == 0) fail(s, err, kDetailEpi | 0x40);
+                u1 = u0;  // no stores, no completion signal
+            }
+        }
         uint32_t dbuf = 0, dphase = 0, sphase = 0;
+        const uint32_t e = warp - kEpiWarp;
         for (uint32_t u = u0; u < u1;) {
             // one W-block segment: units u .. end - 1 of block nb
             const uint32_t nb = u / S;
@@ -566,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                            __uint_as_float(acc[t + 1]) * fac[t + 1],
                            __uint_as_float(acc[t + 2]) * fac[t + 2],
                            __uint_as_float(acc[t + 3]) * fac[t + 3]);
-            __threadfence();
+            ptxstd::fence_acq_rel_gpu();
             __syncwarp();
             // All four warps have reduced (segA), then the first publishes the finished stages
             // and tells the others whether this CTA completes the block (segB). mbarriers rather
@@ -594,22 +632,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             sphase ^= 1u;
             if (*reinterpret_cast<volatile uint32_t*>(&s.finalize)) {
-                __threadfence();
-                // column `col` of the block: its 16 token sums -> y[t][nb * BM + col]
+                ptxstd::fence_acq_rel_gpu();
+                // column `col` of the block: its 16 token sums, as bf16, into this warp's tile
                 const float4* src = reinterpret_cast<const float4*>(
                     wsp.y32 + (static_cast<size_t>(nb) * BM + col) * kTok);
-                uint16_t* yc = y + static_cast<size_t>(nb) * BM + col;
 #pragma unroll
                 for (uint32_t i = 0; i < kTok / 4; ++i) {
                     const float4 f = __ldcg(src + i);
                     const uint32_t p0 = dt::bf16x2_from_f32(f.x, f.y);
                     const uint32_t p1 = dt::bf16x2_from_f32(f.z, f.w);
-                    const uint16_t o[4] = {static_cast<uint16_t>(p0), static_cast<uint16_t>(p0 >> 16),
-                                           static_cast<uint16_t>(p1), static_cast<uint16_t>(p1 >> 16)};
-#pragma unroll
-                    for (uint32_t k = 0; k < 4; ++k)
-                        if (4 * i + k < M) yc[static_cast<size_t>(4 * i + k) * N] = o[k];
+                    s.ytile[e][4 * i + 0][lane] = static_cast<uint16_t>(p0);
+                    s.ytile[e][4 * i + 1][lane] = static_cast<uint16_t>(p0 >> 16);
+                    s.ytile[e][4 * i + 2][lane] = static_cast<uint16_t>(p1);
+                    s.ytile[e][4 * i + 3][lane] = static_cast<uint16_t>(p1 >> 16);
                 }
+                __syncwarp();
+                // 16 tokens x 32 columns = 64 chunks of 8 columns; lane takes chunks lane and
+                // lane + 32 (token ch / 4, columns 8 (ch % 4) ..) -> 16-byte stores into y[t][..]
+                // of every output (this GPU's only, or every rank's over NVLink)
+                const size_t c0 = out.col0 + static_cast<size_t>(nb) * BM + 32 * e;
+                const uint32_t nout = out.nranks != 0 ? out.nranks : 1u;
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {
+                    const uint32_t ch = lane + 32 * h, t = ch >> 2, g = ch & 3u;
+                    if (t >= M) continue;
+                    const uint4 v = *reinterpret_cast<const uint4*>(&s.ytile[e][t][8 * g]);
+                    const size_t off = static_cast<size_t>(t) * out.ldy + c0 + 8 * g;
+                    for (uint32_t r = 0; r < nout; ++r)
+                        *reinterpret_cast<uint4*>(out.y[r] + off) = v;
+                }
+                __syncwarp();
             }
         }
     }
@@ -620,8 +672,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) t5::tmem_dealloc(tmem, kTmemCols);
 }
 
-int launch_decode(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float gw, uint16_t* y,
-                  int64_t M, int64_t N, int64_t K, uint8_t* ws, cudaStream_t stream) {
+// Kernel 3, peer-to-peer output only. It starts after kernel 2 has completed on this GPU, so
+// every store kernel 2 made (into every rank's y) happens before it. Thread r releases them to
+// rank r (one system-scope fence, then DONE[this rank] += 1 on rank r), then waits until rank r has
+// done the same here for this step. Signalling from a fresh kernel keeps the fence off kernel 2's
+// epilogue, where it would wait for the NVLink stores still in flight (measured at about 8 us per
+// step on 2 GPUs). A device with an error recorded (a timed-out wait of this step, or any earlier
+// failure not yet read) withholds its signal, so that every rank's wait fails too instead of
+// reading an incomplete y.
+__global__ void __launch_bounds__(32) decode_done_kernel(const ptxstd::decode::Out out,
+                                                         uint32_t* err) {
+    namespace pd = ptxstd::decode;
+    const uint32_t r = threadIdx.x;
+    if (r >= out.nranks) return;
+    if (*reinterpret_cast<volatile uint32_t*>(err) == 0u) {
+        ptxstd::fence_acq_rel_sys();
+        atomicAdd_system(out.sig[r] + pd::kSigDone + out.rank, 1u);
+    }
+    const uint32_t step = __ldcg(out.sig[out.rank] + pd::kSigStep);
+    if (!wait_counter(out.sig[out.rank] + pd::kSigDone + r, step))
+        ptxstd::record_error(err, PTXSTD_ETIMEOUT, kDetailEpi | 0x50 | r);
+}
+
+int launch_decode(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float gw,
+                  const ptxstd::decode::Out& out, int64_t M, int64_t N, int64_t K, uint8_t* ws,
+                  cudaStream_t stream) {
     CUtensorMap tw;
     int st = ptxstd::make_tmap_2d(&tw, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, N, K / 2,
                                   BKS / 2, BM, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -634,7 +709,7 @@ int launch_decode(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float
     const int sms = ptxstd::sm_count();
     decode_prep_kernel<<<sms, kPrepThreads, 0, stream>>>(x, static_cast<uint32_t>(M),
                                                          static_cast<uint32_t>(K), ws,
-                                                         static_cast<uint32_t>(N));
+                                                         static_cast<uint32_t>(N), out);
     st = ptxstd::launch_status();
     if (st) return st;
     const uint64_t units = static_cast<uint64_t>(N / BM) * static_cast<uint64_t>(K / BKS);
@@ -649,14 +724,50 @@ int launch_decode(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, gemm_decode_kernel, tw, sfW, ws, y, static_cast<uint32_t>(M),
+    if (cudaLaunchKernelEx(&cfg, gemm_decode_kernel, tw, sfW, ws, out, static_cast<uint32_t>(M),
                            static_cast<uint32_t>(N), static_cast<uint32_t>(K), gw,
                            err) != cudaSuccess)
         return PTXSTD_ECUDA;
+    st = ptxstd::launch_status();
+    if (st || out.nranks == 0) return st;
+    decode_done_kernel<<<1, 32, 0, stream>>>(out, err);
     return ptxstd::launch_status();
 }
 
+// Shape, pointer and alignment checks shared by every decode entry point.
+int check_args(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float gw, int64_t M,
+               int64_t N, int64_t K, const void* ws) {
+    if (M <= 0 || M > static_cast<int64_t>(kTok) || N <= 0 || K <= 0 || N % BM || K % BKS)
+        return PTXSTD_EINVAL;
+    if (N >= (1ll << 31) || K >= (1ll << 30)) return PTXSTD_EINVAL;
+    if (!(gw == gw) || !x || !W || !sfW || !ws) return PTXSTD_EINVAL;
+    if (!ptxstd::aligned16(x) || !ptxstd::aligned16(W) || !ptxstd::aligned16(sfW) ||
+        (reinterpret_cast<uintptr_t>(ws) & 1023u))
+        return PTXSTD_EINVAL;
+    return PTXSTD_OK;
+}
+
+ptxstd::decode::Out local_out(uint16_t* y, int64_t N) {
+    ptxstd::decode::Out o = {};
+    o.y[0] = y;
+    o.ldy = static_cast<uint64_t>(N);
+    return o;
+}
+
 }  // namespace
+
+int ptxstd::decode::launch(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float gw,
+                           const Out& out, int64_t M, int64_t N, int64_t K, uint8_t* ws,
+                           cudaStream_t stream) {
+    if (check_args(x, W, sfW, gw, M, N, K, ws) || out.nranks > kMaxRanks ||
+        (out.nranks != 0 && out.rank >= out.nranks) || out.ldy < out.col0 + N ||
+        out.ldy % 8 != 0 || out.col0 % 8 != 0)  // 16-byte output chunks
+        return PTXSTD_EINVAL;
+    for (uint32_t r = 0; r < (out.nranks != 0 ? out.nranks : 1u); ++r)
+        if (!out.y[r] || !ptxstd::aligned16(out.y[r]) || (out.nranks != 0 && !out.sig[r]))
+            return PTXSTD_EINVAL;
+    return launch_decode(x, W, sfW, gw, out, M, N, K, ws, stream);
+}
 
 extern "C" {
 
@@ -668,16 +779,12 @@ size_t ptxstd_gemm_decode_workspace_bytes(int64_t M, int64_t N, int64_t K) {
 int ptxstd_gemm_decode(const uint16_t* d_x, const uint8_t* d_w, const uint8_t* d_sfw, float gw,
                        uint16_t* d_y, int64_t M, int64_t N, int64_t K, void* d_workspace,
                        size_t workspace_bytes, ptxstd_stream stream) {
-    if (M <= 0 || M > static_cast<int64_t>(kTok) || N <= 0 || K <= 0 || N % BM || K % BKS)
-        return PTXSTD_EINVAL;
-    if (N >= (1ll << 31) || K >= (1ll << 30)) return PTXSTD_EINVAL;
-    if (!(gw == gw) || !d_x || !d_w || !d_sfw || !d_y || !d_workspace) return PTXSTD_EINVAL;
-    if (!ptxstd::aligned16(d_x) || !ptxstd::aligned16(d_w) || !ptxstd::aligned16(d_sfw) ||
-        !ptxstd::aligned16(d_y) || (reinterpret_cast<uintptr_t>(d_workspace) & 1023u))
+    if (check_args(d_x, d_w, d_sfw, gw, M, N, K, d_workspace) || !d_y || !ptxstd::aligned16(d_y))
         return PTXSTD_EINVAL;
     if (workspace_bytes < ws_bytes(static_cast<size_t>(N), static_cast<size_t>(K)))
         return PTXSTD_EINVAL;
-    return launch_decode(d_x, d_w, d_sfw, gw, d_y, M, N, K, static_cast<uint8_t*>(d_workspace),
+    return launch_decode(d_x, d_w, d_sfw, gw, local_out(d_y, N), M, N, K,
+                         static_cast<uint8_t*>(d_workspace),
                          static_cast<cudaStream_t>(stream));
 }
 
@@ -739,6 +846,7 @@ extern "C" int ptxstd_gemm_decode_noalloc(const uint16_t* d_x, const uint8_t* d_
     void* scratch = nullptr;
     const int st = decode_scratch_address(&scratch);
     if (st) return st;
-    return launch_decode(d_x, d_w, d_sfw, gw, d_y, M, N, K, static_cast<uint8_t*>(scratch),
+    return launch_decode(d_x, d_w, d_sfw, gw, local_out(d_y, N), M, N, K,
+                         static_cast<uint8_t*>(scratch),
                          static_cast<cudaStream_t>(stream));
 }
