@@ -718,6 +718,10 @@ def run_ours(args, wl) -> dict | None:
             for i in range(args.steps):
                 launches += wl.step(i)
         torch.cuda.synchronize()
+        # One untimed replay (K more warm-up steps): the first launch of a captured graph also
+        # uploads it to the device, a one-time cost that is not part of a step.
+        graph.replay()
+        torch.cuda.synchronize()
 
     # device-timed region: K steps, inputs resident in HBM
     sampler = ClockSampler(torch.cuda.current_device()) if dist.rank == 0 else None
@@ -794,7 +798,8 @@ def run_ours(args, wl) -> dict | None:
         "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"), "vs_baseline": None,
         "dtype": wl.dtype, "data": "synthetic (seeded)",
         "config": dict(wl.config, parallelism=getattr(wl, "parallelism", "replicas") + str(world),
-                       launch="cuda-graph replay of the K steps" if use_graph else "eager"),
+                       launch=("cuda-graph replay of the K steps, after one untimed replay that "
+                               "uploads the graph") if use_graph else "eager"),
         "roofline": roofline,
         "e2e": {"value": round(wl.value(e2e_max / 1e3 / args.steps) * world, 2),
                 "unit": wl.unit, "h2d_bytes_per_step": wl.in_bytes,

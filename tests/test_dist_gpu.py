@@ -61,7 +61,7 @@ def _worker(rank, world, port, out_dir):
     td.init_process_group("gloo", rank=rank, world_size=world)
     dist = Dist.from_torch()
     msgs = []
-    M, N, K = 16, 1024, 2048
+    M, N, K = 16, 512 * world, 2048  # 512 columns per rank
     x = workloads.normal_bf16(M, K, seed=21)
     wb = workloads.normal_bf16(N, K, std=0.02, seed=22)
     gw = float(np.abs((wb.astype(np.uint32) << 16).view(np.float32)).max() / (448.0 * 6.0))
