@@ -196,6 +196,23 @@ class Dist:
 
 # ---- workloads --------------------------------------------------------------------------------
 
+def _pinned_like(torch, t):
+    """A pinned host buffer of t's shape and dtype."""
+    return torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+
+
+def _gemm_slots(torch, inputs, c):
+    """Two end-to-end buffer slots of a GEMM: slot 0 reuses the device operands and output of the
+    device-timed steps, slot 1 has its own; each slot has its own pinned host output."""
+    slots = []
+    for k in range(2):
+        devs = [d if k == 0 else torch.empty_like(d) for d, _ in inputs]
+        ck = c if k == 0 else torch.empty_like(c)
+        slots.append({"in": [(d, h) for d, (_, h) in zip(devs, inputs)],
+                      "out": [(_pinned_like(torch, ck), ck)], "args": (*devs, ck)})
+    return slots
+
+
 class MxFp8Quantize:
     """bf16 [8192, 8192] -> E4M3 [8192, 8192] + UE8M0 [8192, 256] (row-major scales)."""
 
@@ -229,9 +246,6 @@ class MxFp8Quantize:
             q = torch.empty((self.rows, self.cols), dtype=torch.uint8, device="cuda")
             sf = torch.empty((self.rows, self.cols // 32), dtype=torch.uint8, device="cuda")
             self.sets.append((x, q, sf))
-        self.q_host = torch.empty((self.rows, self.cols), dtype=torch.uint8, pin_memory=True)
-        self.sf_host = torch.empty((self.rows, self.cols // 32), dtype=torch.uint8,
-                                   pin_memory=True)
 
     def step(self, i):
         import ptxstd
@@ -239,14 +253,16 @@ class MxFp8Quantize:
         ptxstd.quantize_mxfp8(x, out=(q, sf))
         return 1  # kernel launches
 
-    def e2e_step(self, i):
+    def e2e_slots(self, torch):
         """Public API from host buffers: H2D input, quantise, D2H payload + scales."""
+        return [{"in": [(x, self.x_host)], "out": [(_pinned_like(torch, q), q),
+                                                   (_pinned_like(torch, sf), sf)],
+                 "args": (x, q, sf)} for x, q, sf in self.sets]
+
+    def e2e_compute(self, i, args):
         import ptxstd
-        x, q, sf = self.sets[i % 2]
-        x.copy_(self.x_host, non_blocking=True)
+        x, q, sf = args
         ptxstd.quantize_mxfp8(x, out=(q, sf))
-        self.q_host.copy_(q, non_blocking=True)
-        self.sf_host.copy_(sf, non_blocking=True)
         return 1
 
     def value(self, seconds_per_step: float) -> float:
@@ -302,19 +318,19 @@ class Fp8Gemm:
         self.a = self.a_host.cuda()
         self.b = self.b_host.cuda()
         self.c = torch.empty((self.M, self.N), dtype=torch.bfloat16, device="cuda")
-        self.c_host = torch.empty((self.M, self.N), dtype=torch.bfloat16, pin_memory=True)
 
     def step(self, i):
         import ptxstd
         ptxstd.gemm_fp8(self.a, self.b, 0.75, 1.25, out=self.c)
         return 1
 
-    def e2e_step(self, i):
+    def e2e_slots(self, torch):
+        return _gemm_slots(torch, [(self.a, self.a_host), (self.b, self.b_host)], self.c)
+
+    def e2e_compute(self, i, args):
         import ptxstd
-        self.a.copy_(self.a_host, non_blocking=True)
-        self.b.copy_(self.b_host, non_blocking=True)
-        ptxstd.gemm_fp8(self.a, self.b, 0.75, 1.25, out=self.c)
-        self.c_host.copy_(self.c, non_blocking=True)
+        a, b, c = args
+        ptxstd.gemm_fp8(a, b, 0.75, 1.25, out=c)
         return 1
 
     def value(self, seconds_per_step: float) -> float:
@@ -378,13 +394,14 @@ class Mxfp8Gemm(Fp8Gemm):
         ptxstd.gemm_mxfp8(self.a, self.sfa, self.b, self.sfb, out=self.c)
         return 1
 
-    def e2e_step(self, i):
+    def e2e_slots(self, torch):
+        return _gemm_slots(torch, [(self.a, self.a_host), (self.sfa, self.sfa_host),
+                                   (self.b, self.b_host), (self.sfb, self.sfb_host)], self.c)
+
+    def e2e_compute(self, i, args):
         import ptxstd
-        for dst, src in ((self.a, self.a_host), (self.b, self.b_host), (self.sfa, self.sfa_host),
-                         (self.sfb, self.sfb_host)):
-            dst.copy_(src, non_blocking=True)
-        ptxstd.gemm_mxfp8(self.a, self.sfa, self.b, self.sfb, out=self.c)
-        self.c_host.copy_(self.c, non_blocking=True)
+        a, sfa, b, sfb, c = args
+        ptxstd.gemm_mxfp8(a, sfa, b, sfb, out=c)
         return 1
 
 
@@ -436,14 +453,15 @@ class Mxfp8SparseGemm(Fp8Gemm):
         ptxstd.gemm_mxfp8_sparse(self.vals, self.meta, self.sfa, self.b, self.sfb, out=self.c)
         return 1
 
-    def e2e_step(self, i):
+    def e2e_slots(self, torch):
+        return _gemm_slots(torch, [(self.vals, self.vals_host), (self.meta, self.meta_host),
+                                   (self.sfa, self.sfa_host), (self.b, self.b_host),
+                                   (self.sfb, self.sfb_host)], self.c)
+
+    def e2e_compute(self, i, args):
         import ptxstd
-        for dst, src in ((self.vals, self.vals_host), (self.meta, self.meta_host),
-                         (self.b, self.b_host), (self.sfa, self.sfa_host),
-                         (self.sfb, self.sfb_host)):
-            dst.copy_(src, non_blocking=True)
-        ptxstd.gemm_mxfp8_sparse(self.vals, self.meta, self.sfa, self.b, self.sfb, out=self.c)
-        self.c_host.copy_(self.c, non_blocking=True)
+        vals, meta, sfa, b, sfb, c = args
+        ptxstd.gemm_mxfp8_sparse(vals, meta, sfa, b, sfb, out=c)
         return 1
 
     def cpu_sample(self, threads: int, budget_s: float):
@@ -497,19 +515,20 @@ class Nvfp4Gemm:
         del xa, xb
         self.c = torch.empty((self.M, self.n_local), dtype=torch.bfloat16, device="cuda")
         self.host = [t.cpu().pin_memory() for t in (self.a, self.sfa, self.b, self.sfb)]
-        self.c_host = torch.empty((self.M, self.n_local), dtype=torch.bfloat16, pin_memory=True)
 
     def step(self, i):
         import ptxstd
         ptxstd.gemm_nvfp4(self.a, self.sfa, self.ga, self.b, self.sfb, self.gb, out=self.c)
         return 1
 
-    def e2e_step(self, i):
+    def e2e_slots(self, torch):
+        return _gemm_slots(torch, list(zip((self.a, self.sfa, self.b, self.sfb), self.host)),
+                           self.c)
+
+    def e2e_compute(self, i, args):
         import ptxstd
-        for d, h in zip((self.a, self.sfa, self.b, self.sfb), self.host):
-            d.copy_(h, non_blocking=True)
-        ptxstd.gemm_nvfp4(self.a, self.sfa, self.ga, self.b, self.sfb, self.gb, out=self.c)
-        self.c_host.copy_(self.c, non_blocking=True)
+        a, sfa, b, sfb, c = args
+        ptxstd.gemm_nvfp4(a, sfa, self.ga, b, sfb, self.gb, out=c)
         return 1
 
     def value(self, seconds_per_step: float) -> float:
@@ -583,7 +602,6 @@ class DecodeGemm:
         self.x_host = self.x.cpu().pin_memory()
         # every rank ends the step with the full [16, N] output
         self.y = torch.empty((self.M, self.N), dtype=torch.bfloat16, device="cuda")
-        self.y_host = torch.empty((self.M, self.N), dtype=torch.bfloat16, pin_memory=True)
         self.dist = None
         if self.world > 1:
             from ptxstd.dist import Dist
@@ -617,11 +635,29 @@ class DecodeGemm:
             self.dist.close()
             self.dist = None
 
-    def e2e_step(self, i):
-        self.x.copy_(self.x_host, non_blocking=True)
-        n = self._decode(i)
-        self.y_host.copy_(self.y, non_blocking=True)
-        return n
+    def e2e_slots(self, torch):
+        # the fused multi-GPU decode writes a library-owned y that the next step overwrites, so
+        # each step also copies it into its slot's buffer, which the D2H copy then reads
+        slots = []
+        for k in range(2):
+            x = self.x if k == 0 else torch.empty_like(self.x)
+            y = torch.empty((self.M, self.N), dtype=torch.bfloat16, device="cuda")
+            slots.append({"in": [(x, self.x_host)], "out": [(_pinned_like(torch, y), y)],
+                          "args": (x, y)})
+        return slots
+
+    def e2e_compute(self, i, args):
+        import ptxstd
+        x, y = args
+        w, sfw, gw = self.sets[i % 2]
+        if self.dist is None:
+            ptxstd.gemm_decode(x, w, sfw, gw, out=y)
+            return 2
+        if self.gather == "p2p":
+            self.dist.gemm_decode_p2p(x, w, sfw, gw, self.N, out=y)
+            return 3
+        self.dist.gemm_decode(x, w, sfw, gw, self.N, out=y)
+        return 3
 
     def value(self, seconds_per_step: float) -> float:
         return self.bytes / seconds_per_step / 1e9
@@ -663,13 +699,10 @@ class MxFp8QuantizeSR(MxFp8Quantize):
         ptxstd.quantize_mxfp8(x, out=(q, sf), seed=0x5EED + i)
         return 1
 
-    def e2e_step(self, i):
+    def e2e_compute(self, i, args):
         import ptxstd
-        x, q, sf = self.sets[i % 2]
-        x.copy_(self.x_host, non_blocking=True)
+        x, q, sf = args
         ptxstd.quantize_mxfp8(x, out=(q, sf), seed=0x5EED + i)
-        self.q_host.copy_(q, non_blocking=True)
-        self.sf_host.copy_(sf, non_blocking=True)
         return 1
 
     def cpu_sample(self, threads: int, budget_s: float):
@@ -745,19 +778,49 @@ def run_ours(args, wl) -> dict | None:
     if graph is not None:
         del graph
 
-    # end-to-end through the public API with host buffers
-    for i in range(2):
-        wl.e2e_step(i)
-    torch.cuda.synchronize()
+    # End to end through the public API with host buffers: every step copies its inputs from
+    # pinned host memory and its results back. Two buffer slots are used in turn, with the copies
+    # on their own streams, so that step i+1's H2D and step i's D2H overlap step i's compute
+    # (PCIe carries both directions at once); events keep a slot's buffers from being reused
+    # before its previous step has finished with them.
+    slots = wl.e2e_slots(torch)
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def run_e2e(n):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev_in = [torch.cuda.Event() for _ in range(n)]
+        ev_run = [torch.cuda.Event() for _ in range(n)]
+        ev_out = [torch.cuda.Event() for _ in range(n)]
+        start.record(stream)
+        h2d.wait_event(start)
+        d2h.wait_event(start)
+        for i in range(n):
+            slot = slots[i % 2]
+            with torch.cuda.stream(h2d):
+                if i >= 2:
+                    h2d.wait_event(ev_run[i - 2])  # inputs of step i-2 consumed
+                for dev, host in slot["in"]:
+                    dev.copy_(host, non_blocking=True)
+                ev_in[i].record(h2d)
+            stream.wait_event(ev_in[i])
+            if i >= 2:
+                stream.wait_event(ev_out[i - 2])  # outputs of step i-2 read back
+            wl.e2e_compute(i, slot["args"])
+            ev_run[i].record(stream)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(ev_run[i])
+                for host, dev in slot["out"]:
+                    host.copy_(dev, non_blocking=True)
+                ev_out[i].record(d2h)
+        stream.wait_event(ev_out[n - 1])
+        end.record(stream)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end)
+
+    run_e2e(3)
     dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        wl.e2e_step(i)
-    e1.record(stream)
-    torch.cuda.synchronize()
+    e2e_ms = run_e2e(args.steps)
     dist.barrier()
-    e2e_ms = e0.elapsed_time(e1)
 
     ms_max = dist.max(ms)
     e2e_max = dist.max(e2e_ms)
