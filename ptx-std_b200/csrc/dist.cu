@@ -208,7 +208,8 @@ size_t p2p_y_bytes(int64_t N) {
 
 int ptxstd_dist_decode_p2p_init(ptxstd_dist* d, int64_t N, uint16_t** d_y) {
     namespace pd = ptxstd::decode;
-    if (!d || !d_y || N <= 0 || N % d->nranks != 0 || d->nranks > static_cast<int>(pd::kMaxRanks))
+    if (!d || !d_y || N <= 0 || N % (128 * static_cast<int64_t>(d->nranks)) != 0 ||
+        d->nranks > static_cast<int>(pd::kMaxRanks))
         return PTXSTD_EINVAL;
     if (d->p2p_local) return PTXSTD_EINVAL;  // once per communicator
     Nccl& n = nccl();

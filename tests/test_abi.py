@@ -63,3 +63,25 @@ def test_host_validation_without_gpu(ptxstd_lib):
     assert L.ptxstd_quantize_mxfp8_rs(16, 128, 96 + 1, 16, 16, 0, 1, None) == EINVAL
     assert L.ptxstd_quantize_nvfp4_rs(16, 128, 64, 0.0, 16, 16, 0, 1, None) == EINVAL
     assert L.ptxstd_cvt_sweep(0, (1 << 32) - 8, 16, 16, None) == EINVAL
+
+
+def test_dist_validation_without_gpu(ptxstd_lib):
+    """The multi-GPU entry points reject a missing communicator or bad arguments before any CUDA
+    or NCCL call."""
+    from ptxstd import dist as D
+    L = D._lib()
+    EINVAL = ptxstd_lib.EINVAL
+    out = C.c_void_p()
+    assert L.ptxstd_dist_unique_id(None) == EINVAL
+    assert L.ptxstd_dist_init(None, 2, 0, C.byref(out)) == EINVAL
+    assert L.ptxstd_dist_init((C.c_uint8 * 128)(), 2, 2, C.byref(out)) == EINVAL  # rank >= nranks
+    assert L.ptxstd_dist_free(None) == ptxstd_lib.OK
+    assert L.ptxstd_gemm_nvfp4_sharded(None, 16, 16, 1.0, 16, 16, 1.0, 16, 256, 512, 256,
+                                       None) == EINVAL
+    assert L.ptxstd_gemm_decode_sharded_workspace_bytes(None, 16, 1024, 2048) == 0
+    assert L.ptxstd_gemm_decode_sharded(None, 16, 16, 16, 1.0, 16, 16, 1024, 2048, 1024,
+                                        1 << 20, None) == EINVAL
+    y = C.c_void_p()
+    assert L.ptxstd_dist_decode_p2p_init(None, 1024, C.byref(y)) == EINVAL
+    assert L.ptxstd_gemm_decode_sharded_p2p(None, 16, 16, 16, 1.0, None, 16, 1024, 2048, 1024,
+                                            1 << 20, None) == EINVAL
