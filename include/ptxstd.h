@@ -241,6 +241,34 @@ PTXSTD_API int ptxstd_gemm_nvfp4(const uint8_t* d_a, const uint8_t* d_sfa, float
 PTXSTD_API int ptxstd_gemm_mxfp8(const uint8_t* d_a, const uint8_t* d_sfa, const uint8_t* d_b,
                                  const uint8_t* d_sfb, uint16_t* d_c, int64_t M, int64_t N,
                                  int64_t K, ptxstd_stream stream);
+/* MX element types of kind::f8f6f4 / mxf8f6f4, with the values of the reference's
+ * F8f6f4ElementType (src/tcgen05/descriptor.rs:316-327). */
+enum ptxstd_mx_type {
+    PTXSTD_MX_E4M3 = 0,
+    PTXSTD_MX_E5M2 = 1,
+    PTXSTD_MX_E2M3 = 3,
+    PTXSTD_MX_E3M2 = 4,
+    PTXSTD_MX_E2M1 = 5,
+};
+/* OCP MX quantisation of bf16 [rows, cols] (cols % 32 == 0) to any MX element type: one UE8M0
+ * scale per 32 contiguous elements (floor-pow2 of the block amax, f8e8m0::from_f32::<TowardZero,
+ * SaturateFinite>, minus the format's emax: E4M3 8, E5M2 15, E2M3 2, E3M2 4, E2M1 2, clamped at 0),
+ * elements x * 2^-(scale-127) RN .satfinite (narrow.rs:125-130). q [rows, cols] bytes in the
+ * tensor cores' operand layout for K = 32 MMAs (descriptor.rs:306-315): FP8 one code per byte;
+ * FP6 16 six-bit codes packed little-endian in 12 bytes + 4 zero bytes per 16 elements; FP4 16
+ * nibbles in 8 bytes + 8 zero bytes. sf_layout as ptxstd_quantize_mxfp8_layout. For E4M3 the
+ * result equals ptxstd_quantize_mxfp8_layout's. */
+PTXSTD_API int ptxstd_quantize_mx(const uint16_t* d_x, int64_t rows, int64_t cols, int elem_type,
+                                  uint8_t* d_q, uint8_t* d_sf, int sf_layout,
+                                  ptxstd_stream stream);
+/* MX GEMM with any pair of element types (mma_block_scaled with MmaKind::Mxf8f6f4,
+ * InstrDescriptor::<Mxf8f6f4>::new(a_type, b_type, 256, 256), src/tcgen05/descriptor.rs:601-611):
+ * C[M,N] bf16 = sum_k (A[m,k] 2^(sfA-127)) (B[n,k] 2^(sfB-127)); A [M,K] and B [N,K] in the
+ * operand layout of ptxstd_quantize_mx, scales blocked (sf_layout 1). ptxstd_gemm_mxfp8 is
+ * a_type = b_type = PTXSTD_MX_E4M3. M % 256 == 0, N % 256 == 0, K % 128 == 0. */
+PTXSTD_API int ptxstd_gemm_mx(const uint8_t* d_a, int a_type, const uint8_t* d_sfa,
+                              const uint8_t* d_b, int b_type, const uint8_t* d_sfb, uint16_t* d_c,
+                              int64_t M, int64_t N, int64_t K, ptxstd_stream stream);
 /* 2:4 structured sparsity (the A operand of tcgen05.mma.sp, src/tcgen05/mma.rs:725-777): in each
  * group of four consecutive elements of a row of E4M3 codes [rows, cols], the two of largest
  * magnitude (code & 0x7F, ties to the lower index) are kept, in index order, in vals

@@ -969,6 +969,141 @@ void ptxo_gemm_mxfp8_ref(const uint8_t* A, const uint8_t* sfA, const uint8_t* B,
     parallel_for((uint64_t)n_samples, threads, mxfp8_samples, &c);
 }
 
+/* ---- MX formats in the tcgen05 operand layout --------------------------------------------- */
+/* Packing of 4- and 6-bit elements for kind::f8f6f4 / mxf8f6f4 operands in shared memory
+ * (documented beside F8f6f4ElementType, src/tcgen05/descriptor.rs:306-315): groups of 16 elements
+ * padded to 16 bytes. */
+void ptxo_mx_pack(int format, const uint8_t* codes, uint8_t* packed, size_t n) {
+    for (size_t g = 0; g < n / 16; ++g) {
+        const uint8_t* c = codes + 16 * g;
+        uint8_t* o = packed + 16 * g;
+        memset(o, 0, 16);
+        if (format == PTXO_E4M3 || format == PTXO_E5M2) {
+            memcpy(o, c, 16);
+        } else if (format == PTXO_E2M3 || format == PTXO_E3M2) {
+            for (int i = 0; i < 16; ++i) {
+                const uint32_t v = c[i] & 0x3Fu, bit = 6u * (uint32_t)i;
+                o[bit / 8] |= (uint8_t)(v << (bit % 8));
+                if (bit % 8 > 2) o[bit / 8 + 1] |= (uint8_t)(v >> (8 - bit % 8));
+            }
+        } else {
+            for (int j = 0; j < 8; ++j)
+                o[j] = (uint8_t)((c[2 * j] & 0xF) | ((c[2 * j + 1] & 0xF) << 4));
+        }
+    }
+}
+
+void ptxo_mx_unpack(int format, const uint8_t* packed, uint8_t* codes, size_t n) {
+    for (size_t g = 0; g < n / 16; ++g) {
+        const uint8_t* p = packed + 16 * g;
+        uint8_t* c = codes + 16 * g;
+        if (format == PTXO_E4M3 || format == PTXO_E5M2) {
+            memcpy(c, p, 16);
+        } else if (format == PTXO_E2M3 || format == PTXO_E3M2) {
+            for (int i = 0; i < 16; ++i) {
+                const uint32_t bit = 6u * (uint32_t)i;
+                uint32_t v = (uint32_t)p[bit / 8] >> (bit % 8);
+                if (bit % 8 > 2) v |= (uint32_t)p[bit / 8 + 1] << (8 - bit % 8);
+                c[i] = (uint8_t)(v & 0x3Fu);
+            }
+        } else {
+            for (int j = 0; j < 8; ++j) {
+                c[2 * j] = p[j] & 0xF;
+                c[2 * j + 1] = p[j] >> 4;
+            }
+        }
+    }
+}
+
+static int mx_emax(int format) {
+    switch (format) {
+    case PTXO_E4M3: return 8;
+    case PTXO_E5M2: return 15;
+    case PTXO_E3M2: return 4;
+    default: return 2;  /* E2M3, E2M1 */
+    }
+}
+
+static float mx_decode(int format, uint8_t code) {
+    switch (format) {
+    case PTXO_E4M3: return ptxo_e4m3_to_f32(code);
+    case PTXO_E5M2: return ptxo_e5m2_to_f32(code);
+    case PTXO_E2M3: return ptxo_e2m3_to_f32(code);
+    case PTXO_E3M2: return ptxo_e3m2_to_f32(code);
+    default: return ptxo_e2m1_to_f32(code);
+    }
+}
+
+typedef struct { const uint16_t* x; int64_t cols; int format; uint8_t *q, *sf; } mx_ctx;
+
+static void mx_rows(void* p, uint64_t lo, uint64_t hi) {
+    mx_ctx* c = (mx_ctx*)p;
+    float buf[32];
+    uint8_t codes[32];
+    const int emax = mx_emax(c->format);
+    for (uint64_t r = lo; r < hi; ++r) {
+        const uint16_t* xr = c->x + r * c->cols;
+        for (int64_t b = 0; b < c->cols / 32; ++b) {
+            for (int i = 0; i < 32; ++i) buf[i] = ptxo_bf16_to_f32(xr[b * 32 + i]);
+            const uint8_t u = ptxo_f32_to_ue8m0(block_amax(buf, 32), 0, 1);
+            const uint8_t code = (u == 0xFF) ? 0xFF : (u > emax ? (uint8_t)(u - emax) : 0);
+            const float inv = ue8m0_inverse(code);
+            for (int i = 0; i < 32; ++i) codes[i] = ptxo_f32_to_narrow(c->format, buf[i] * inv, 0);
+            c->sf[r * (c->cols / 32) + b] = code;
+            ptxo_mx_pack(c->format, codes, c->q + r * c->cols + b * 32, 32);
+        }
+    }
+}
+
+void ptxo_quantize_mx(const uint16_t* x, int64_t rows, int64_t cols, int format, uint8_t* q,
+                      uint8_t* sf, int threads) {
+    mx_ctx c = {x, cols, format, q, sf};
+    parallel_for((uint64_t)rows, threads, mx_rows, &c);
+}
+
+typedef struct {
+    const uint8_t *A, *B, *sfA, *sfB;
+    int fa, fb;
+    int64_t K;
+    const int64_t *rows, *cols;
+    double *ref, *mag;
+} mx_gemm_ctx;
+
+static void mx_samples(void* p, uint64_t lo, uint64_t hi) {
+    mx_gemm_ctx* c = (mx_gemm_ctx*)p;
+    double la[256], lb[256];
+    for (int i = 0; i < 256; ++i) {
+        la[i] = mx_decode(c->fa, (uint8_t)i);
+        lb[i] = mx_decode(c->fb, (uint8_t)i);
+    }
+    uint8_t* ca = (uint8_t*)malloc((size_t)c->K);
+    uint8_t* cb = (uint8_t*)malloc((size_t)c->K);
+    if (!ca || !cb) { free(ca); free(cb); return; }
+    for (uint64_t s = lo; s < hi; ++s) {
+        ptxo_mx_unpack(c->fa, c->A + c->rows[s] * c->K, ca, (size_t)c->K);
+        ptxo_mx_unpack(c->fb, c->B + c->cols[s] * c->K, cb, (size_t)c->K);
+        const uint8_t* sa = c->sfA + c->rows[s] * (c->K / 32);
+        const uint8_t* sb = c->sfB + c->cols[s] * (c->K / 32);
+        double acc = 0, mag = 0;
+        for (int64_t k = 0; k < c->K; ++k) {
+            const double t = la[ca[k]] * (double)ptxo_ue8m0_to_f32(sa[k >> 5]) * lb[cb[k]] *
+                             (double)ptxo_ue8m0_to_f32(sb[k >> 5]);
+            acc += t; mag += fabs(t);
+        }
+        c->ref[s] = acc; c->mag[s] = mag;
+    }
+    free(ca); free(cb);
+}
+
+void ptxo_gemm_mx_ref(const uint8_t* A, int fa, const uint8_t* sfA, const uint8_t* B, int fb,
+                      const uint8_t* sfB, int64_t M, int64_t N, int64_t K, const int64_t* rows,
+                      const int64_t* cols, int64_t n_samples, double* ref, double* mag,
+                      int threads) {
+    (void)M; (void)N;
+    mx_gemm_ctx c = {A, B, sfA, sfB, fa, fb, K, rows, cols, ref, mag};
+    parallel_for((uint64_t)n_samples, threads, mx_samples, &c);
+}
+
 /* 2:4 pruning (one row per job step): magnitude = code & 0x7F (E4M3 codes order like their
  * magnitudes; the NaN code 0x7F sorts highest), ties to the lower index. */
 typedef struct { const uint8_t* codes; int64_t cols; uint8_t *vals, *meta; } prune_ctx;

@@ -184,6 +184,22 @@ void ptxo_quantize_mxfp8_rs(const uint16_t* x, int64_t rows, int64_t cols, uint6
 int ptxo_quantize_nvfp4_rs(const uint16_t* x, int64_t rows, int64_t cols, float g, uint64_t seed,
                            uint8_t* q, uint8_t* sf, int threads);
 
+/* MX formats in the tcgen05 operand layout (kind::f8f6f4 / mxf8f6f4, dense K = 32; the
+ * reference's F8f6f4ElementType, src/tcgen05/descriptor.rs:306-327). Every format takes one byte
+ * per element in memory: FP8 codes as they are; FP6 (E2M3/E3M2) as groups of 16 six-bit codes
+ * packed little-endian (element i at bits 6i .. 6i+5 of the group's 96 bits, 12 bytes) followed
+ * by 4 zero bytes; FP4 (E2M1) as groups of 16 nibbles (element 2j in the low nibble of byte j, 8
+ * bytes) followed by 8 zero bytes. n % 16 == 0. `codes` holds one code per byte (format PTXO_*). */
+void ptxo_mx_pack(int format, const uint8_t* codes, uint8_t* packed, size_t n);
+void ptxo_mx_unpack(int format, const uint8_t* packed, uint8_t* codes, size_t n);
+/* OCP MX quantisation to any of the five element formats: one UE8M0 scale per 32 contiguous
+ * elements, floor-pow2 of the block amax (f8e8m0::from_f32::<TowardZero, SaturateFinite>) minus
+ * the format's emax (E4M3 8, E5M2 15, E2M3 2, E3M2 4, E2M1 2), clamped at 0; elements
+ * x * 2^-(scale - 127) encoded RN .satfinite. q [rows, cols] in the packed layout above,
+ * sf [rows, cols / 32] row-major. For PTXO_E4M3 this is ptxo_quantize_mxfp8. */
+void ptxo_quantize_mx(const uint16_t* x, int64_t rows, int64_t cols, int format, uint8_t* q,
+                      uint8_t* sf, int threads);
+
 /* ---- GEMM references (f64 over decoded values) at sampled outputs ------------------------- */
 /* FP8: C[i,j] = sa * sb * sum_k A[i,k] B[j,k]; A [M,K], B [N,K] E4M3 (K contiguous). For each
  * sample s: ref[s] = exact-ish f64 value, mag[s] = sa*sb*sum_k |A B|. */
@@ -201,6 +217,12 @@ void ptxo_gemm_mxfp8_ref(const uint8_t* A, const uint8_t* sfA, const uint8_t* B,
                          const uint8_t* sfB, int64_t M, int64_t N, int64_t K,
                          const int64_t* rows, const int64_t* cols, int64_t n_samples, double* ref,
                          double* mag, int threads);
+/* MX GEMM with any pair of element formats: A [M,K] and B [N,K] in the packed layout of
+ * ptxo_mx_pack (formats fa, fb), sfA [M,K/32], sfB [N,K/32] UE8M0 row-major. */
+void ptxo_gemm_mx_ref(const uint8_t* A, int fa, const uint8_t* sfA, const uint8_t* B, int fb,
+                      const uint8_t* sfB, int64_t M, int64_t N, int64_t K, const int64_t* rows,
+                      const int64_t* cols, int64_t n_samples, double* ref, double* mag,
+                      int threads);
 /* 2:4 structured sparsity of E4M3 codes [rows, cols] (cols % 8 == 0): in every group of four
  * consecutive elements of a row, the two with the largest magnitude (code & 0x7F; ties go to the
  * lower index) are kept, in index order, in vals [rows, cols/2]; meta [rows, cols/8] holds one

@@ -17,6 +17,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 
 E4M3, E5M2, E2M1, E2M3, E3M2 = 0, 1, 2, 3, 4
+# the tcgen05 element-type codes of kind::f8f6f4 / mxf8f6f4 (F8f6f4ElementType,
+# src/tcgen05/descriptor.rs:316-327) -> these formats
+MMA_TYPE_TO_FORMAT = {0: E4M3, 1: E5M2, 3: E2M3, 4: E3M2, 5: E2M1}
 (V_E4M3, V_E5M2, V_E2M1, V_E4M3_RELU, V_E5M2_RELU, V_E2M1_RELU, V_UE8M0_RZ,
  V_UE8M0_RP) = range(8)
 VARIANT_NAMES = ["e4m3", "e5m2", "e2m1", "e4m3_relu", "e5m2_relu", "e2m1_relu", "ue8m0_rz",
@@ -82,6 +85,10 @@ def _declare(L: C.CDLL) -> None:
                                        i32]),
         "ptxo_gemm_decode_ref": (None, [p, p, p, f32, i64, i64, i64, p, p, i64, p, p, i32]),
         "ptxo_gemm_mxfp8_ref": (None, [p, p, p, p, i64, i64, i64, p, p, i64, p, p, i32]),
+        "ptxo_mx_pack": (None, [i32, p, p, C.c_size_t]),
+        "ptxo_mx_unpack": (None, [i32, p, p, C.c_size_t]),
+        "ptxo_quantize_mx": (None, [p, i64, i64, i32, p, p, i32]),
+        "ptxo_gemm_mx_ref": (None, [p, i32, p, p, i32, p, i64, i64, i64, p, p, i64, p, p, i32]),
         "ptxo_sgemm_nt": (None, [p, p, p, i64, i64, i64, i32]),
         "ptxo_idesc_f16": (i32, [i32, i32, i32, u32, u32, C.POINTER(u32)]),
         "ptxo_idesc_tf32": (i32, [u32, u32, C.POINTER(u32)]),
@@ -211,6 +218,43 @@ def gemm_mxfp8_ref(A, sfA, B, sfB, rows, cols, threads=0):
     r, c, ref, mag = _samples(rows, cols)
     lib().ptxo_gemm_mxfp8_ref(_ptr(A), _ptr(sfA), _ptr(B), _ptr(sfB), M, N, K, _ptr(r), _ptr(c),
                               r.size, _ptr(ref), _ptr(mag), threads)
+    return ref, mag
+
+
+def mx_pack(fmt: int, codes: np.ndarray) -> np.ndarray:
+    """One code per byte -> the tcgen05 operand layout (FP6/FP4 groups of 16 padded to 16 bytes);
+    the last axis is the K axis (a multiple of 16)."""
+    c = np.ascontiguousarray(codes, dtype=np.uint8)
+    out = np.empty_like(c)
+    lib().ptxo_mx_pack(fmt, _ptr(c), _ptr(out), c.size)
+    return out
+
+
+def mx_unpack(fmt: int, packed: np.ndarray) -> np.ndarray:
+    p = np.ascontiguousarray(packed, dtype=np.uint8)
+    out = np.empty_like(p)
+    lib().ptxo_mx_unpack(fmt, _ptr(p), _ptr(out), p.size)
+    return out
+
+
+def quantize_mx(x_bf16: np.ndarray, fmt: int, threads: int = 0):
+    """OCP MX quantisation to `fmt` (E4M3 .. E3M2): (q [rows, cols] packed, sf [rows, cols/32])."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    rows, cols = x.shape
+    q = np.empty((rows, cols), dtype=np.uint8)
+    sf = np.empty((rows, cols // 32), dtype=np.uint8)
+    lib().ptxo_quantize_mx(_ptr(x), rows, cols, fmt, _ptr(q), _ptr(sf), threads)
+    return q, sf
+
+
+def gemm_mx_ref(A, fa, sfA, B, fb, sfB, rows, cols, threads=0):
+    """MX GEMM reference at sampled outputs: packed operands of formats fa / fb, row-major
+    UE8M0 scales [rows, K/32]."""
+    A, sfA, B, sfB = (np.ascontiguousarray(t, dtype=np.uint8) for t in (A, sfA, B, sfB))
+    (M, K), N = A.shape, B.shape[0]
+    r, c, ref, mag = _samples(rows, cols)
+    lib().ptxo_gemm_mx_ref(_ptr(A), fa, _ptr(sfA), _ptr(B), fb, _ptr(sfB), M, N, K, _ptr(r),
+                           _ptr(c), r.size, _ptr(ref), _ptr(mag), threads)
     return ref, mag
 
 

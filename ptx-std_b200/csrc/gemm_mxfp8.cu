@@ -9,6 +9,13 @@
 // InstrDescriptor::<Mxf8f6f4>::new(E4m3, E4m3, 256, 256) with its scale-factor ids
 // (src/tcgen05/descriptor.rs:601-611, :660-813).
 //
+// ptxstd_gemm_mx runs the same kernel for any pair of kind::mxf8f6f4 element types (E4M3, E5M2,
+// E2M3, E3M2, E2M1; A and B may differ), set in the instruction descriptor. For K = 32 MMAs the
+// 4- and 6-bit types take one byte per element in shared memory (16-element groups padded to 16
+// bytes, src/tcgen05/descriptor.rs:306-315), so the tiles, TMA boxes and shared-memory
+// descriptors are those of FP8; operands come in that padded layout, as ptxstd_quantize_mx
+// writes it.
+//
 // A cluster of two CTAs computes a 256 x 256 tile. CTA r loads A rows [128 r, +128) and B rows
 // [128 r, +128) of the tile, A's scales for its rows and B's scales for all 256 columns (each
 // CTA accumulates all N columns of its rows), everything completing on the leader's `full`
@@ -111,7 +118,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                            const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmSfa,
                            const __grid_constant__ CUtensorMap tmSfb, uint16_t* __restrict__ C,
-                           uint32_t M, uint32_t N, uint32_t K, uint32_t* err) {
+                           uint32_t M, uint32_t N, uint32_t K, uint32_t atype, uint32_t btype,
+                           uint32_t* err) {
     extern __shared__ uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~static_cast<uintptr_t>(1023));
@@ -190,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- MMA issuer (leader) ----------------
         if (rank == 0 && ptxstd::elect_one()) {
             uint32_t idesc0 = 0;
-            t5::idesc_mxf8f6f4(/*E4m3*/ 0, /*E4m3*/ 0, P_BM, P_BN, idesc0);
+            t5::idesc_mxf8f6f4(atype, btype, P_BM, P_BN, idesc0);
             uint32_t idesc[kMmas];
 #pragma unroll
             for (uint32_t j = 0; j < kMmas; ++j) {
@@ -300,9 +308,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-extern "C" int ptxstd_gemm_mxfp8(const uint8_t* d_a, const uint8_t* d_sfa, const uint8_t* d_b,
-                                 const uint8_t* d_sfb, uint16_t* d_c, int64_t M, int64_t N,
-                                 int64_t K, ptxstd_stream stream) {
+namespace {
+bool mx_type_ok(int t) { return t == 0 || t == 1 || t == 3 || t == 4 || t == 5; }
+}  // namespace
+
+extern "C" int ptxstd_gemm_mx(const uint8_t* d_a, int a_type, const uint8_t* d_sfa,
+                              const uint8_t* d_b, int b_type, const uint8_t* d_sfb, uint16_t* d_c,
+                              int64_t M, int64_t N, int64_t K, ptxstd_stream stream) {
+    if (!mx_type_ok(a_type) || !mx_type_ok(b_type)) return PTXSTD_EINVAL;
     if (M <= 0 || N <= 0 || K <= 0 || M % P_BM || N % P_BN || K % BK) return PTXSTD_EINVAL;
     if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) return PTXSTD_EINVAL;
     if (!d_a || !d_b || !d_c || !d_sfa || !d_sfb || !ptxstd::aligned16(d_a) ||
@@ -358,7 +371,14 @@ extern "C" int ptxstd_gemm_mxfp8(const uint8_t* d_a, const uint8_t* d_sfa, const
     cfg.gridDim = dim3(2 * pairs);
     if (cudaLaunchKernelEx(&cfg, gemm_mxfp8_pair_kernel, ta, tb, tsa, tsb, d_c,
                            static_cast<uint32_t>(M), static_cast<uint32_t>(N),
-                           static_cast<uint32_t>(K), err) != cudaSuccess)
+                           static_cast<uint32_t>(K), static_cast<uint32_t>(a_type),
+                           static_cast<uint32_t>(b_type), err) != cudaSuccess)
         return PTXSTD_ECUDA;
     return ptxstd::launch_status();
+}
+
+extern "C" int ptxstd_gemm_mxfp8(const uint8_t* d_a, const uint8_t* d_sfa, const uint8_t* d_b,
+                                 const uint8_t* d_sfb, uint16_t* d_c, int64_t M, int64_t N,
+                                 int64_t K, ptxstd_stream stream) {
+    return ptxstd_gemm_mx(d_a, 0, d_sfa, d_b, 0, d_sfb, d_c, M, N, K, stream);
 }

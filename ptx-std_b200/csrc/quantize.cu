@@ -127,6 +127,85 @@ struct Nvfp4 {
     }
 };
 
+// OCP MX quantisation to any element type of kind::mxf8f6f4, named by its tcgen05 code T
+// (F8f6f4ElementType, src/tcgen05/descriptor.rs:316-327): 0 E4M3, 1 E5M2, 3 E2M3, 4 E3M2,
+// 5 E2M1. The scale is the MXFP8 recipe with the format's own emax (floor-pow2 of the block amax,
+// TowardZero + SaturateFinite, minus emax, clamped at 0); the elements are RN .satfinite. The
+// payload is written in the tensor cores' operand layout, one byte per element in memory
+// (descriptor.rs:306-315): FP8 codes as they are; FP6 as groups of 16 six-bit codes packed
+// little-endian into 12 bytes plus 4 zero bytes; FP4 as 16 nibbles in 8 bytes plus 8 zero bytes.
+// A 16-element group is the vectors of two neighbouring lanes, so the even lane gathers the bits
+// that spill into its 8 bytes from its partner with one shuffle.
+template <bool BLOCKED, uint32_t T>
+struct MxAny {
+    static constexpr uint32_t kLanesPerBlock = 4;  // 32 elements
+    static constexpr uint32_t kEmax = T == 0 ? 8u : T == 1 ? 15u : T == 4 ? 4u : 2u;
+    float six_g;  // unused
+    __device__ __forceinline__ void operator()(const uint4 v, bool valid, size_t gv, uint32_t lane,
+                                               uint8_t* q, uint8_t* sf, size_t sf_cols) const {
+        uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                              dt::bf16x2_absmax_bits(v.z, v.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        const uint32_t u = dt::ue8m0_from_f32<false, true>(__uint_as_float(m << 16));
+        const uint32_t code = u == 0xFFu ? 0xFFu : (u > kEmax ? u - kEmax : 0u);
+        const float inv = dt::ue8m0_inverse(code);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t lo, hi;  // this vector's 8 bytes of the payload
+        if constexpr (T == 0 || T == 1) {
+            uint32_t p[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = dt::bf16x2_mul_f32(w[k], inv);
+                p[k] = T == 0 ? dt::e4m3x2_from_f32<false>(f.x, f.y)
+                              : dt::e5m2x2_from_f32<false>(f.x, f.y);
+            }
+            lo = p[0] | (p[1] << 16);
+            hi = p[2] | (p[3] << 16);
+        } else if constexpr (T == 3 || T == 4) {
+            uint64_t bits = 0;  // element i of the vector at bits 6i .. 6i+5
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = dt::bf16x2_mul_f32(w[k], inv);
+                const uint32_t c2 = T == 3 ? dt::e2m3x2_from_f32<false>(f.x, f.y)
+                                           : dt::e3m2x2_from_f32<false>(f.x, f.y);
+                bits |= static_cast<uint64_t>(c2 & 0x3Fu) << (12 * k);
+                bits |= static_cast<uint64_t>((c2 >> 8) & 0x3Fu) << (12 * k + 6);
+            }
+            const uint32_t b_lo = static_cast<uint32_t>(bits);
+            const uint32_t b_hi = static_cast<uint32_t>(bits >> 32);  // bits 32 .. 47
+            const uint32_t partner_lo = __shfl_xor_sync(0xffffffffu, b_lo, 1);
+            if (lane & 1u) {
+                // elements 8..15 hold group bits 48..95; bytes 8..15 = group bits 64..95 + pad
+                lo = (b_lo >> 16) | (b_hi << 16);
+                hi = 0u;
+            } else {
+                // bytes 0..7 = group bits 0..63: own 48 bits, then the partner's first 16
+                lo = b_lo;
+                hi = b_hi | (partner_lo << 16);
+            }
+        } else {
+            uint32_t packed = 0;  // 8 nibbles, element 0 in the low nibble
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = dt::bf16x2_mul_f32(w[k], inv);
+                packed |= dt::e2m1x2_from_f32<false>(f.x, f.y) << (8 * k);
+            }
+            const uint32_t partner = __shfl_xor_sync(0xffffffffu, packed, 1);
+            lo = (lane & 1u) ? 0u : packed;
+            hi = (lane & 1u) ? 0u : partner;
+        }
+        if (valid) {
+            reinterpret_cast<uint2*>(q)[gv] = make_uint2(lo, hi);
+            if ((lane & 3u) == 0) store_scale<BLOCKED>(sf, gv >> 2, sf_cols, code);
+        }
+    }
+};
+
+template <uint32_t T>
+int launch_mx(const uint16_t* x, size_t n, uint8_t* q, uint8_t* sf, size_t sf_cols, int blocked,
+              cudaStream_t s);
+
 // Stochastic-rounding MXFP8: the same scale; elements 8 gv .. 8 gv + 3 with the low word of
 // splitmix64(seed, gv), elements + 4 .. + 7 with the high word.
 template <bool BLOCKED>
@@ -292,9 +371,36 @@ int launch(const uint16_t* x, size_t n_elems, Op op, uint8_t* q, uint8_t* sf, si
     return ptxstd::launch_status();
 }
 
+template <uint32_t T>
+int launch_mx(const uint16_t* x, size_t n, uint8_t* q, uint8_t* sf, size_t sf_cols, int blocked,
+              cudaStream_t s) {
+    if (blocked) return launch<DefaultCfg>(x, n, MxAny<true, T>{0.0f}, q, sf, sf_cols, s);
+    return launch<DefaultCfg>(x, n, MxAny<false, T>{0.0f}, q, sf, sf_cols, s);
+}
+
 }  // namespace
 
 extern "C" {
+
+int ptxstd_quantize_mx(const uint16_t* d_x, int64_t rows, int64_t cols, int elem_type,
+                       uint8_t* d_q, uint8_t* d_sf, int sf_layout, ptxstd_stream stream) {
+    if (rows <= 0 || cols <= 0 || cols % 32 != 0) return PTXSTD_EINVAL;
+    if (!d_x || !d_q || !d_sf || !ptxstd::aligned16(d_x) || !ptxstd::aligned16(d_q))
+        return PTXSTD_EINVAL;
+    if (sf_layout != 0 && sf_layout != 1) return PTXSTD_EINVAL;
+    if (sf_layout == 1 && (rows % 128 != 0 || cols % 128 != 0)) return PTXSTD_EINVAL;
+    const size_t n = static_cast<size_t>(rows) * static_cast<size_t>(cols);
+    const size_t sf_cols = static_cast<size_t>(cols) / 32;
+    auto s = static_cast<cudaStream_t>(stream);
+    switch (elem_type) {
+    case 0: return launch_mx<0>(d_x, n, d_q, d_sf, sf_cols, sf_layout, s);
+    case 1: return launch_mx<1>(d_x, n, d_q, d_sf, sf_cols, sf_layout, s);
+    case 3: return launch_mx<3>(d_x, n, d_q, d_sf, sf_cols, sf_layout, s);
+    case 4: return launch_mx<4>(d_x, n, d_q, d_sf, sf_cols, sf_layout, s);
+    case 5: return launch_mx<5>(d_x, n, d_q, d_sf, sf_cols, sf_layout, s);
+    default: return PTXSTD_EINVAL;
+    }
+}
 
 int ptxstd_quantize_mxfp8_layout(const uint16_t* d_x, int64_t rows, int64_t cols, uint8_t* d_q,
                                  uint8_t* d_sf, int sf_layout, ptxstd_stream stream) {

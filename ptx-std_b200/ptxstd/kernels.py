@@ -63,6 +63,49 @@ def gemm_mxfp8(a, sfa, b, sfb, out=None, stream=None):
     return c
 
 
+# MX element types (the tcgen05 F8f6f4ElementType codes)
+MX_E4M3, MX_E5M2, MX_E2M3, MX_E3M2, MX_E2M1 = 0, 1, 3, 4, 5
+MX_TYPES = {"e4m3": MX_E4M3, "e5m2": MX_E5M2, "e2m3": MX_E2M3, "e3m2": MX_E3M2, "e2m1": MX_E2M1}
+
+
+def _mx_type(t) -> int:
+    return MX_TYPES[t] if isinstance(t, str) else int(t)
+
+
+def quantize_mx(x, elem_type, sf_layout: int = 1, out=None, stream=None):
+    """bf16 [rows, cols] -> (payload [rows, cols] uint8 in the tensor-core operand layout,
+    UE8M0 scales per 32) for any MX element type ("e4m3", "e5m2", "e2m3", "e3m2", "e2m1" or the
+    MX_* code). FP6 / FP4 payloads are 16-element groups padded to 16 bytes."""
+    torch = _torch()
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise TypeError("expected a 2-D bfloat16 tensor")
+    rows, cols = x.shape
+    if out is None:
+        q = torch.empty((rows, cols), dtype=torch.uint8, device=x.device)
+        sf = torch.empty((rows, cols // 32), dtype=torch.uint8, device=x.device)
+    else:
+        q, sf = out
+    check(lib().ptxstd_quantize_mx(_dev(x), rows, cols, _mx_type(elem_type), _dev(q), _dev(sf),
+                                   sf_layout, _stream(stream)), "quantize_mx")
+    return q, sf
+
+
+def gemm_mx(a, a_type, sfa, b, b_type, sfb, out=None, stream=None):
+    """MX GEMM with any pair of element types: a [M, K], b [N, K] payloads in the operand layout
+    of quantize_mx, blocked UE8M0 scales per 32 -> bf16 [M, N]."""
+    torch = _torch()
+    M, K = a.shape
+    N = b.shape[0]
+    if b.shape[1] != K:
+        raise ValueError("K mismatch")
+    if sfa.numel() != M * K // 32 or sfb.numel() != N * K // 32:
+        raise ValueError("scale tensors must hold one UE8M0 per 32 elements")
+    c = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    check(lib().ptxstd_gemm_mx(_dev(a), _mx_type(a_type), _dev(sfa), _dev(b), _mx_type(b_type),
+                               _dev(sfb), _dev(c), M, N, K, _stream(stream)), "gemm_mx")
+    return c
+
+
 def prune_24(codes, stream=None):
     """2:4 pruning of E4M3 codes [rows, cols] (uint8) -> (vals [rows, cols/2], meta [rows, cols/8])
     (ptxstd_prune_24_e4m3: the two largest magnitudes of each group of four are kept)."""

@@ -63,6 +63,12 @@ def test_host_validation_without_gpu(ptxstd_lib):
     assert L.ptxstd_quantize_mxfp8_rs(16, 128, 96 + 1, 16, 16, 0, 1, None) == EINVAL
     assert L.ptxstd_quantize_nvfp4_rs(16, 128, 64, 0.0, 16, 16, 0, 1, None) == EINVAL
     assert L.ptxstd_cvt_sweep(0, (1 << 32) - 8, 16, 16, None) == EINVAL
+    # MX element types are the tcgen05 codes 0, 1, 3, 4, 5 (2 is not one)
+    assert L.ptxstd_quantize_mx(16, 128, 128, 2, 16, 16, 0, None) == EINVAL
+    assert L.ptxstd_quantize_mx(16, 128, 96 + 1, 0, 16, 16, 0, None) == EINVAL
+    assert L.ptxstd_gemm_mx(16, 2, 16, 16, 0, 16, 16, 256, 256, 128, None) == EINVAL
+    assert L.ptxstd_gemm_mx(16, 0, 16, 16, 6, 16, 16, 256, 256, 128, None) == EINVAL
+    assert L.ptxstd_gemm_mx(16, 3, 16, 16, 5, 16, 16, 256, 256, 100, None) == EINVAL
 
 
 def test_dist_validation_without_gpu(ptxstd_lib):

@@ -532,3 +532,70 @@ def test_bf16_mode_rules(oracle):
     assert f(0x7F7FFFFF) == 0x7F80 and f(0x7F7FFFFF, 0, 1) == 0x7F7F   # rounds past max
     assert f(0xFF800000, 0, 1) == 0xFF7F and f(0xFF800000, 1, 0) == 0
     assert f(0x80000000, 1, 0) == 0 and f(0x7FC00001) == 0x7FFF
+
+
+# ---- MX formats in the tensor-core operand layout ------------------------------------------
+
+_MX_FORMATS = [("e4m3", 0, 0xFF), ("e5m2", 1, 0xFF), ("e2m3", 3, 0x3F), ("e3m2", 4, 0x3F),
+               ("e2m1", 2, 0x0F)]
+
+
+@pytest.mark.parametrize("name,fmt,mask", _MX_FORMATS)
+def test_mx_pack_round_trip(oracle, name, fmt, mask):
+    """Packing into the K = 32 operand layout (descriptor.rs:306-315) and back is the identity;
+    FP6 groups end in 4 zero bytes, FP4 groups in 8."""
+    rng = np.random.default_rng(7 + fmt)
+    codes = (rng.integers(0, 256, (8, 128)) & mask).astype(np.uint8)
+    packed = oracle.mx_pack(fmt, codes)
+    assert packed.shape == codes.shape
+    assert np.array_equal(oracle.mx_unpack(fmt, packed), codes)
+    pad = {oracle.E2M3: 12, oracle.E3M2: 12, oracle.E2M1: 8}.get(fmt)
+    if pad is not None:
+        assert not packed.reshape(-1, 16)[:, pad:].any()
+    else:
+        assert np.array_equal(packed, codes)
+
+
+def test_mx_pack_known_answers(oracle):
+    """Element i of an FP6 group at bits 6i .. 6i+5 of its little-endian 96 bits; FP4 element 2j
+    in the low nibble of byte j."""
+    one = np.zeros((1, 16), dtype=np.uint8)
+    for i in range(16):
+        c = one.copy()
+        c[0, i] = 0x3F
+        bits = int.from_bytes(oracle.mx_pack(oracle.E2M3, c).tobytes()[:12], "little")
+        assert bits == 0x3F << (6 * i)
+        c[0, i] = 0x9
+        p = oracle.mx_pack(oracle.E2M1, c & 0xF).tobytes()
+        assert p[i // 2] == (0x9 << (4 * (i % 2))) and sum(p) == p[i // 2]
+
+
+def test_quantize_mx_e4m3_is_mxfp8(oracle):
+    from ptxstd import workloads
+    x = workloads.mxfp8_activation(64, 512)
+    q, sf = oracle.quantize_mx(x, oracle.E4M3)
+    q8, sf8 = oracle.quantize_mxfp8(x)
+    assert np.array_equal(q, q8) and np.array_equal(sf, sf8)
+
+
+@pytest.mark.parametrize("name,fmt,mask", _MX_FORMATS)
+def test_quantize_mx_scale_recipe(oracle, name, fmt, mask):
+    """Scale = floor(log2 amax) - emax(format) + 127: a block whose amax is the format's largest
+    finite value gets 2^0, one whose amax is 2^e gets 2^(e - emax); elements then decode back to
+    the input exactly when it is representable."""
+    emax = {0: 8, 1: 15, 3: 2, 4: 4, 2: 2}[fmt]
+    top = {0: 448.0, 1: 57344.0, 3: 7.5, 4: 28.0, 2: 6.0}[fmt]
+    x = np.zeros((2, 32), dtype=np.float32)
+    x[0, :] = np.linspace(-top, top, 32).astype(np.float32)
+    x[0, 0], x[0, 31] = -top, top
+    x[1, :] = 0.0
+    x[1, 5] = 2.0 ** 10
+    bf = (x.view(np.uint32) >> 16).astype(np.uint16)
+    q, sf = oracle.quantize_mx(bf, fmt)
+    assert sf[0, 0] == 127 + (int(np.floor(np.log2(top))) - emax)
+    assert sf[1, 0] == 127 + 10 - emax
+    codes = oracle.mx_unpack(fmt, q)
+    dec = oracle.decode(fmt, codes[0] if fmt != oracle.E2M1 else
+                        (codes[0, 0::2] | (codes[0, 1::2] << 4)).astype(np.uint8))
+    assert dec[0] == -top * 2.0 ** -(int(sf[0, 0]) - 127) and dec[-1] == -dec[0]
+    assert codes[1, 5] != 0 and not np.delete(codes[1], 5).any()
