@@ -405,6 +405,57 @@ class Mxfp8Gemm(Fp8Gemm):
         return 1
 
 
+class MxFp6Gemm(Fp8Gemm):
+    """MXFP6 (OCP MX, E2M3 elements, UE8M0 per 32) A [8192, 8192] x B [8192, 8192] -> bf16 C on
+    tcgen05.mma.kind::mxf8f6f4: payloads in the padded FP6 operand layout (16 six-bit codes + 4
+    zero bytes per 16 bytes), quantised on the device from N(0, 1) bf16 by ptxstd_quantize_mx."""
+
+    name = "mxfp6_gemm"
+    dtype = "e2m3 x e2m3 (ue8m0/32 scales) -> f32 acc -> bf16"
+    kernel = "gemm_mxfp8_pair_kernel"
+    peak_note = "dense MXFP6 on kind::mxf8f6f4 = 2x bf16"
+
+    def __init__(self, world: int = 1):
+        super().__init__(world)
+        self.in_bytes += (self.M + self.N) * self.K // 32
+        self.bytes = self.in_bytes + self.out_bytes
+        self.config = {"workload": "mxfp6_gemm e2m3+ue8m0/32 8192x8192x8192 -> bf16",
+                       "M": self.M, "N": self.N, "K": self.K,
+                       "layout": "FP6 16-element groups padded to 16 bytes (1 byte per element)",
+                       "l2": "operands 132 MiB + output 128 MiB per step (> L2)"}
+
+    # host_input (inherited) gives the CPU baseline its operands: the f32 blocked GEMM over decoded
+    # values costs the same whatever narrow format they were decoded from
+
+    def setup(self, torch, _):
+        import ptxstd
+        g = torch.Generator(device="cuda")
+        g.manual_seed(6161)
+        xa = torch.randn((self.M, self.K), generator=g, device="cuda").to(torch.bfloat16)
+        xb = torch.randn((self.N, self.K), generator=g, device="cuda").to(torch.bfloat16)
+        self.a, self.sfa = ptxstd.quantize_mx(xa, ptxstd.MX_E2M3, sf_layout=1)
+        self.b, self.sfb = ptxstd.quantize_mx(xb, ptxstd.MX_E2M3, sf_layout=1)
+        del xa, xb
+        self.c = torch.empty((self.M, self.N), dtype=torch.bfloat16, device="cuda")
+        self.host = [t.cpu().pin_memory() for t in (self.a, self.sfa, self.b, self.sfb)]
+
+    def step(self, i):
+        import ptxstd
+        ptxstd.gemm_mx(self.a, ptxstd.MX_E2M3, self.sfa, self.b, ptxstd.MX_E2M3, self.sfb,
+                       out=self.c)
+        return 1
+
+    def e2e_slots(self, torch):
+        return _gemm_slots(torch, list(zip((self.a, self.sfa, self.b, self.sfb), self.host)),
+                           self.c)
+
+    def e2e_compute(self, i, args):
+        import ptxstd
+        a, sfa, b, sfb, c = args
+        ptxstd.gemm_mx(a, ptxstd.MX_E2M3, sfa, b, ptxstd.MX_E2M3, sfb, out=c)
+        return 1
+
+
 class Mxfp8SparseGemm(Fp8Gemm):
     """2:4-sparse MXFP8: A [8192, 8192] pruned to 2:4 (vals [8192, 4096] + metadata [8192, 1024]) x
     dense B [8192, 8192], UE8M0 scales per 64 logical K -> bf16 C. TFLOP/s count the logical
@@ -722,7 +773,8 @@ class MxFp8QuantizeSR(MxFp8Quantize):
 
 WORKLOADS = {"mxfp8_quantize": MxFp8Quantize, "fp8_gemm": Fp8Gemm, "nvfp4_gemm": Nvfp4Gemm,
              "decode_gemm": DecodeGemm, "mxfp8_gemm": Mxfp8Gemm,
-             "mxfp8_quantize_sr": MxFp8QuantizeSR, "mxfp8_gemm_sparse": Mxfp8SparseGemm}
+             "mxfp8_quantize_sr": MxFp8QuantizeSR, "mxfp8_gemm_sparse": Mxfp8SparseGemm,
+             "mxfp6_gemm": MxFp6Gemm}
 
 
 # ---- arms -----------------------------------------------------------------------------------

@@ -269,6 +269,13 @@ PTXSTD_API int ptxstd_quantize_mx(const uint16_t* d_x, int64_t rows, int64_t col
 PTXSTD_API int ptxstd_gemm_mx(const uint8_t* d_a, int a_type, const uint8_t* d_sfa,
                               const uint8_t* d_b, int b_type, const uint8_t* d_sfb, uint16_t* d_c,
                               int64_t M, int64_t N, int64_t K, ptxstd_stream stream);
+/* The decompressing shared-memory -> Tensor Memory copy (copy::<S128x256b, B6x16P32 | B4x16P64>,
+ * src/tcgen05/copy.rs:32-46, :76-116), run over n_tiles tiles of 128 rows x 32 bytes: packed FP6
+ * (elem_type PTXSTD_MX_E2M3 / E3M2: .b8x16.b6x16_p32) or FP4 (PTXSTD_MX_E2M1: .b8x16.b4x16_p64)
+ * groups in the layout of ptxstd_quantize_mx go through tcgen05.cp into TMEM and come back with
+ * tcgen05.ld as one 8-bit container per element, [n_tiles * 128, 32] bytes. */
+PTXSTD_API int ptxstd_tcgen05_cp_unpack(const uint8_t* d_packed, uint8_t* d_out, int64_t n_tiles,
+                                        int elem_type, ptxstd_stream stream);
 /* 2:4 structured sparsity (the A operand of tcgen05.mma.sp, src/tcgen05/mma.rs:725-777): in each
  * group of four consecutive elements of a row of E4M3 codes [rows, cols], the two of largest
  * magnitude (code & 0x7F, ties to the lower index) are kept, in index order, in vals

@@ -1015,6 +1015,15 @@ void ptxo_mx_unpack(int format, const uint8_t* packed, uint8_t* codes, size_t n)
     }
 }
 
+void ptxo_cp_unpack(int format, const uint8_t* packed, uint8_t* containers, size_t n) {
+    /* FP6: the 6-bit code in bits 5..0 of its container. FP4: the nibble in bits 5..2, i.e. at
+     * the sign / exponent / mantissa positions of an E2M3 value with two zero mantissa bits
+     * below (pinned on the B200). The other bits are zero. */
+    ptxo_mx_unpack(format, packed, containers, n);
+    if (format == PTXO_E2M1)
+        for (size_t i = 0; i < n; ++i) containers[i] = (uint8_t)(containers[i] << 2);
+}
+
 static int mx_emax(int format) {
     switch (format) {
     case PTXO_E4M3: return 8;

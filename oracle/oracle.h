@@ -192,6 +192,10 @@ int ptxo_quantize_nvfp4_rs(const uint16_t* x, int64_t rows, int64_t cols, float 
  * bytes) followed by 8 zero bytes. n % 16 == 0. `codes` holds one code per byte (format PTXO_*). */
 void ptxo_mx_pack(int format, const uint8_t* codes, uint8_t* packed, size_t n);
 void ptxo_mx_unpack(int format, const uint8_t* packed, uint8_t* codes, size_t n);
+/* The 8-bit containers that tcgen05.cp's .b8x16.b6x16_p32 / .b8x16.b4x16_p64 decompression
+ * writes for n elements of packed FP6 / FP4 groups (copy.rs:32-46), one per element: an FP6 code
+ * in bits 5..0; an FP4 code in bits 5..2 (E2M3-aligned, two zero mantissa bits below). */
+void ptxo_cp_unpack(int format, const uint8_t* packed, uint8_t* containers, size_t n);
 /* OCP MX quantisation to any of the five element formats: one UE8M0 scale per 32 contiguous
  * elements, floor-pow2 of the block amax (f8e8m0::from_f32::<TowardZero, SaturateFinite>) minus
  * the format's emax (E4M3 8, E5M2 15, E2M3 2, E3M2 4, E2M1 2), clamped at 0; elements

@@ -87,6 +87,7 @@ def _declare(L: C.CDLL) -> None:
         "ptxo_gemm_mxfp8_ref": (None, [p, p, p, p, i64, i64, i64, p, p, i64, p, p, i32]),
         "ptxo_mx_pack": (None, [i32, p, p, C.c_size_t]),
         "ptxo_mx_unpack": (None, [i32, p, p, C.c_size_t]),
+        "ptxo_cp_unpack": (None, [i32, p, p, C.c_size_t]),
         "ptxo_quantize_mx": (None, [p, i64, i64, i32, p, p, i32]),
         "ptxo_gemm_mx_ref": (None, [p, i32, p, p, i32, p, i64, i64, i64, p, p, i64, p, p, i32]),
         "ptxo_sgemm_nt": (None, [p, p, p, i64, i64, i64, i32]),
@@ -234,6 +235,14 @@ def mx_unpack(fmt: int, packed: np.ndarray) -> np.ndarray:
     p = np.ascontiguousarray(packed, dtype=np.uint8)
     out = np.empty_like(p)
     lib().ptxo_mx_unpack(fmt, _ptr(p), _ptr(out), p.size)
+    return out
+
+
+def cp_unpack(fmt: int, packed: np.ndarray) -> np.ndarray:
+    """The 8-bit containers of tcgen05.cp's FP6 / FP4 decompression, one per element."""
+    p_ = np.ascontiguousarray(packed, dtype=np.uint8)
+    out = np.empty_like(p_)
+    lib().ptxo_cp_unpack(fmt, _ptr(p_), _ptr(out), p_.size)
     return out
 
 

@@ -378,6 +378,28 @@ __device__ __forceinline__ void ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32])
         : "r"(taddr)
         : "memory");
 }
+// load::<S32x32b, x8>.
+__device__ __forceinline__ void ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7])
+        : "r"(taddr)
+        : "memory");
+}
+// copy::<S128x256b, B6x16P32> / <S128x256b, B4x16P64> (src/tcgen05/copy.rs:32-46, :76-116):
+// 128 rows x 32 bytes of packed 6-bit (4-bit) elements, 16 per 16-byte group, into 128 lanes x
+// 256 bits of 8-bit containers.
+__device__ __forceinline__ void cp_128x256b_b6x16_p32(uint32_t taddr, uint64_t src_desc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x256b.b8x16.b6x16_p32 [%0], %1;" ::"r"(taddr),
+                 "l"(src_desc)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_128x256b_b4x16_p64(uint32_t taddr, uint64_t src_desc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x256b.b8x16.b4x16_p64 [%0], %1;" ::"r"(taddr),
+                 "l"(src_desc)
+                 : "memory");
+}
 // load::<S32x32b, x16>.
 __device__ __forceinline__ void ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(

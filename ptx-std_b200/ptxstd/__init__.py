@@ -114,6 +114,8 @@ _SIGS = {
                                     C.c_void_p]),
     "ptxstd_quantize_mx": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int, C.c_void_p,
                                      C.c_void_p, C.c_int, C.c_void_p]),
+    "ptxstd_tcgen05_cp_unpack": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int,
+                                           C.c_void_p]),
     "ptxstd_gemm_mx": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                                  C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
                                  C.c_void_p]),
@@ -212,9 +214,11 @@ def last_device_error(clear: bool = True, stream=None) -> tuple[int, int]:
 from . import data_types, tcgen05  # noqa: E402
 from .kernels import (MX_E2M1, MX_E2M3, MX_E3M2, MX_E4M3, MX_E5M2,  # noqa: E402
                       gemm_decode, gemm_fp8, gemm_mx, gemm_mxfp8, gemm_mxfp8_sparse, gemm_nvfp4,
-                      prune_24, quantize_mx, quantize_mxfp8, quantize_nvfp4)
+                      prune_24, quantize_mx, quantize_mxfp8, quantize_nvfp4,
+                      tcgen05_cp_unpack)
 
 __all__ = ["lib", "check", "PtxStdError", "status_string", "last_device_error", "data_types",
            "tcgen05", "quantize_mxfp8", "quantize_nvfp4", "quantize_mx", "gemm_fp8",
            "gemm_mxfp8", "gemm_mx", "gemm_nvfp4", "gemm_decode", "gemm_mxfp8_sparse", "prune_24",
+           "tcgen05_cp_unpack",
            "MX_E4M3", "MX_E5M2", "MX_E2M3", "MX_E3M2", "MX_E2M1"]

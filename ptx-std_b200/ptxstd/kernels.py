@@ -106,6 +106,20 @@ def gemm_mx(a, a_type, sfa, b, b_type, sfb, out=None, stream=None):
     return c
 
 
+def tcgen05_cp_unpack(packed, elem_type, stream=None):
+    """Packed FP6 / FP4 rows [n * 128, 32] (uint8, the quantize_mx layout) through the
+    decompressing tcgen05.cp into TMEM and back: one 8-bit container per element, same shape."""
+    torch = _torch()
+    if packed.dtype != torch.uint8 or packed.dim() != 2 or packed.shape[1] != 32 or \
+            packed.shape[0] % 128:
+        raise ValueError("expected uint8 [n * 128, 32]")
+    out = torch.empty_like(packed)
+    check(lib().ptxstd_tcgen05_cp_unpack(_dev(packed), _dev(out), packed.shape[0] // 128,
+                                         _mx_type(elem_type), _stream(stream)),
+          "tcgen05_cp_unpack")
+    return out
+
+
 def prune_24(codes, stream=None):
     """2:4 pruning of E4M3 codes [rows, cols] (uint8) -> (vals [rows, cols/2], meta [rows, cols/8])
     (ptxstd_prune_24_e4m3: the two largest magnitudes of each group of four are kept)."""

@@ -125,3 +125,24 @@ def test_quantize_then_gemm_mx(cuda, oracle, ta, tb):
     ref, mag = oracle.gemm_mx_ref(Ao, TYPES[ta][1], sfAo, Bo, TYPES[tb][1], sfBo, rows, cols)
     got = C.float().cpu().numpy()[rows, cols].astype(np.float64)
     assert (np.abs(got - ref) <= 2.0 ** -10 * mag + 2.0 ** -8 * np.abs(ref)).all()
+
+
+@pytest.mark.parametrize("name", ["e2m3", "e3m2", "e2m1"])
+def test_tcgen05_cp_decompression(cuda, oracle, name):
+    """tcgen05.cp .b8x16.b6x16_p32 / .b8x16.b4x16_p64 on every code: each packed element lands in
+    its own 8-bit container, in order: an FP6 code in bits 5..0, an FP4 code in bits 5..2 (as an
+    E2M3-aligned value), the other bits zero."""
+    torch = cuda
+    import ptxstd
+    t, fmt, mask = TYPES[name]
+    rows = 128 * 8
+    rng = np.random.default_rng(90 + t)
+    codes = (rng.integers(0, 256, (rows, 32)) & mask).astype(np.uint8)
+    codes[0, :] = np.arange(32) & mask                      # a known row
+    packed = oracle.mx_pack(fmt, codes)
+    got = ptxstd.tcgen05_cp_unpack(torch.from_numpy(packed).cuda(), name).cpu().numpy()
+    code, detail = ptxstd.last_device_error()
+    assert code == 0, (code, hex(detail))
+    want = oracle.cp_unpack(fmt, packed)
+    assert np.array_equal(got, want), (got[0].tobytes().hex(), want[0].tobytes().hex(),
+                                       packed[0].tobytes().hex())

@@ -599,3 +599,13 @@ def test_quantize_mx_scale_recipe(oracle, name, fmt, mask):
                         (codes[0, 0::2] | (codes[0, 1::2] << 4)).astype(np.uint8))
     assert dec[0] == -top * 2.0 ** -(int(sf[0, 0]) - 127) and dec[-1] == -dec[0]
     assert codes[1, 5] != 0 and not np.delete(codes[1], 5).any()
+
+
+def test_cp_unpack_container_rule(oracle):
+    """tcgen05.cp decompression, as pinned on the B200: an FP6 code sits in bits 5..0 of its 8-bit
+    container, an FP4 code in bits 5..2 (row of codes 0..15 twice -> 00 04 08 .. 3c, twice)."""
+    c6 = (np.arange(32) & 0x3F).astype(np.uint8)[None, :]
+    assert np.array_equal(oracle.cp_unpack(oracle.E2M3, oracle.mx_pack(oracle.E2M3, c6)), c6)
+    c4 = (np.arange(32) & 0xF).astype(np.uint8)[None, :]
+    got = oracle.cp_unpack(oracle.E2M1, oracle.mx_pack(oracle.E2M1, c4))
+    assert got.tobytes().hex() == "0004080c1014181c2024282c3034383c" * 2
