@@ -59,7 +59,9 @@ constexpr uint32_t kSfBase = kAccCols;
 constexpr uint32_t kTmemCols = 512;
 static_assert(kSfBase + STAGES * kSlotCols <= kTmemCols, "TMEM budget");
 static_assert(kSlotCols % 4 == 0, "metadata and scale slots start on 4-column boundaries");
-constexpr uint32_t kGroupM = 8;
+// Grouped raster of kGroupM row-tiles; 16 measured 2-4 % ahead of 8 at 8192^3 (five interleaved
+// repetitions each on one B200, bit-identical output).
+constexpr uint32_t kGroupM = 16;
 
 struct alignas(1024) Smem {
     uint8_t a[STAGES][kABytes];
