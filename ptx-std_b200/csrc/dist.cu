@@ -228,25 +228,43 @@ int ptxstd_dist_decode_p2p_init(ptxstd_dist* d, int64_t N, uint16_t** d_y) {
         cudaFree(buf);
         return PTXSTD_ECUDA;
     }
-    // every rank's handle, gathered with one NCCL all-gather through a device staging buffer
+    // every rank's record {IPC handle, GPU UUID}, gathered with one NCCL all-gather through a
+    // device staging buffer
+    constexpr size_t kRec = 128;
+    uint8_t mine[kRec] = {};
+    memcpy(mine, &h, 64);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, d->device) != cudaSuccess) {
+        cudaFree(buf);
+        return PTXSTD_ECUDA;
+    }
+    static_assert(sizeof(prop.uuid) == 16, "UUID size");
+    memcpy(mine + 64, &prop.uuid, 16);
     uint8_t* stage = nullptr;
-    std::vector<uint8_t> all(64 * static_cast<size_t>(d->nranks));
+    std::vector<uint8_t> all(kRec * static_cast<size_t>(d->nranks));
     int st = PTXSTD_OK;
     if (cudaMalloc(&stage, all.size()) != cudaSuccess) st = PTXSTD_ECUDA;
-    if (!st && cudaMemcpy(stage + 64 * d->rank, &h, 64, cudaMemcpyHostToDevice) != cudaSuccess)
+    if (!st && cudaMemcpy(stage + kRec * d->rank, mine, kRec, cudaMemcpyHostToDevice) != cudaSuccess)
         st = PTXSTD_ECUDA;
-    if (!st && n.all_gather(stage + 64 * d->rank, stage, 64, ncclUint8, d->comm, 0) != ncclSuccess)
+    if (!st && n.all_gather(stage + kRec * d->rank, stage, kRec, ncclUint8, d->comm, 0) !=
+                   ncclSuccess)
         st = PTXSTD_ENCCL;
     if (!st && (cudaMemcpy(all.data(), stage, all.size(), cudaMemcpyDeviceToHost) != cudaSuccess))
         st = PTXSTD_ECUDA;
     if (stage) cudaFree(stage);
+    // The step's kernels wait on the other ranks' kernels, so every rank needs a GPU of its own:
+    // two ranks on one GPU are refused (every rank sees the same records and decides the same).
+    for (int a = 0; !st && a < d->nranks; ++a)
+        for (int b = a + 1; !st && b < d->nranks; ++b)
+            if (memcmp(all.data() + kRec * a + 64, all.data() + kRec * b + 64, 16) == 0)
+                st = PTXSTD_EUNSUPPORTED;
     for (int r = 0; !st && r < d->nranks; ++r) {
         if (r == d->rank) {
             d->p2p_peer[r] = buf;
             continue;
         }
         cudaIpcMemHandle_t hr;
-        memcpy(&hr, all.data() + 64 * r, 64);
+        memcpy(&hr, all.data() + kRec * r, 64);
         void* p = nullptr;
         if (cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
             st = PTXSTD_ECUDA;
