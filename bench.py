@@ -7,7 +7,8 @@ One JSON line on rank 0. A "step" is one pass of the hot path over one batch of 
 for ``mxfp8_quantize`` (the default, 8192 x 8192 bf16 -> E4M3 + UE8M0 per 32) one quantise
 launch. ``value`` is device-timed (CUDA events on the launching stream, max over ranks) with the
 inputs resident in HBM; ``e2e`` is the same metric through the public API with host buffers,
-including the host->device copy of the input and the device->host copy of the results.
+including every step's host->device copy of its inputs and device->host copy of its results,
+pipelined over two buffer slots (copies on their own streams, overlapping the compute).
 
 ``--impl reference`` times the reference's conversion semantics on the host cores instead (the
 C oracle: the reference crate itself cannot be built here, it targets nvptx64 only), on the same
