@@ -632,6 +632,9 @@ class DecodeGemm:
                        "M": self.M, "N": self.N, "K": self.K, "n_per_gpu": self.n_local,
                        "sharding": "W along N, output columns gathered to every rank",
                        "l2": "weights 252 MiB per step (> L2), 2 rotating weight copies"}
+        if world > 1:
+            # (g - 1) / g of the 1,835,008-byte output crosses NVLink into every rank per step
+            self.config["nvlink_bytes_in_per_rank"] = self.gather_bytes
 
     def host_input(self):
         return None
