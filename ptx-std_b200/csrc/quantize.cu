@@ -50,7 +50,9 @@ struct QCfg {
 // Default: 24 consumer warps x 2 vectors per lane = 24 KiB stages, 6 stages (144 KiB in flight
 // per SM). Best of a sweep on B200 at 8192 x 8192 (35.1 us vs 36.8 for 16x2x8, 35.9 for 16x4x4,
 // 45.4 for 8x4x8): with ~10 instructions per element the consumers need enough warps per
-// scheduler to hide latency, and the ring supplies the bytes in flight.
+// scheduler to hide latency, and the ring supplies the bytes in flight. A later sweep at the same
+// size (MXFP8, GB/s over five interleaved runs) kept it: 24x2x6 6061-6138, 16x4x4 6072-6092,
+// 28x2x6 5989-6022, 24x2x7 5906-5993, 24x4x3 5883-5922, 24x2x8 5814-5897.
 using DefaultCfg = QCfg<24, 2, 6>;
 
 enum : uint32_t { kDetailProducer = 0x2100, kDetailConsumer = 0x2200 };
