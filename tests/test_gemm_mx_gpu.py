@@ -90,8 +90,8 @@ def _gemm_check(torch, oracle, A, ta, sfA, B, tb, sfB, n_samples=2048, seed=0):
     assert bad.size == 0, [(int(rows[i]), int(cols[i]), got[i], ref[i]) for i in bad[:6]]
 
 
-PAIRS = [("e4m3", "e4m3"), ("e5m2", "e5m2"), ("e2m3", "e2m3"), ("e3m2", "e3m2"),
-         ("e2m1", "e2m1"), ("e4m3", "e2m1"), ("e2m3", "e5m2"), ("e2m1", "e3m2")]
+# every (A, B) pair of kind::mxf8f6f4 element types
+PAIRS = [(ta, tb) for ta in TYPES for tb in TYPES]
 
 
 @pytest.mark.parametrize("ta,tb", PAIRS)
