@@ -7,8 +7,9 @@ of element types).
     layouts, inputs with zero blocks, NaN / inf and heavy-tailed rows;
   - GEMM: against the oracle's f64 GEMM over the decoded payloads, with the MXFP8 tolerance
     |C - ref| <= 2^-10 * sum_k |a b| + 2^-8 |ref|. Random codes of every finite value check the
-    packing the tensor cores read (a misplaced bit changes the products); quantised operands
-    check the quantise -> GEMM chain, including mixed A / B types.
+    packing the tensor cores read (a misplaced bit changes the products), over all 25 (A, B)
+    type pairs; quantised operands check the quantise -> GEMM chain, mixed types included;
+  - the decompressing tcgen05.cp: every FP6 / FP4 code into its 8-bit container.
 """
 
 import numpy as np
