@@ -69,7 +69,11 @@ MX_TYPES = {"e4m3": MX_E4M3, "e5m2": MX_E5M2, "e2m3": MX_E2M3, "e3m2": MX_E3M2, 
 
 
 def _mx_type(t) -> int:
-    return MX_TYPES[t] if isinstance(t, str) else int(t)
+    """An MX element type by name or tcgen05 code; ValueError for anything else."""
+    code = MX_TYPES.get(t) if isinstance(t, str) else int(t)
+    if code not in MX_TYPES.values():
+        raise ValueError(f"unknown MX element type {t!r} (one of {sorted(MX_TYPES)})")
+    return code
 
 
 def quantize_mx(x, elem_type, sf_layout: int = 1, out=None, stream=None):
@@ -79,14 +83,15 @@ def quantize_mx(x, elem_type, sf_layout: int = 1, out=None, stream=None):
     torch = _torch()
     if x.dtype != torch.bfloat16 or x.dim() != 2:
         raise TypeError("expected a 2-D bfloat16 tensor")
+    t = _mx_type(elem_type)
     rows, cols = x.shape
     if out is None:
         q = torch.empty((rows, cols), dtype=torch.uint8, device=x.device)
         sf = torch.empty((rows, cols // 32), dtype=torch.uint8, device=x.device)
     else:
         q, sf = out
-    check(lib().ptxstd_quantize_mx(_dev(x), rows, cols, _mx_type(elem_type), _dev(q), _dev(sf),
-                                   sf_layout, _stream(stream)), "quantize_mx")
+    check(lib().ptxstd_quantize_mx(_dev(x), rows, cols, t, _dev(q), _dev(sf), sf_layout,
+                                   _stream(stream)), "quantize_mx")
     return q, sf
 
 
@@ -94,6 +99,7 @@ def gemm_mx(a, a_type, sfa, b, b_type, sfb, out=None, stream=None):
     """MX GEMM with any pair of element types: a [M, K], b [N, K] payloads in the operand layout
     of quantize_mx, blocked UE8M0 scales per 32 -> bf16 [M, N]."""
     torch = _torch()
+    ta, tb = _mx_type(a_type), _mx_type(b_type)
     M, K = a.shape
     N = b.shape[0]
     if b.shape[1] != K:
@@ -101,8 +107,8 @@ def gemm_mx(a, a_type, sfa, b, b_type, sfb, out=None, stream=None):
     if sfa.numel() != M * K // 32 or sfb.numel() != N * K // 32:
         raise ValueError("scale tensors must hold one UE8M0 per 32 elements")
     c = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
-    check(lib().ptxstd_gemm_mx(_dev(a), _mx_type(a_type), _dev(sfa), _dev(b), _mx_type(b_type),
-                               _dev(sfb), _dev(c), M, N, K, _stream(stream)), "gemm_mx")
+    check(lib().ptxstd_gemm_mx(_dev(a), ta, _dev(sfa), _dev(b), tb, _dev(sfb), _dev(c), M, N, K,
+                               _stream(stream)), "gemm_mx")
     return c
 
 
@@ -110,13 +116,15 @@ def tcgen05_cp_unpack(packed, elem_type, stream=None):
     """Packed FP6 / FP4 rows [n * 128, 32] (uint8, the quantize_mx layout) through the
     decompressing tcgen05.cp into TMEM and back: one 8-bit container per element, same shape."""
     torch = _torch()
+    t = _mx_type(elem_type)
+    if t not in (MX_E2M3, MX_E3M2, MX_E2M1):
+        raise ValueError("the decompressing copy takes FP6 (e2m3, e3m2) or FP4 (e2m1) payloads")
     if packed.dtype != torch.uint8 or packed.dim() != 2 or packed.shape[1] != 32 or \
             packed.shape[0] % 128:
         raise ValueError("expected uint8 [n * 128, 32]")
     out = torch.empty_like(packed)
-    check(lib().ptxstd_tcgen05_cp_unpack(_dev(packed), _dev(out), packed.shape[0] // 128,
-                                         _mx_type(elem_type), _stream(stream)),
-          "tcgen05_cp_unpack")
+    check(lib().ptxstd_tcgen05_cp_unpack(_dev(packed), _dev(out), packed.shape[0] // 128, t,
+                                         _stream(stream)), "tcgen05_cp_unpack")
     return out
 
 
