@@ -367,7 +367,8 @@ PTXSTD_API int ptxstd_gemm_decode_sharded(const ptxstd_dist* dist, const uint16_
  * library until ptxstd_dist_free, is returned in *d_y. A step (collective): rows 0..M-1 of that y
  * hold the full product when the stream reaches the end of the call; with d_y_copy non-null they
  * are also copied there. Steps of one communicator must be issued in the same order on every
- * rank. N % (128 * world) == 0; at most 8 ranks, each on a GPU of its own (the step's kernels
+ * rank, with the communicator's GPU current (else EINVAL). N % (128 * world) == 0; at most 8
+ * ranks, each on a GPU of its own (the step's kernels
  * wait on the other ranks' kernels; ranks that share a GPU get PTXSTD_EUNSUPPORTED from the
  * setup); workspace as ptxstd_gemm_decode_workspace_bytes(M, N / world, K). */
 PTXSTD_API int ptxstd_dist_decode_p2p_init(ptxstd_dist* dist, int64_t N, uint16_t** d_y);

@@ -212,6 +212,9 @@ int ptxstd_dist_decode_p2p_init(ptxstd_dist* d, int64_t N, uint16_t** d_y) {
         d->nranks > static_cast<int>(pd::kMaxRanks))
         return PTXSTD_EINVAL;
     if (d->p2p_local) return PTXSTD_EINVAL;  // once per communicator
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess) return PTXSTD_ECUDA;
+    if (cur != d->device) return PTXSTD_EINVAL;  // the communicator's GPU must be current
     Nccl& n = nccl();
     if (!n.ok) return PTXSTD_ENCCL;
     const size_t bytes = p2p_y_bytes(N) + pd::kSigWords * sizeof(uint32_t);
@@ -291,6 +294,9 @@ int ptxstd_gemm_decode_sharded_p2p(const ptxstd_dist* d, const uint16_t* d_x,
     namespace pd = ptxstd::decode;
     if (!d || !d->p2p_local || N != d->p2p_n || M <= 0 || M > kP2pRows || !d_workspace)
         return PTXSTD_EINVAL;
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess) return PTXSTD_ECUDA;
+    if (cur != d->device) return PTXSTD_EINVAL;  // the communicator's GPU must be current
     const int64_t ns = N / d->nranks;
     if (ns % 128 != 0) return PTXSTD_EINVAL;
     const size_t dec = ptxstd_gemm_decode_workspace_bytes(M, ns, K);
