@@ -609,3 +609,40 @@ def test_cp_unpack_container_rule(oracle):
     c4 = (np.arange(32) & 0xF).astype(np.uint8)[None, :]
     got = oracle.cp_unpack(oracle.E2M1, oracle.mx_pack(oracle.E2M1, c4))
     assert got.tobytes().hex() == "0004080c1014181c2024282c3034383c" * 2
+
+
+# (format, significand bits after the point, smallest normal exponent, largest finite value)
+_MX_FORMAT_GEOMETRY = [(0, 3, -6, 448.0), (1, 2, -14, 57344.0), (3, 3, 0, 7.5),
+                       (4, 2, -2, 28.0), (2, 1, 0, 6.0)]
+
+
+@pytest.mark.parametrize("fmt,mbits,emin,top", _MX_FORMAT_GEOMETRY)
+def test_quantize_mx_error_bound(oracle, fmt, mbits, emin, top):
+    """Independent float64 check of the MX recipe: each element, decoded and scaled by its block's
+    2^(sf - 127), is within half a unit in the last place (of the format, at the element's scaled
+    magnitude, subnormal quantum below the normal range) of the input; where the scaled input
+    exceeds the format's largest finite value, the element saturates to it."""
+    from ptxstd import workloads
+    x_bits = workloads.mxfp8_activation(64, 1024, seed=1234 + fmt)
+    x = (x_bits.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    q, sf = oracle.quantize_mx(x_bits, fmt)
+    codes = oracle.mx_unpack(fmt, q)
+    if fmt == oracle.E2M1:
+        dec = oracle.decode(fmt, (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8))
+    else:
+        dec = oracle.decode(fmt, codes)
+    dec = dec.reshape(x.shape).astype(np.float64)
+    scale = np.exp2(np.repeat(sf.astype(np.float64) - 127.0, 32, axis=1))
+    y = x / scale                               # the scaled input the element encodes
+    a = np.abs(y)
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** emin)))
+    half_ulp = np.exp2(e - mbits - 1)
+    sat = a > top
+    assert np.all(np.abs(dec[sat]) == top) and np.all(np.sign(dec[sat]) == np.sign(y[sat]))
+    ok = ~sat
+    assert np.all(np.abs(dec[ok] - y[ok]) <= half_ulp[ok]), fmt
+    # the recipe keeps every block's largest element at or above half the format's top binade
+    amax = np.abs(x).reshape(64, -1, 32).max(axis=2)
+    big = amax > 0
+    ratio = amax[big] / np.exp2(sf[big].astype(np.float64) - 127.0)
+    assert np.all(ratio >= 2.0 ** np.floor(np.log2(top)))
