@@ -646,3 +646,25 @@ def test_quantize_mx_error_bound(oracle, fmt, mbits, emin, top):
     big = amax > 0
     ratio = amax[big] / np.exp2(sf[big].astype(np.float64) - 127.0)
     assert np.all(ratio >= 2.0 ** np.floor(np.log2(top)))
+
+
+def test_gemm_mx_ref_matches_numpy(oracle):
+    """The MX GEMM reference (mixed E3M2 x E2M1 here) equals a float64 numpy product of the
+    unpacked, decoded and scaled operands at every output."""
+    rng = np.random.default_rng(17)
+    M, N, K = 8, 6, 128
+    ca = (rng.integers(0, 64, (M, K))).astype(np.uint8)
+    cb = (rng.integers(0, 16, (N, K))).astype(np.uint8)
+    sfa = rng.integers(120, 135, (M, K // 32), dtype=np.uint8)
+    sfb = rng.integers(120, 135, (N, K // 32), dtype=np.uint8)
+    A, B = oracle.mx_pack(oracle.E3M2, ca), oracle.mx_pack(oracle.E2M1, cb)
+    da = oracle.decode(oracle.E3M2, ca).reshape(M, K).astype(np.float64)
+    db = oracle.decode(oracle.E2M1, (cb[:, 0::2] | (cb[:, 1::2] << 4)).astype(np.uint8))
+    db = db.reshape(N, K).astype(np.float64)
+    da *= np.exp2(np.repeat(sfa.astype(np.float64) - 127, 32, axis=1))
+    db *= np.exp2(np.repeat(sfb.astype(np.float64) - 127, 32, axis=1))
+    want = da @ db.T
+    r, c = np.meshgrid(np.arange(M), np.arange(N), indexing="ij")
+    ref, mag = oracle.gemm_mx_ref(A, oracle.E3M2, sfa, B, oracle.E2M1, sfb, r.ravel(), c.ravel())
+    assert np.allclose(ref, want.ravel(), rtol=1e-12, atol=0)
+    assert np.allclose(mag, (np.abs(da) @ np.abs(db).T).ravel(), rtol=1e-12, atol=0)
