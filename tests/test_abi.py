@@ -91,3 +91,13 @@ def test_dist_validation_without_gpu(ptxstd_lib):
     assert L.ptxstd_dist_decode_p2p_init(None, 1024, C.byref(y)) == EINVAL
     assert L.ptxstd_gemm_decode_sharded_p2p(None, 16, 16, 16, 1.0, None, 16, 1024, 2048, 1024,
                                             1 << 20, None) == EINVAL
+
+
+def test_integration_binding_names_exist():
+    """Every function the Rust `extern "C"` block of INTEGRATION.md binds is declared in
+    include/ptxstd.h (the documented binding cannot drift from the header)."""
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    bound = set(re.findall(r"pub fn (ptxstd_\w+)\s*\(", doc))
+    assert bound, "no bindings found"
+    missing = bound - _declared()
+    assert not missing, sorted(missing)
