@@ -1,7 +1,7 @@
 """Benchmark of the narrow-float quantise / block-scaled GEMM path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload mxfp8_quantize|...]
+                    [--workload mxfp8_quantize|...] [--extra auto|none|w1,w2,...]
 
 One JSON line on rank 0. A "step" is one pass of the hot path over one batch of synthetic input:
 for ``mxfp8_quantize`` (the default, 8192 x 8192 bf16 -> E4M3 + UE8M0 per 32) one quantise
@@ -10,9 +10,16 @@ inputs resident in HBM; ``e2e`` is the same metric through the public API with h
 including every step's host->device copy of its inputs and device->host copy of its results,
 pipelined over two buffer slots (copies on their own streams, overlapping the compute).
 
+With the default headline the same line also carries a ``workloads`` object: one record per GEMM
+configuration (``fp8_gemm`` 8192^3, ``mxfp8_gemm`` 8192^3, ``nvfp4_gemm`` 8192 x 28672 x 8192
+sharded along N over the ranks, ``decode_gemm`` 16 x 57344 x 8192 sharded along N with the output
+gathered to every rank; on several ranks also ``decode_gemm_nccl``), each measured in this
+process with the same rules and carrying its own ``ms_per_step``, ``roofline``, ``clocks``,
+``e2e`` and, on one GPU, ``cpu_baseline``.
+
 ``--impl reference`` times the reference's conversion semantics on the host cores instead (the
 C oracle: the reference crate itself cannot be built here, it targets nvptx64 only), on the same
-workload, metric and unit.
+workloads, metric, unit and config.
 """
 
 from __future__ import annotations
@@ -524,7 +531,8 @@ class Mxfp8SparseGemm(Fp8Gemm):
 
 class Nvfp4Gemm:
     """NVFP4 MLP up-projection: A [8192, 8192] x B [28672, 8192] (E2M1 + E4M3/16 + f32 global)
-    -> bf16 [8192, 28672]; B is sharded along N across ranks (no communication)."""
+    -> bf16 [8192, 28672]; B is sharded along N across ranks (no communication). On several
+    ranks each step is ptxstd_gemm_nvfp4_sharded on this rank's 28672 / world columns."""
 
     name = "nvfp4_gemm"
     unit = "TFLOP/s"
@@ -547,6 +555,8 @@ class Nvfp4Gemm:
         self.config = {"workload": "nvfp4_gemm 8192x28672x8192 (MLP up-projection) -> bf16",
                        "M": self.M, "N": self.N, "K": self.K, "n_per_gpu": self.n_local,
                        "sharding": "B along N, no communication",
+                       "entry_point": "ptxstd_gemm_nvfp4_sharded" if world > 1
+                       else "ptxstd_gemm_nvfp4",
                        "l2": "operands 127 MiB + output 448 MiB per step (> L2)"}
 
     def host_input(self):
@@ -567,21 +577,26 @@ class Nvfp4Gemm:
         del xa, xb
         self.c = torch.empty((self.M, self.n_local), dtype=torch.bfloat16, device="cuda")
         self.host = [t.cpu().pin_memory() for t in (self.a, self.sfa, self.b, self.sfb)]
+        ctx = getattr(self, "ctx", None)
+        self.pd = ctx.ptxstd_dist() if ctx is not None and self.world > 1 else None
+
+    def _gemm(self, a, sfa, b, sfb, c):
+        import ptxstd
+        if self.pd is None:
+            ptxstd.gemm_nvfp4(a, sfa, self.ga, b, sfb, self.gb, out=c)
+        else:
+            self.pd.gemm_nvfp4(a, sfa, self.ga, b, sfb, self.gb, self.N, out=c)
+        return 1
 
     def step(self, i):
-        import ptxstd
-        ptxstd.gemm_nvfp4(self.a, self.sfa, self.ga, self.b, self.sfb, self.gb, out=self.c)
-        return 1
+        return self._gemm(self.a, self.sfa, self.b, self.sfb, self.c)
 
     def e2e_slots(self, torch):
         return _gemm_slots(torch, list(zip((self.a, self.sfa, self.b, self.sfb), self.host)),
                            self.c)
 
     def e2e_compute(self, i, args):
-        import ptxstd
-        a, sfa, b, sfb, c = args
-        ptxstd.gemm_nvfp4(a, sfa, self.ga, b, sfb, self.gb, out=c)
-        return 1
+        return self._gemm(*args)
 
     def value(self, seconds_per_step: float) -> float:
         return self.flops / seconds_per_step / 1e12
@@ -609,7 +624,9 @@ class DecodeGemm:
     """Decode step: x bf16 [16, 8192] (MXFP8 in the call) x NVFP4 W [57344, 8192] -> bf16
     [16, 57344]; W is sharded along N across ranks and every rank ends with all output columns:
     with `gather` "p2p" (default) the decode epilogue stores them into every rank's output over
-    NVLink peer memory, with "nccl" an NCCL all-gather follows the GEMM."""
+    NVLink peer memory, with "nccl" an NCCL all-gather follows the GEMM. On several ranks the
+    record also times the rank's GEMM alone (its own columns into a local output, no gather), so
+    that the gather's share of a step is reported apart from the GEMM's."""
 
     name = "decode_gemm"
     unit = "GB/s"
@@ -619,9 +636,9 @@ class DecodeGemm:
     scaling = "strong"
     parallelism = "n-shard"
 
-    def __init__(self, world: int = 1):
+    def __init__(self, world: int = 1, gather: str = "p2p"):
         self.world = world
-        self.gather = "p2p"
+        self.gather = gather
         self.n_local = self.N // world
         w_bytes = self.n_local * self.K // 2 + self.n_local * self.K // 16
         self.bytes = w_bytes + self.M * self.K * 2 + self.M * self.n_local * 2
@@ -635,6 +652,12 @@ class DecodeGemm:
         if world > 1:
             # (g - 1) / g of the 1,835,008-byte output crosses NVLink into every rank per step
             self.config["nvlink_bytes_in_per_rank"] = self.gather_bytes
+            self.config["sharding"] = (
+                "W along N; the decode epilogue stores each rank's columns into every rank's "
+                "output over NVLink (CUDA IPC peer memory), no collective" if gather == "p2p"
+                else "W along N, NCCL all-gather of output columns + device unshard permute")
+            self.config["entry_point"] = ("ptxstd_gemm_decode_sharded_p2p" if gather == "p2p"
+                                          else "ptxstd_gemm_decode_sharded")
 
     def host_input(self):
         return None
@@ -657,18 +680,16 @@ class DecodeGemm:
         self.x_host = self.x.cpu().pin_memory()
         # every rank ends the step with the full [16, N] output
         self.y = torch.empty((self.M, self.N), dtype=torch.bfloat16, device="cuda")
-        self.dist = None
-        if self.world > 1:
-            from ptxstd.dist import Dist
-            self.dist = Dist.from_torch()
-            self.config["sharding"] = (
-                "W along N; the decode epilogue stores each rank's columns into every rank's "
-                "output over NVLink (CUDA IPC peer memory), no collective" if self.gather == "p2p"
-                else "W along N, NCCL all-gather of output columns + device unshard permute")
+        self.y_local = None
+        ctx = getattr(self, "ctx", None)
+        self.dist = ctx.ptxstd_dist() if ctx is not None and self.world > 1 else None
+        if self.dist is not None:
+            self.y_local = torch.empty((self.M, self.n_local), dtype=torch.bfloat16,
+                                       device="cuda")
             if self.gather == "p2p":
                 self.y = self.dist.decode_p2p_output(self.N)
 
-    def _decode(self, i):
+    def step(self, i):
         import ptxstd
         w, sfw, gw = self.sets[i % 2]
         if self.dist is None:
@@ -682,13 +703,17 @@ class DecodeGemm:
         self.dist.gemm_decode(self.x, w, sfw, gw, self.N, out=self.y)
         return 3
 
-    def step(self, i):
-        return self._decode(i)
+    def gemm_only_step(self):
+        """The rank's GEMM over its own columns, with no gather (several ranks only)."""
+        if self.dist is None:
+            return None
 
-    def teardown(self):
-        if self.dist is not None:
-            self.dist.close()
-            self.dist = None
+        def run(i):
+            import ptxstd
+            w, sfw, gw = self.sets[i % 2]
+            ptxstd.gemm_decode(self.x, w, sfw, gw, out=self.y_local)
+            return 2
+        return run
 
     def e2e_slots(self, torch):
         # the fused multi-GPU decode writes a library-owned y that the next step overwrites, so
@@ -736,6 +761,18 @@ class DecodeGemm:
         return wbytes / el / 1e9, "16x8192x8192 block, f32 blocked GEMM on decoded weights"
 
 
+class DecodeGemmNccl(DecodeGemm):
+    """The decode step with the NCCL all-gather of output columns in place of the fused
+    peer-store gather (the same as decode_gemm on one GPU)."""
+
+    name = "decode_gemm_nccl"
+
+    def __init__(self, world: int = 1):
+        super().__init__(world, gather="nccl")
+        self.config = dict(self.config, workload="decode_gemm_nccl x[16,8192] bf16 -> mxfp8, "
+                           "W nvfp4 [57344,8192], NCCL all-gather")
+
+
 class MxFp8QuantizeSR(MxFp8Quantize):
     """The same MXFP8 quantise with stochastic rounding of the elements (cvt.rs, random bits from
     SplitMix64 of a per-step seed, generated on the device)."""
@@ -776,43 +813,89 @@ class MxFp8QuantizeSR(MxFp8Quantize):
 
 
 WORKLOADS = {"mxfp8_quantize": MxFp8Quantize, "fp8_gemm": Fp8Gemm, "nvfp4_gemm": Nvfp4Gemm,
-             "decode_gemm": DecodeGemm, "mxfp8_gemm": Mxfp8Gemm,
+             "decode_gemm": DecodeGemm, "decode_gemm_nccl": DecodeGemmNccl,
+             "mxfp8_gemm": Mxfp8Gemm,
              "mxfp8_quantize_sr": MxFp8QuantizeSR, "mxfp8_gemm_sparse": Mxfp8SparseGemm,
              "mxfp6_gemm": MxFp6Gemm}
 
 
 # ---- arms -----------------------------------------------------------------------------------
 
-def run_ours(args, wl) -> dict | None:
+# Workloads measured in the same process after the headline one, each as its own record of the
+# line's "workloads" object: the GEMM configurations (E4M3 8192^3, MXFP8 8192^3, NVFP4
+# 8192 x 28672 x 8192 N-sharded, decode 16 x 57344 x 8192 N-sharded). On several ranks the decode
+# is measured with both gathers: the fused peer-store one and the NCCL all-gather.
+EXTRA_DEFAULT = ["fp8_gemm", "mxfp8_gemm", "nvfp4_gemm", "decode_gemm"]
+EXTRA_MULTI = ["decode_gemm_nccl"]
+
+
+def extra_workloads(args, world: int) -> list[str]:
+    if args.extra == "none":
+        return []
+    if args.extra != "auto":
+        return [w for w in args.extra.split(",") if w]
+    if args.workload != "mxfp8_quantize":
+        return []
+    return EXTRA_DEFAULT + (EXTRA_MULTI if world > 1 else [])
+
+
+class Ctx:
+    """Run state shared by the workloads of one process: torch.distributed plumbing and the
+    libptxstd communicator (created on first use; every rank creates it at the same point)."""
+
+    def __init__(self, n_gpus: int):
+        self.dist = Dist(n_gpus)
+        self._pd = None
+
+    def ptxstd_dist(self):
+        if self._pd is None and self.dist.world > 1:
+            from ptxstd.dist import Dist as PtxDist
+            self._pd = PtxDist.from_torch()
+        return self._pd
+
+    def close(self):
+        if self._pd is not None:
+            import torch
+            torch.cuda.synchronize()
+            self._pd.close()
+            self._pd = None
+        self.dist.close()
+
+
+def uses_graph(args, wl, world: int) -> bool:
+    return not args.no_graph and not (world > 1 and getattr(wl, "collective", False))
+
+
+def line_config(wl, world: int, graph: bool) -> dict:
+    """The config dict of a record; both arms emit exactly this dict for the same workload."""
+    return dict(wl.config, parallelism=getattr(wl, "parallelism", "replicas") + str(world),
+                launch=("cuda-graph replay of the K steps, after one untimed replay that "
+                        "uploads the graph") if graph else "eager")
+
+
+def time_steps(args, ctx, step, graph: bool):
+    """W warm-up steps, then K steps bracketed by a barrier and a synchronize on both sides,
+    timed with CUDA events on the launching stream. With `graph` the K steps are captured once
+    into a CUDA graph and replayed (after one untimed replay that uploads it), so that the device
+    time is not padded by host-side launch gaps between short kernels; the multi-GPU decode's
+    NCCL all-gather is issued by libptxstd on the same stream and is captured with it.
+    Returns (device ms of the K steps, max over ranks; kernel launches; clock record)."""
     import torch
-    dist = Dist(args.gpus)
-    torch.manual_seed(0)
-    wl.setup(torch, wl.host_input())
+    dist = ctx.dist
     stream = torch.cuda.current_stream()
-
     for i in range(args.warmup):
-        wl.step(i)
+        step(i)
     torch.cuda.synchronize()
-
-    # The K timed steps are captured once into a CUDA graph and replayed, so that the device
-    # time is not padded by host-side launch gaps between short kernels. The multi-GPU decode's
-    # NCCL all-gather is issued by libptxstd on the same stream and is captured with it; a
-    # workload marked `collective` (a torch.distributed call in its step) would run eagerly.
-    use_graph = not args.no_graph and not (dist.world > 1 and getattr(wl, "collective", False))
-    graph = None
+    g = None
     launches = 0
-    if use_graph:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
             for i in range(args.steps):
-                launches += wl.step(i)
+                launches += step(i)
         torch.cuda.synchronize()
-        # One untimed replay (K more warm-up steps): the first launch of a captured graph also
-        # uploads it to the device, a one-time cost that is not part of a step.
-        graph.replay()
+        g.replay()
         torch.cuda.synchronize()
-
-    # device-timed region: K steps, inputs resident in HBM
     sampler = ClockSampler(torch.cuda.current_device()) if dist.rank == 0 else None
     if sampler:
         sampler.start()
@@ -821,28 +904,34 @@ def run_ours(args, wl) -> dict | None:
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    if graph is not None:
-        graph.replay()
+    if g is not None:
+        g.replay()
     else:
         for i in range(args.steps):
-            launches += wl.step(i)
+            launches += step(i)
     ev1.record(stream)
     torch.cuda.synchronize()
     dist.barrier()
     ms = ev0.elapsed_time(ev1)
     clocks = sampler.stop() if sampler else None
-    if graph is not None:
-        del graph
+    if g is not None:
+        del g  # a graph holding NCCL calls is released before the process group goes
+    return dist.max(ms), launches, clocks
 
-    # End to end through the public API with host buffers: every step copies its inputs from
-    # pinned host memory and its results back. Two buffer slots are used in turn, with the copies
-    # on their own streams, so that step i+1's H2D and step i's D2H overlap step i's compute
-    # (PCIe carries both directions at once); events keep a slot's buffers from being reused
-    # before its previous step has finished with them.
+
+def time_e2e(args, ctx, wl) -> float:
+    """End to end through the public API with host buffers: every step copies its inputs from
+    pinned host memory and its results back. Two buffer slots are used in turn, with the copies
+    on their own streams, so that step i+1's H2D and step i's D2H overlap step i's compute
+    (PCIe carries both directions at once); events keep a slot's buffers from being reused before
+    its previous step has finished with them. Returns ms of the K steps, max over ranks."""
+    import torch
+    dist = ctx.dist
+    stream = torch.cuda.current_stream()
     slots = wl.e2e_slots(torch)
     h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
 
-    def run_e2e(n):
+    def run(n):
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev_in = [torch.cuda.Event() for _ in range(n)]
         ev_run = [torch.cuda.Event() for _ in range(n)]
@@ -873,91 +962,160 @@ def run_ours(args, wl) -> dict | None:
         torch.cuda.synchronize()
         return start.elapsed_time(end)
 
-    run_e2e(3)
+    run(3)
     dist.barrier()
-    e2e_ms = run_e2e(args.steps)
+    ms = run(args.steps)
     dist.barrier()
+    del slots
+    return dist.max(ms)
 
-    ms_max = dist.max(ms)
-    e2e_max = dist.max(e2e_ms)
-    if hasattr(wl, "teardown"):
-        torch.cuda.synchronize()
-        wl.teardown()
-    rank = dist.rank
-    world = dist.world
-    dist.close()
-    if rank != 0:
-        return None
 
-    per_step_s = ms_max / 1e3 / args.steps
-    value = wl.value(per_step_s) * world
+def roofline(wl, per_launch_s: float) -> dict:
     peaks = measured_peaks()
-    per_launch_s = per_step_s  # one launch per step
     traffic = profiled_traffic(wl.kernel)
     if getattr(wl, "bound", "hbm") == "tensor":
-        # Dense FP8 runs at twice the bf16 rate on B200 (4.5 vs 2.25 PFLOP/s nominal); the
-        # denominator is the measured cuBLAS bf16 burst figure times that ratio.
+        # Dense FP8 runs at twice the bf16 rate on B200 (4.5 vs 2.25 PFLOP/s nominal), FP4 at
+        # four times; the denominator is the measured cuBLAS bf16 burst figure times that ratio.
         peak = peaks["bf16_tflops"] * wl.peak_ratio_to_bf16
         achieved = wl.flops / per_launch_s / 1e12
-        roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
-                    "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                    "peak_source": f"{peaks['source']} bf16_tflops (cuBLAS burst) x "
-                                   f"{wl.peak_ratio_to_bf16} ({wl.peak_note})",
-                    "algorithmic_flops_per_launch": wl.flops}
-    else:
-        achieved = wl.bytes / per_launch_s / 1e9
-        roofline = {"bound": "hbm", "achieved": round(achieved, 1),
-                    "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                    "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
-                    "peak_source": peaks["source"] + " hbm_gbs (burst copy)",
-                    "algorithmic_bytes_per_launch": wl.bytes}
-    out = {
-        "metric": METRIC, "value": round(value, 2), "unit": wl.unit, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
-        "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"), "vs_baseline": None,
-        "dtype": wl.dtype, "data": "synthetic (seeded)",
-        "config": dict(wl.config, parallelism=getattr(wl, "parallelism", "replicas") + str(world),
-                       launch=("cuda-graph replay of the K steps, after one untimed replay that "
-                               "uploads the graph") if use_graph else "eager"),
-        "roofline": roofline,
-        "e2e": {"value": round(wl.value(e2e_max / 1e3 / args.steps) * world, 2),
+        return {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_source": f"{peaks['source']} bf16_tflops (cuBLAS burst) x "
+                               f"{wl.peak_ratio_to_bf16} ({wl.peak_note})",
+                "algorithmic_flops_per_launch": wl.flops}
+    achieved = wl.bytes / per_launch_s / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+            "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+            "peak_source": peaks["source"] + " hbm_gbs (burst copy)",
+            "algorithmic_bytes_per_launch": wl.bytes}
+
+
+def measure(args, ctx, wl, cpu_budget_s: float = 3.0) -> dict | None:
+    """One workload, set up, device-timed, clock-sampled, timed end to end and (one GPU only)
+    timed on the host cores; returns its record on rank 0, None on the other ranks."""
+    import torch
+    world = ctx.dist.world
+    wl.ctx = ctx
+    torch.manual_seed(0)
+    wl.setup(torch, wl.host_input())
+    graph = uses_graph(args, wl, world)
+    ms, launches, clocks = time_steps(args, ctx, wl.step, graph)
+    split = None
+    only = wl.gemm_only_step() if hasattr(wl, "gemm_only_step") else None
+    if only is not None:
+        ms_gemm, _, _ = time_steps(args, ctx, only, graph)
+        split = {"gemm_us_per_step": round(ms_gemm * 1e3 / args.steps, 2),
+                 "gather_us_per_step": round((ms - ms_gemm) * 1e3 / args.steps, 2),
+                 "how": "the same K steps timed again with each rank's GEMM writing only its own "
+                        "columns (no gather); gather = step - that"}
+    e2e_ms = time_e2e(args, ctx, wl)
+    if ctx.dist.rank != 0:
+        return None
+    per_step_s = ms / 1e3 / args.steps
+    rec = {
+        "value": round(wl.value(per_step_s) * world, 2), "unit": wl.unit,
+        "ms_per_step": round(ms / args.steps, 5), "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"),
+        "dtype": wl.dtype, "config": line_config(wl, world, graph),
+        "roofline": roofline(wl, per_step_s),
+        "e2e": {"value": round(wl.value(e2e_ms / 1e3 / args.steps) * world, 2),
                 "unit": wl.unit, "h2d_bytes_per_step": wl.in_bytes,
                 "d2h_bytes_per_step": wl.out_bytes},
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if split is not None:
+        rec["split"] = split
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        v, sample = wl.cpu_sample(threads, budget_s=3.0)
-        out["cpu_baseline"] = {"value": round(v, 3), "unit": wl.unit, "cores": threads,
+        v, sample = wl.cpu_sample(threads, budget_s=cpu_budget_s)
+        rec["cpu_baseline"] = {"value": round(v, 3), "unit": wl.unit, "cores": threads,
                                "kind": "port", "sample": sample}
+    return rec
+
+
+def _release(wl):
+    import torch
+    if hasattr(wl, "teardown"):
+        torch.cuda.synchronize()
+        wl.teardown()
+    wl.__dict__.clear()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+
+def run_ours(args, wl) -> dict | None:
+    ctx = Ctx(args.gpus)
+    world = ctx.dist.world
+    head = measure(args, ctx, wl)
+    _release(wl)
+    extras = {}
+    for name in extra_workloads(args, world):
+        sub = WORKLOADS[name](world)
+        rec = measure(args, ctx, sub, cpu_budget_s=1.0)
+        _release(sub)
+        if rec is not None:
+            extras[name] = rec
+    rank = ctx.dist.rank
+    ctx.close()
+    if rank != 0:
+        return None
+    out = {"metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+           "higher_is_better": True, "scaling": head["scaling"], "vs_baseline": None,
+           "dtype": head["dtype"], "data": "synthetic (seeded)", "config": head["config"],
+           "roofline": head["roofline"], "e2e": head["e2e"],
+           "gpu_launches": head["gpu_launches"], "clocks": head["clocks"]}
+    if "cpu_baseline" in head:
+        out["cpu_baseline"] = head["cpu_baseline"]
+    if extras:
+        out["workloads"] = extras
     return out
+
+
+def reference_record(args, wl, world: int, samples: int, warmup: int) -> tuple[dict, float]:
+    threads = os.cpu_count() or 1
+    for _ in range(warmup):
+        wl.cpu_sample(threads, budget_s=0.0)
+    vals, sample = [], ""
+    for _ in range(samples):
+        v, sample = wl.cpu_sample(threads, budget_s=0.0)
+        vals.append(v)
+    v = statistics.median(vals)
+    what = ("the C restatement of the reference's conversion semantics (oracle/)"
+            if wl.unit == "GB/s" and not hasattr(wl, "gather") else
+            "a blocked f32 GEMM (oracle/) over operands decoded by the C restatement of the "
+            "reference's conversions")
+    rec = {"value": round(v, 3), "unit": wl.unit, "steps": samples, "warmup": warmup,
+           "higher_is_better": True, "dtype": wl.dtype,
+           "config": line_config(wl, world, uses_graph(args, wl, world)),
+           "cpu_baseline": {"value": round(v, 3), "unit": wl.unit, "cores": threads,
+                            "kind": "port",
+                            "sample": f"per step: {sample}; {what}, all host threads"},
+           "e2e": {"value": round(v, 3), "unit": wl.unit, "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    return rec, v
 
 
 def run_reference(args, wl) -> dict | None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
-    threads = os.cpu_count() or 1
-    vals = []
-    sample = ""
-    for _ in range(args.warmup):
-        wl.cpu_sample(threads, budget_s=0.0)
-    for _ in range(args.steps):
-        v, sample = wl.cpu_sample(threads, budget_s=0.0)
-        vals.append(v)
-    v = statistics.median(vals)
-    return {"metric": METRIC, "value": round(v, 3), "unit": wl.unit, "impl": "reference",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "dtype": wl.dtype, "data": "synthetic (seeded numpy)",
-            "config": wl.config,
-            "cpu_baseline": {"value": round(v, 3), "unit": wl.unit, "cores": threads,
-                             "kind": "port",
-                             "sample": f"per step: {sample}; the C restatement of the "
-                                       "reference's conversion semantics (oracle/), all host "
-                                       "threads"},
-            "e2e": {"value": round(v, 3), "unit": wl.unit, "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    head, _ = reference_record(args, wl, world, args.steps, args.warmup)
+    out = {"metric": METRIC, "value": head["value"], "unit": wl.unit, "impl": "reference",
+           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+           "higher_is_better": True, "dtype": wl.dtype, "data": "synthetic (seeded numpy)",
+           "config": head["config"], "cpu_baseline": head["cpu_baseline"], "e2e": head["e2e"]}
+    extras = {}
+    for name in extra_workloads(args, world):
+        # a bounded sample per workload (one warm-up and up to 3 timed samples of a row block of
+        # the GEMM) keeps the arm within minutes
+        extras[name], _ = reference_record(args, WORKLOADS[name](world), world,
+                                           min(args.steps, 3), 1)
+    if extras:
+        out["workloads"] = extras
+    return out
 
 
 def main() -> int:
@@ -967,6 +1125,10 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mxfp8_quantize")
+    ap.add_argument("--extra", default="auto",
+                    help="comma-separated workloads measured after the headline one, each as a "
+                         "record of the line's 'workloads' object; 'auto' (default) = the GEMM "
+                         "configurations when the headline is mxfp8_quantize; 'none'")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the timed steps eagerly instead of replaying a CUDA graph")
@@ -976,9 +1138,10 @@ def main() -> int:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    wl = WORKLOADS[args.workload](int(os.environ.get("WORLD_SIZE", "1")))
-    if hasattr(wl, "gather"):
-        wl.gather = args.gather
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    wl = WORKLOADS[args.workload](world)
+    if args.workload == "decode_gemm" and args.gather == "nccl":
+        wl = DecodeGemmNccl(world)
     res = run_reference(args, wl) if args.impl == "reference" else run_ours(args, wl)
     if res is not None:
         print(json.dumps(res), flush=True)

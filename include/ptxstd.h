@@ -322,12 +322,17 @@ PTXSTD_API int ptxstd_gemm_decode(const uint16_t* d_x, const uint8_t* d_w, const
  * synchronise the device and fragment a sized pool, so they are not allowed per request), or a
  * thin C / Rust binding that owns only its input and output buffers and has no allocator of its
  * own for a workspace. Its scratch is a file-scope device array of
- * PTXSTD_DECODE_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until the process
- * exits; shapes whose scratch (ptxstd_gemm_decode_workspace_bytes) would exceed it are rejected
- * with PTXSTD_EINVAL (the 16 x 57344 x 8192 decode shape fits). The first call on a device looks up
- * the array's device address for that device; make that first call before any stream capture.
- * All calls on a device share the array (each call clears what must start at zero); calls that
- * overlap on the GPU, e.g. on two streams, race on it and must be serialised by the caller. */
+ * PTXSTD_DECODE_NOALLOC_SCRATCH_BYTES (1024-byte aligned); shapes whose scratch
+ * (ptxstd_gemm_decode_workspace_bytes) would exceed it are rejected with PTXSTD_EINVAL (the
+ * 16 x 57344 x 8192 decode shape fits). A device reserves the array when the decode code is first
+ * used on it (the CUDA runtime loads device code lazily by default), i.e. at the first call of
+ * this entry point or of ptxstd_gemm_decode there, and holds it until the process exits; the
+ * regular ptxstd_gemm_decode therefore carries the same 4 MiB. The first call on a device also
+ * looks up the array's device address for that device. So make one warm-up call per device at
+ * start-up, before serving and before any stream capture. The address is kept for the life of
+ * the process: calls across a device reset (cudaDeviceReset) are not supported. All calls on a
+ * device share the array (each call clears what must start at zero); calls that overlap on the
+ * GPU, e.g. on two streams, race on it and must be serialised by the caller. */
 PTXSTD_API int ptxstd_gemm_decode_noalloc(const uint16_t* d_x, const uint8_t* d_w,
                                           const uint8_t* d_sfw, float gw, uint16_t* d_y,
                                           int64_t M, int64_t N, int64_t K, ptxstd_stream stream);

@@ -797,16 +797,22 @@ int ptxstd_gemm_decode(const uint16_t* d_x, const uint8_t* d_w, const uint8_t* d
 // whose device-memory plan is fixed at start-up must not call cudaMalloc / cudaFree per request
 // (both can synchronise the device and fragment a carefully sized pool), and a thin C or Rust
 // binding may own only the input and output buffers, with no allocator of its own to create a
-// workspace. For them the scratch lives in this file-scope device array instead. Every GPU that
-// loads the library reserves it until the process exits.
+// workspace. For them the scratch lives in this file-scope device array instead. The array
+// belongs to this file's device module, which the CUDA runtime loads onto a device (lazily, by
+// default) at the first use of the module there: the first call of either decode entry point on
+// that device. From then until the process exits that device holds the 4 MiB, for the regular
+// ptxstd_gemm_decode as much as for this one. A caller that must not reserve memory while serving
+// makes one warm-up call per device at start-up, which also does the address look-up below.
 //
 // In host code `g_decode_scratch` is only a host-side stand-in for the symbol, not a device
 // address; its device address is fetched with cudaGetSymbolAddress, once per device, with that
-// device current, on the first call on that device. That first call should come before any
-// stream capture. All calls on a device share the one array: decode_prep clears the parts that
-// must start at zero on every call, and calls that overlap on the GPU (e.g. on two streams) race
-// on it.
-static __device__ __align__(256) uint8_t g_decode_scratch[PTXSTD_DECODE_NOALLOC_SCRATCH_BYTES];
+// device current, on the first call on that device, and kept for the life of the process. That
+// first call should come before any stream capture. A device reset (cudaDeviceReset) or a new
+// primary context invalidates the kept address; the library does not support calls across one.
+// All calls on a device share the one array: decode_prep clears the parts that must start at
+// zero on every call, and calls that overlap on the GPU (e.g. on two streams) race on it. The
+// array is 1024-byte aligned, the alignment ptxstd_gemm_decode asks of a caller's workspace.
+static __device__ __align__(1024) uint8_t g_decode_scratch[PTXSTD_DECODE_NOALLOC_SCRATCH_BYTES];
 
 namespace {
 

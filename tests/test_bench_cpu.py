@@ -24,7 +24,8 @@ def _run(args, env=None):
 
 @pytest.mark.parametrize("workload", ["mxfp8_quantize", "decode_gemm"])
 def test_reference_arm_line(workload):
-    lines = _run(["--impl", "reference", "--steps", "1", "--warmup", "3", "--workload", workload])
+    lines = _run(["--impl", "reference", "--steps", "1", "--warmup", "3", "--workload", workload,
+                  "--extra", "none"])
     assert len(lines) == 1
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["n_gpus"] == 1 and d["steps"] == 1
@@ -36,6 +37,46 @@ def test_reference_arm_line(workload):
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
     assert d["config"]["workload"].startswith(workload)
+
+
+def test_reference_arm_workload_records():
+    """The reference arm carries a record per extra workload, with the config dict the GPU arm
+    emits for it (same function, same keys: parallelism and launch included)."""
+    sys.path.insert(0, ROOT)
+    import bench
+    lines = _run(["--impl", "reference", "--steps", "1", "--warmup", "3",
+                  "--extra", "fp8_gemm,decode_gemm"])
+    d = json.loads(lines[0])
+    assert set(d["workloads"]) == {"fp8_gemm", "decode_gemm"}
+    for name, rec in d["workloads"].items():
+        wl = bench.WORKLOADS[name](1)
+        assert rec["config"] == bench.line_config(wl, 1, True), name
+        assert rec["value"] > 0 and rec["unit"] == wl.unit
+        assert rec["cpu_baseline"]["value"] == rec["value"]
+        assert rec["e2e"]["h2d_bytes_per_step"] == 0
+    head = bench.WORKLOADS["mxfp8_quantize"](1)
+    assert d["config"] == bench.line_config(head, 1, True)
+
+
+def test_extra_workload_selection():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    class A:
+        extra, workload = "auto", "mxfp8_quantize"
+    assert bench.extra_workloads(A, 1) == ["fp8_gemm", "mxfp8_gemm", "nvfp4_gemm",
+                                           "decode_gemm"]
+    assert bench.extra_workloads(A, 4)[-1] == "decode_gemm_nccl"
+    A.workload = "nvfp4_gemm"
+    assert bench.extra_workloads(A, 1) == []
+    A.extra = "none"
+    assert bench.extra_workloads(A, 1) == []
+    # the multi-rank records name the entry points they run
+    assert bench.WORKLOADS["nvfp4_gemm"](4).config["entry_point"] == "ptxstd_gemm_nvfp4_sharded"
+    assert bench.WORKLOADS["decode_gemm"](2).config["entry_point"] == \
+        "ptxstd_gemm_decode_sharded_p2p"
+    assert bench.WORKLOADS["decode_gemm_nccl"](2).config["entry_point"] == \
+        "ptxstd_gemm_decode_sharded"
 
 
 def test_reference_arm_other_ranks_print_nothing():

@@ -1,10 +1,15 @@
 """Decode-shape GEMM (x bf16 -> MXFP8 in the call; NVFP4 weights) vs the oracle (B200).
 
 The oracle quantises x with the MXFP8 recipe and takes an f64 dot product over the decoded
-operands; tolerance per output: |y - ref| <= 2^-10 * sum_k |x w| + 2^-8 * |ref| (the second term:
-bf16 rounding of the output). Covers M = 1, 5, 16 tokens, single and multiple 128-row weight
-blocks, stage counts that split unevenly across CTAs, two calls in a row on one workspace, and
-the N = 57344, K = 8192 decode workload at sampled outputs plus whole rows.
+operands. The N = 57344, K = 8192 decode workload (N(0, 1) activations, N(0, 0.02) weights) is
+held to the plain accumulation bound |y - ref| <= 2^-10 * sum_k |x w| at sampled outputs plus
+whole rows: with random signs and K = 8192, |ref| is a small fraction of sum |x w|, so the bound
+also covers the bf16 rounding of the output. The small shapes (K down to 256, and rows scaled by
+up to 2^8 with a x100 outlier) add the bf16 rounding, 2^-8 * |ref| (half an ulp, relative): at
+small K, or with one outlier product, |ref| can come close to sum |x w|, and the rounding of a
+correct result alone can then exceed the plain bound. Covers M = 1, 5, 16 tokens, single and
+multiple 128-row weight blocks, stage counts that split unevenly across CTAs, and two calls in a
+row on one workspace.
 """
 
 import numpy as np
@@ -49,13 +54,18 @@ def _run(torch, x, W, sfW, gw, calls=1):
     return [y.float().cpu().numpy() for y in ys]
 
 
-def _check(oracle, x, W, sfW, gw, yg, rows, cols):
+def _check(oracle, x, W, sfW, gw, yg, rows, cols, plain=False):
+    """Checks the sampled outputs; plain=True drops the output-rounding term. Prints and returns
+    the largest err / (2^-10 * sum |x w|)."""
     ref, mag = oracle.gemm_decode_ref(x, W, sfW, gw, rows, cols)
     got = yg[rows, cols].astype(np.float64)
     err = np.abs(got - ref)
-    tol = TOL_ACC * mag + TOL_OUT * np.abs(ref)
+    tol = TOL_ACC * mag + (0.0 if plain else TOL_OUT * np.abs(ref))
     bad = np.nonzero(err > tol)[0]
     assert bad.size == 0, [(int(rows[i]), int(cols[i]), got[i], ref[i], mag[i]) for i in bad[:8]]
+    ratio = float((err / np.maximum(TOL_ACC * mag, 1e-300)).max())
+    print(f"max err / (2^-10 sum|xw|) = {ratio:.4f} over {rows.size} outputs")
+    return ratio
 
 
 @pytest.mark.parametrize("M,N,K", [(16, 128, 256), (16, 256, 512), (5, 384, 1024),
@@ -91,7 +101,7 @@ def test_decode_workload_sampled(cuda, oracle):
     rng = np.random.default_rng(9)
     rows = np.concatenate([rng.integers(0, M, 4096), np.full(N, 0), np.full(N, 15)])
     cols = np.concatenate([rng.integers(0, N, 4096), np.arange(N), np.arange(N)])
-    _check(oracle, x, W, sfW, gw, y, rows, cols)
+    _check(oracle, x, W, sfW, gw, y, rows, cols, plain=True)
 
 
 def test_rejects_bad_shapes(cuda):

@@ -1,10 +1,13 @@
 """FP8 E4M3 GEMM (tcgen05.mma.kind::f8f6f4) vs the oracle's f64 GEMM over decoded values (B200).
 
-Tolerance, per output: |C - ref| <= 2^-10 * sa*sb*sum_k |a_ik b_jk|  +  2^-8 * |ref|.
-The first term is the stated accumulation bound; the second is the bf16 rounding of the output
-(half an ulp of bf16 is at most 2^-8 relative), which the stated bound does not include.
-Small shapes are checked at every output; the 8192^3 workload at 4096 random outputs plus two
-full rows and two full columns.
+The 8192^3 workload (random signs) is held to the plain accumulation bound, per output
+  |C - ref| <= 2^-10 * sa*sb*sum_k |a_ik b_jk|,
+at 4096 random outputs plus two full rows and two full columns; with random signs at K = 8192,
+|ref| stays a small fraction of sum |a b| (under 0.18 in a 512 x 512 numpy trial of these
+operands), so the bound also covers the bf16 rounding of the output. Small shapes (K down to 128)
+are checked at every output with the bf16 rounding added, 2^-8 * |ref| (half an ulp of bf16,
+relative): there a few large products can make |ref| close to sum |a b|, and the rounding of a
+correct result alone can then exceed the plain bound.
 """
 
 import numpy as np
@@ -27,14 +30,18 @@ def _run(torch, A, B, sa, sb):
     return c.float().cpu().numpy()
 
 
-def _check(oracle, A, B, sa, sb, Cg, rows, cols):
+def _check(oracle, A, B, sa, sb, Cg, rows, cols, plain=False):
+    """Checks the sampled outputs; plain=True drops the output-rounding term. Prints and returns
+    the largest err / (2^-10 * sum |a b|)."""
     ref, mag = oracle.gemm_fp8_ref(A, B, sa, sb, rows, cols)
     got = Cg[rows, cols].astype(np.float64)
     err = np.abs(got - ref)
-    tol = TOL_ACC * mag + TOL_OUT * np.abs(ref)
+    tol = TOL_ACC * mag + (0.0 if plain else TOL_OUT * np.abs(ref))
     bad = np.nonzero(err > tol)[0]
     assert bad.size == 0, [(int(rows[i]), int(cols[i]), got[i], ref[i], mag[i]) for i in bad[:8]]
-    return float((err / np.maximum(mag, 1e-30)).max())
+    ratio = float((err / np.maximum(TOL_ACC * mag, 1e-300)).max())
+    print(f"max err / (2^-10 sum|ab|) = {ratio:.4f} over {rows.size} outputs")
+    return ratio
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 128), (128, 256, 1024), (256, 512, 256),
@@ -71,7 +78,7 @@ def test_full_size_sampled(cuda, oracle):
                            np.arange(M), np.arange(M)])
     cols = np.concatenate([rng.integers(0, N, 4096), np.arange(N), np.arange(N),
                            np.full(M, 0), np.full(M, N - 129)])
-    _check(oracle, A, B, 0.75, 1.25, Cg, rows, cols)
+    _check(oracle, A, B, 0.75, 1.25, Cg, rows, cols, plain=True)
 
 
 def test_rejects_bad_shapes(cuda):

@@ -3,7 +3,12 @@
 Operands are E4M3 codes with UE8M0 scales per 32 K elements; the scales are rearranged into the
 blocked 128x4 layout in numpy (or come straight from ptxstd.quantize_mxfp8 with sf_layout 1), and
 the device result is compared with the oracle's f64 GEMM over the decoded values:
-  |C - ref| <= 2^-10 * sum_k |a b|  +  2^-8 * |ref|   (the second term: bf16 output rounding).
+  |C - ref| <= 2^-10 * sum_k |a b|  +  half an ulp of bf16 at C,
+i.e. the f32 accumulator is within the accumulation bound and C is its bf16 rounding. The
+rounding term cannot be dropped here, even at K = 8192 with random signs: the block scales span
+2^-5 .. 2^5, so a few 32-element blocks whose two scales are both near the top carry most of
+sum |a b|, and |ref| can reach over half of it (0.60 in a 512 x 512 numpy trial of these
+operands, where the bf16 rounding of the exact result alone reached 1.8 x the plain bound).
 Structured cases isolate the scale layout: per-row A scales, per-K-block A scales (each of the four
 MMAs of a stage reads its own scale byte), per-column B scales; random cases cover several tile
 counts, a quantise -> GEMM chain and a sampled 8192-cube.
@@ -15,7 +20,6 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 TOL_ACC = 2.0 ** -10
-TOL_OUT = 2.0 ** -8
 ONE = 0x38  # E4M3 1.0
 
 
@@ -40,13 +44,23 @@ def _run(torch, A, sfA, B, sfB):
     return c.float().cpu().numpy()
 
 
+def _half_ulp_bf16(c: np.ndarray) -> np.ndarray:
+    """Half an ulp of bf16 (8 significant bits) at each value of c (2^-134 at zero)."""
+    e = np.floor(np.log2(np.maximum(np.abs(c), 2.0 ** -126)))
+    return np.exp2(e - 8)
+
+
 def _check(oracle, A, sfA, B, sfB, Cg, rows, cols):
+    """Checks the sampled outputs; prints and returns the largest err / tolerance."""
     ref, mag = oracle.gemm_mxfp8_ref(A, sfA, B, sfB, rows, cols)
     got = Cg[rows, cols].astype(np.float64)
     err = np.abs(got - ref)
-    tol = TOL_ACC * mag + TOL_OUT * np.abs(ref)
+    tol = TOL_ACC * mag + _half_ulp_bf16(got)
     bad = np.nonzero(~(err <= tol))[0]
     assert bad.size == 0, [(int(rows[i]), int(cols[i]), got[i], ref[i]) for i in bad[:8]]
+    ratio = float((err / np.maximum(tol, 1e-300)).max())
+    print(f"max err / (2^-10 sum|ab| + half ulp) = {ratio:.4f} over {rows.size} outputs")
+    return ratio
 
 
 def _bf16(x: float) -> float:

@@ -2,10 +2,15 @@
 
 Operands are built on the CPU (the oracle's NVFP4 quantiser, row-major scales), the scales are
 rearranged into the blocked 128x4 layout in numpy, and the device result is compared with the
-oracle's f64 GEMM over the decoded values:
-  |C - ref| <= 2^-10 * ga*gb*sum_k |a b|  +  2^-8 * |ref|   (the second term: bf16 output rounding).
-Structured cases isolate the scale layout: per-row A scales, per-K-block A scales, per-column B
-scales; random cases cover several tile counts and the MLP up-projection shape (sampled).
+oracle's f64 GEMM over the decoded values. The MLP up-projection shape (M = 8192, N = 28672,
+K = 8192, random signs) is held to the plain accumulation bound
+  |C - ref| <= 2^-10 * ga*gb*sum_k |a b|,
+which also covers the bf16 rounding of the output there: with random signs |ref| is a small
+fraction of sum |a b| at K = 8192. The small random shapes (K down to 256) add the bf16 rounding
+of the output, 2^-8 * |ref| (half an ulp of bf16, relative): at small K a few large products can
+make |ref| close to sum |a b|, and then the rounding of a correct result alone can exceed the
+plain bound. Structured cases isolate the scale layout (per-row A scales, per-K-block A scales,
+per-column B scales) and are checked exactly.
 """
 
 import numpy as np
@@ -38,13 +43,18 @@ def _run(torch, A, sfA, ga, B, sfB, gb):
     return c.float().cpu().numpy()
 
 
-def _check(oracle, A, sfA, ga, B, sfB, gb, Cg, rows, cols):
+def _check(oracle, A, sfA, ga, B, sfB, gb, Cg, rows, cols, plain=False):
+    """Checks the sampled outputs; plain=True drops the output-rounding term. Prints and returns
+    the largest err / (2^-10 * sum |a b|)."""
     ref, mag = oracle.gemm_nvfp4_ref(A, sfA, ga, B, sfB, gb, rows, cols)
     got = Cg[rows, cols].astype(np.float64)
     err = np.abs(got - ref)
-    tol = TOL_ACC * mag + TOL_OUT * np.abs(ref)
+    tol = TOL_ACC * mag + (0.0 if plain else TOL_OUT * np.abs(ref))
     bad = np.nonzero(err > tol)[0]
     assert bad.size == 0, [(int(rows[i]), int(cols[i]), got[i], ref[i]) for i in bad[:8]]
+    ratio = float((err / np.maximum(TOL_ACC * mag, 1e-300)).max())
+    print(f"max err / (2^-10 sum|ab|) = {ratio:.4f} over {rows.size} outputs")
+    return ratio
 
 
 def _all(M, N):
@@ -122,4 +132,4 @@ def test_mlp_up_projection_sampled(cuda, oracle):
     rng = np.random.default_rng(6)
     rows = np.concatenate([rng.integers(0, M, 4096), np.full(N, 5), np.arange(M)])
     cols = np.concatenate([rng.integers(0, N, 4096), np.arange(N), np.full(M, N - 1)])
-    _check(oracle, A, sfA, ga, B, sfB, gb, Cg, rows, cols)
+    _check(oracle, A, sfA, ga, B, sfB, gb, Cg, rows, cols, plain=True)

@@ -6,9 +6,11 @@ scratch in a fixed device array inside the library instead of a caller workspace
 it through the C ABI twice in a row (the array keeps the previous call's contents, so the second
 call checks that each call re-initialises what it needs) and compares each result with
 ptxstd_gemm_decode's on the same inputs, within the tolerance the GEMM tests use:
-|a - b| <= 2^-10 * sum_k |x w| + 2^-8 * max(|a|, |b|). It also checks that a shape whose scratch
-exceeds the array is rejected. The file sorts last so that a run stopping at the first failure has
-already run every other test.
+|a - b| <= 2^-10 * sum_k |x w| + 2^-8 * max(|a|, |b|). Bit equality is not asked for: the decode
+adds the fp32 partial sums of a weight block's K segments into the scratch with atomic adds, in
+whatever order the CTAs finish, so two calls of either entry point can differ in the last bits.
+It also checks that a shape whose scratch exceeds the array is rejected. The file sorts last so
+that a run stopping at the first failure has already run every other test.
 """
 
 import ctypes as C
