@@ -178,13 +178,14 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
-// tma_store_tile::<2> (:746): smem -> global, tracked by the bulk async-group.
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t c0,
+// tma_store_tile::<2> (:746): smem (a .shared::cta address) -> global, tracked by the bulk
+// async-group. Stores never start at a negative coordinate here.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t c0,
                                              int32_t c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
             reinterpret_cast<uint64_t>(map)),
-        "r"(smem_u32(src)), "r"(c0), "r"(c1)
+        "r"(src), "r"(c0), "r"(c1)
         : "memory");
 }
 // bulk_commit_group / bulk_wait_group::<N> read variant (src/tma/mod.rs:204, :220).
@@ -213,6 +214,14 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
     return p;
+}
+
+// 16-byte store to a .shared::cta address.
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
 }
 
 // ---- streaming global memory ------------------------------------------------------------------

@@ -199,3 +199,16 @@ def test_sharded_two_gpus(cuda, tmp_path):
                        start_method="spawn")
     for r in range(2):
         assert open(tmp_path / f"rank{r}").read() == "ok"
+
+
+def test_sharded_all_gpus(cuda, tmp_path):
+    """The same checks with one rank on every visible GPU (4 or 8 on one box)."""
+    torch = cuda
+    n = torch.cuda.device_count()
+    if n <= 2:
+        pytest.skip("needs more than two GPUs")
+    import torch.multiprocessing as mp
+    mp.start_processes(_worker, args=(n, _free_port(), str(tmp_path)), nprocs=n, join=True,
+                       start_method="spawn")
+    for r in range(n):
+        assert open(tmp_path / f"rank{r}").read() == "ok"
