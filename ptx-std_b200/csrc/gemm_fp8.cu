@@ -11,7 +11,9 @@
 //                 N=256, K=32) four times per stage and commits each stage back to `empty[s]`
 //                 (src/tcgen05/mma.rs:434-453, sync.rs:70-80);
 //   warps 2..5    epilogue: tcgen05.ld.32x32b of their TMEM lane quarter, scale, RN to bf16,
-//                 16-byte stores (src/tcgen05/ld_st.rs:252-300).
+//                 16-byte stores (src/tcgen05/ld_st.rs:252-300); in the CTA-pair form the bf16
+//                 rows go through two swizzled staging buffers per warp and TMA tile stores of
+//                 32 rows x 64 columns (epilogue.cuh).
 // Two 128x256 fp32 accumulators (all 512 TMEM columns) let the epilogue of tile i overlap the
 // main loop of tile i+1. Tiles are visited in groups of 8 M-blocks so that concurrently running
 // CTAs share B tiles in L2. Every wait is bounded (kWaitLimitNs); a timeout records
@@ -19,6 +21,7 @@
 // returns.
 #include "common.cuh"
 #include "data_types.cuh"
+#include "epilogue.cuh"
 #include "tcgen05.cuh"
 #include "tma_host.h"
 
@@ -257,6 +260,8 @@ constexpr uint32_t kPStageBytesPair = 4 * kPHalfBytes;  // both CTAs' A and B ha
 struct alignas(1024) SmemPair {
     uint8_t a[P_STAGES][kPHalfBytes];
     uint8_t b[P_STAGES][kPHalfBytes];
+    // epilogue staging: two buffers of 32 rows x 64 bf16 columns per epilogue warp
+    uint8_t cstage[4][2][ptxstd::epi::Box<64>::kBytes];
     uint64_t full[P_STAGES];   // leader's counts both CTAs' bytes
     uint64_t empty[P_STAGES];
     uint64_t tfull[2];
@@ -278,8 +283,9 @@ __device__ __forceinline__ bool aborted_pair(SmemPair& s) {
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                         const __grid_constant__ CUtensorMap tmB, uint16_t* __restrict__ C,
-                         uint32_t M, uint32_t N, uint32_t K, float alpha, uint32_t* err) {
+                         const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmC, uint32_t M, uint32_t N,
+                         uint32_t K, float alpha, uint32_t* err) {
     extern __shared__ uint8_t smem_raw[];
     SmemPair& s = *reinterpret_cast<SmemPair*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -292,6 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         ptxstd::prefetch_tensormap(&tmA);
         ptxstd::prefetch_tensormap(&tmB);
+        ptxstd::prefetch_tensormap(&tmC);
         for (uint32_t i = 0; i < P_STAGES; ++i) {
             ptxstd::mbar_init(&s.full[i], 1);
             ptxstd::mbar_init(&s.empty[i], 1);
@@ -398,6 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
         const uint32_t q = warp & 3u;
+        const uint32_t stg = ptxstd::smem_u32(s.cstage[warp - 2u][0]);  // two buffers in a row
         uint32_t acc = 0, acc_phase = 0;
         for (uint32_t t = pair; t < num_tiles; t += n_pairs) {
             bool ok = !aborted_pair(s) && mbar_wait(&s.tfull[acc], acc_phase);
@@ -409,23 +417,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             t5::fence_after_thread_sync();
             uint32_t mb, nb;
             tile_coords(t, num_m, num_n, mb, nb);
-            const uint32_t row = mb * P_BM + rank * P_HALF + 32 * q + lane;
-            uint16_t* crow = C + static_cast<size_t>(row) * N + nb * P_BN;
+            const int32_t row0 = static_cast<int32_t>(mb * P_BM + rank * P_HALF + 32 * q);
+            const int32_t col0 = static_cast<int32_t>(nb * P_BN);
             const uint32_t tbase = tmem + ((32 * q) << 16) + acc * kAccCols;
+            // 64 columns at a time: TMEM -> registers -> staging buffer (two in turn) -> TMA store
 #pragma unroll 1
-            for (uint32_t c = 0; c < P_BN / 32; ++c) {
-                uint32_t r[32];
-                t5::ld_32x32b_x32(tbase + 32 * c, r);
+            for (uint32_t c = 0; c < P_BN / 64; ++c) {
+                uint32_t r[64];
+                t5::ld_32x32b_x32(tbase + 64 * c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+                t5::ld_32x32b_x32(tbase + 64 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
                 t5::wait_ld();
-                uint32_t p[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    p[j] = dt::bf16x2_from_f32(__uint_as_float(r[2 * j]) * alpha,
-                                               __uint_as_float(r[2 * j + 1]) * alpha);
-                uint4* dst = reinterpret_cast<uint4*>(crow + 32 * c);
-#pragma unroll
-                for (int v = 0; v < 4; ++v)
-                    dst[v] = make_uint4(p[4 * v], p[4 * v + 1], p[4 * v + 2], p[4 * v + 3]);
+                ptxstd::epi::wait_staging<1>(lane);
+                const uint32_t buf = stg + (c & 1u) * ptxstd::epi::Box<64>::kBytes;
+                ptxstd::epi::stage_store<64, 0>(&tmC, buf, r, alpha,
+                                                col0 + static_cast<int32_t>(64 * c), row0, lane);
             }
             t5::fence_before_thread_sync();
             __syncwarp();
@@ -436,6 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc_phase ^= 1u;
             }
         }
+        ptxstd::epi::drain(lane);
     }
 
     t5::fence_before_thread_sync();
@@ -446,12 +452,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 int launch_pair(const uint8_t* d_a, const uint8_t* d_b, uint16_t* d_c, int64_t M, int64_t N,
                 int64_t K, float alpha, cudaStream_t stream) {
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tc;
     int st = ptxstd::make_tmap_2d(&ta, d_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, K, BK, P_HALF,
                                   CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
     st = ptxstd::make_tmap_2d(&tb, d_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, K, BK, P_HALF,
                               CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = ptxstd::epi::make_store_map<64>(&tc, d_c, M, N);
     if (st) return st;
     st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(gemm_fp8_pair_kernel),
                                       static_cast<int>(kSmemPairBytes));
@@ -485,7 +493,7 @@ int launch_pair(const uint8_t* d_a, const uint8_t* d_b, uint16_t* d_c, int64_t M
     const uint32_t pairs = tiles < static_cast<uint32_t>(max_pairs[dev]) ? tiles
                                                                         : static_cast<uint32_t>(max_pairs[dev]);
     cfg.gridDim = dim3(2 * pairs);
-    if (cudaLaunchKernelEx(&cfg, gemm_fp8_pair_kernel, ta, tb, d_c, static_cast<uint32_t>(M),
+    if (cudaLaunchKernelEx(&cfg, gemm_fp8_pair_kernel, ta, tb, tc, static_cast<uint32_t>(M),
                            static_cast<uint32_t>(N), static_cast<uint32_t>(K), alpha,
                            err) != cudaSuccess)
         return PTXSTD_ECUDA;

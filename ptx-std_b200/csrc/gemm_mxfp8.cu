@@ -30,9 +30,11 @@
 // TMEM: one 256-column f32 accumulator plus 6 stages x 12 scale columns. Two accumulators
 // (512 columns) would leave no room for the scales, so eight epilogue warps (two per lane quarter,
 // 128 columns each) copy the accumulator to registers and release it before converting and
-// storing.
+// storing. The bf16 tile leaves through a swizzled staging buffer per warp and TMA tile stores
+// of 32 rows x 32 columns (epilogue.cuh).
 #include "common.cuh"
 #include "data_types.cuh"
+#include "epilogue.cuh"
 #include "tcgen05.cuh"
 #include "tma_host.h"
 
@@ -60,12 +62,16 @@ constexpr uint32_t kSfBase = kAccCols;
 constexpr uint32_t kTmemCols = 512;
 static_assert(kSfBase + STAGES * kSlotCols <= kTmemCols, "TMEM budget");
 constexpr uint32_t kGroupM = 8;
+// Epilogue stores: 32 bf16 columns (64-byte row segments) per TMA store, so that the 2 KiB
+// staging buffers of the eight epilogue warps fit beside six stages.
+constexpr uint32_t kCCols = 32;
 
 struct alignas(1024) Smem {
     uint8_t a[STAGES][kABytes];
     uint8_t b[STAGES][kBBytes];
     uint8_t sfa[STAGES][kSfaBytes];
     uint8_t sfb[STAGES][kSfbBytes];
+    uint8_t cstage[kEpiWarps][ptxstd::epi::Box<kCCols>::kBytes];  // epilogue staging per warp
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
     uint64_t tfull;
@@ -117,9 +123,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_mxfp8_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                            const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmSfa,
-                           const __grid_constant__ CUtensorMap tmSfb, uint16_t* __restrict__ C,
-                           uint32_t M, uint32_t N, uint32_t K, uint32_t atype, uint32_t btype,
-                           uint32_t* err) {
+                           const __grid_constant__ CUtensorMap tmSfb,
+                           const __grid_constant__ CUtensorMap tmC, uint32_t M, uint32_t N,
+                           uint32_t K, uint32_t atype, uint32_t btype, uint32_t* err) {
     extern __shared__ uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~static_cast<uintptr_t>(1023));
@@ -133,6 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         ptxstd::prefetch_tensormap(&tmA);
         ptxstd::prefetch_tensormap(&tmB);
+        ptxstd::prefetch_tensormap(&tmC);
         ptxstd::prefetch_tensormap(&tmSfa);
         ptxstd::prefetch_tensormap(&tmSfb);
         for (uint32_t i = 0; i < STAGES; ++i) {
@@ -258,6 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t half = (warp - 2u) >> 2;
         uint32_t acc_phase = 0;
         const uint32_t tempty_leader = ptxstd::mapa_shared(ptxstd::smem_u32(&s.tempty), 0);
+        const uint32_t stg = ptxstd::smem_u32(s.cstage[warp - 2u]);
         for (uint32_t t = pair; t < num_tiles; t += n_pairs) {
             bool ok = !aborted(s) && mbar_wait(&s.tfull, acc_phase);
             ok = __all_sync(0xffffffffu, ok);
@@ -286,18 +294,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             uint32_t mb, nb;
             tile_coords(t, num_m, num_n, mb, nb);
-            const uint32_t row = mb * P_BM + rank * P_HALF + 32 * q + lane;
-            uint16_t* crow = C + static_cast<size_t>(row) * N + nb * P_BN + half * 128;
-#pragma unroll
-            for (uint32_t c = 0; c < 16; ++c) {
-                uint32_t p[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    p[j] = dt::bf16x2_from_f32(__uint_as_float(r[8 * c + 2 * j]),
-                                               __uint_as_float(r[8 * c + 2 * j + 1]));
-                reinterpret_cast<uint4*>(crow)[c] = make_uint4(p[0], p[1], p[2], p[3]);
-            }
+            const int32_t row0 = static_cast<int32_t>(mb * P_BM + rank * P_HALF + 32 * q);
+            const int32_t col0 = static_cast<int32_t>(nb * P_BN + half * 128);
+            ptxstd::epi::store_row_block<kCCols>(&tmC, stg, r, 1.0f, col0, row0, lane);
         }
+        ptxstd::epi::drain(lane);
     }
 
     t5::fence_before_thread_sync();
@@ -322,7 +323,7 @@ extern "C" int ptxstd_gemm_mx(const uint8_t* d_a, int a_type, const uint8_t* d_s
         !ptxstd::aligned16(d_b) || !ptxstd::aligned16(d_c) || !ptxstd::aligned16(d_sfa) ||
         !ptxstd::aligned16(d_sfb))
         return PTXSTD_EINVAL;
-    CUtensorMap ta, tb, tsa, tsb;
+    CUtensorMap ta, tb, tsa, tsb, tc;
     int st = ptxstd::make_tmap_2d(&ta, d_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, K, BK, P_HALF,
                                   CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
@@ -335,6 +336,8 @@ extern "C" int ptxstd_gemm_mx(const uint8_t* d_a, int a_type, const uint8_t* d_s
     if (st) return st;
     st = ptxstd::make_tmap_2d(&tsb, d_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 128,
                               (N / 128) * (K / 128), 512, 128, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    st = ptxstd::epi::make_store_map<kCCols>(&tc, d_c, M, N);
     if (st) return st;
     st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(gemm_mxfp8_pair_kernel),
                                       static_cast<int>(kSmemBytes));
@@ -369,7 +372,7 @@ extern "C" int ptxstd_gemm_mx(const uint8_t* d_a, int a_type, const uint8_t* d_s
     const uint32_t pairs =
         tiles < static_cast<uint32_t>(max_pairs[dev]) ? tiles : static_cast<uint32_t>(max_pairs[dev]);
     cfg.gridDim = dim3(2 * pairs);
-    if (cudaLaunchKernelEx(&cfg, gemm_mxfp8_pair_kernel, ta, tb, tsa, tsb, d_c,
+    if (cudaLaunchKernelEx(&cfg, gemm_mxfp8_pair_kernel, ta, tb, tsa, tsb, tc,
                            static_cast<uint32_t>(M), static_cast<uint32_t>(N),
                            static_cast<uint32_t>(K), static_cast<uint32_t>(a_type),
                            static_cast<uint32_t>(b_type), err) != cudaSuccess)

@@ -27,6 +27,7 @@
 // then issues the stage's four K = 64 MMAs with scale ids j.
 #include "common.cuh"
 #include "data_types.cuh"
+#include "epilogue.cuh"
 #include "tcgen05.cuh"
 #include "tma_host.h"
 
@@ -62,6 +63,9 @@ static_assert(kSlotCols % 4 == 0, "metadata and scale slots start on 4-column bo
 // Grouped raster of kGroupM row-tiles; 16 measured 2-4 % ahead of 8 at 8192^3 (five interleaved
 // repetitions each on one B200, bit-identical output).
 constexpr uint32_t kGroupM = 16;
+// Epilogue stores: 16 bf16 columns (32-byte row segments, whole L2 sectors) per TMA store, so that
+// the 1 KiB staging buffers of the eight epilogue warps fit beside the four 53.5 KiB stages.
+constexpr uint32_t kCCols = 16;
 
 struct alignas(1024) Smem {
     uint8_t a[STAGES][kABytes];
@@ -69,6 +73,7 @@ struct alignas(1024) Smem {
     uint8_t meta[STAGES][2][kMetaChunkBytes];
     uint8_t sfa[STAGES][kSfaBytes];
     uint8_t sfb[STAGES][kSfbBytes];
+    uint8_t cstage[kEpiWarps][ptxstd::epi::Box<kCCols>::kBytes];  // epilogue staging per warp
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
     uint64_t tfull;
@@ -107,8 +112,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   const __grid_constant__ CUtensorMap tmB,
                                   const __grid_constant__ CUtensorMap tmSfa,
                                   const __grid_constant__ CUtensorMap tmSfb,
-                                  uint16_t* __restrict__ C, uint32_t M, uint32_t N, uint32_t K,
-                                  uint32_t* err) {
+                                  const __grid_constant__ CUtensorMap tmC, uint32_t M, uint32_t N,
+                                  uint32_t K, uint32_t* err) {
     extern __shared__ uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~static_cast<uintptr_t>(1023));
@@ -126,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptxstd::prefetch_tensormap(&tmB);
         ptxstd::prefetch_tensormap(&tmSfa);
         ptxstd::prefetch_tensormap(&tmSfb);
+        ptxstd::prefetch_tensormap(&tmC);
         for (uint32_t i = 0; i < STAGES; ++i) {
             ptxstd::mbar_init(&s.full[i], 1);
             ptxstd::mbar_init(&s.empty[i], 1);
@@ -267,6 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t half = (warp - 2u) >> 2;
         uint32_t acc_phase = 0;
         const uint32_t tempty_leader = ptxstd::mapa_shared(ptxstd::smem_u32(&s.tempty), 0);
+        const uint32_t stg = ptxstd::smem_u32(s.cstage[warp - 2u]);
         for (uint32_t t = pair; t < num_tiles; t += n_pairs) {
             bool ok = !aborted(s) && mbar_wait(&s.tfull, acc_phase);
             ok = __all_sync(0xffffffffu, ok);
@@ -295,18 +302,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             uint32_t mb, nb;
             tile_coords(t, num_m, num_n, mb, nb);
-            const uint32_t row = mb * P_BM + rank * P_HALF + 32 * q + lane;
-            uint16_t* crow = C + static_cast<size_t>(row) * N + nb * P_BN + half * 128;
-#pragma unroll
-            for (uint32_t c = 0; c < 16; ++c) {
-                uint32_t p[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    p[j] = dt::bf16x2_from_f32(__uint_as_float(r[8 * c + 2 * j]),
-                                               __uint_as_float(r[8 * c + 2 * j + 1]));
-                reinterpret_cast<uint4*>(crow)[c] = make_uint4(p[0], p[1], p[2], p[3]);
-            }
+            const int32_t row0 = static_cast<int32_t>(mb * P_BM + rank * P_HALF + 32 * q);
+            const int32_t col0 = static_cast<int32_t>(nb * P_BN + half * 128);
+            ptxstd::epi::store_row_block<kCCols>(&tmC, stg, r, 1.0f, col0, row0, lane);
         }
+        ptxstd::epi::drain(lane);
     }
 
     t5::fence_before_thread_sync();
@@ -374,7 +374,7 @@ extern "C" int ptxstd_gemm_mxfp8_sparse(const uint8_t* d_vals, const uint8_t* d_
         !ptxstd::aligned16(d_meta) || !ptxstd::aligned16(d_b) || !ptxstd::aligned16(d_c) ||
         !ptxstd::aligned16(d_sfa) || !ptxstd::aligned16(d_sfb))
         return PTXSTD_EINVAL;
-    CUtensorMap ta, tm, tb, tsa, tsb;
+    CUtensorMap ta, tm, tb, tsa, tsb, tc;
     int st = ptxstd::make_tmap_2d(&ta, d_vals, CU_TENSOR_MAP_DATA_TYPE_UINT8, K / 2, M, K / 2,
                                   BKL / 2, P_HALF, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
@@ -390,6 +390,8 @@ extern "C" int ptxstd_gemm_mxfp8_sparse(const uint8_t* d_vals, const uint8_t* d_
     if (st) return st;
     st = ptxstd::make_tmap_2d(&tsb, d_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 128,
                               (N / 128) * (K / 256), 512, 128, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    st = ptxstd::epi::make_store_map<kCCols>(&tc, d_c, M, N);
     if (st) return st;
     st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(gemm_mxfp8_sparse_pair_kernel),
                                       static_cast<int>(kSmemBytes));
@@ -423,7 +425,7 @@ extern "C" int ptxstd_gemm_mxfp8_sparse(const uint8_t* d_vals, const uint8_t* d_
     const uint32_t pairs =
         tiles < static_cast<uint32_t>(max_pairs[dev]) ? tiles : static_cast<uint32_t>(max_pairs[dev]);
     cfg.gridDim = dim3(2 * pairs);
-    if (cudaLaunchKernelEx(&cfg, gemm_mxfp8_sparse_pair_kernel, ta, tm, tb, tsa, tsb, d_c,
+    if (cudaLaunchKernelEx(&cfg, gemm_mxfp8_sparse_pair_kernel, ta, tm, tb, tsa, tsb, tc,
                            static_cast<uint32_t>(M), static_cast<uint32_t>(N),
                            static_cast<uint32_t>(K), err) != cudaSuccess)
         return PTXSTD_ECUDA;

@@ -309,7 +309,7 @@ struct alignas(1024) SmemPair {
     uint8_t b[P_STAGES][kPBBytes];
     uint8_t sfa[P_STAGES][kPSfaBytes];
     uint8_t sfb[P_STAGES][kPSfbBytes];
-    uint8_t cstage[kEpiWarps][ptxstd::epi::kStageBytes];  // epilogue staging, one per warp
+    uint8_t cstage[kEpiWarps][ptxstd::epi::Box<64>::kBytes];  // epilogue staging, one per warp
     uint64_t full[P_STAGES];
     uint64_t empty[P_STAGES];
     uint64_t tfull;
@@ -509,10 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // warp's staging buffer
             const int32_t row0 = static_cast<int32_t>(mb * P_BM + rank * P_HALF + 32 * q);
             const int32_t col0 = static_cast<int32_t>(nb * P_BN + half * 128);
-            ptxstd::epi::wait_staging(lane);
-            ptxstd::epi::stage_store<0>(&tmC, stg, r, alpha, col0, row0, lane);
-            ptxstd::epi::wait_staging(lane);
-            ptxstd::epi::stage_store<1>(&tmC, stg, r, alpha, col0 + 64, row0, lane);
+            ptxstd::epi::store_row_block<64>(&tmC, stg, r, alpha, col0, row0, lane);
         }
         ptxstd::epi::drain(lane);
     }
@@ -540,8 +537,7 @@ int launch_pair(const uint8_t* d_a, const uint8_t* d_sfa, const uint8_t* d_b,
     st = ptxstd::make_tmap_2d(&tsb, d_sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 128,
                               (N / 128) * (K / 64), 512, 128, kMmas, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
-    st = ptxstd::make_tmap_2d(&tc, d_c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, N, M, N * 2,
-                              ptxstd::epi::kCols, ptxstd::epi::kRows, CU_TENSOR_MAP_SWIZZLE_128B);
+    st = ptxstd::epi::make_store_map<64>(&tc, d_c, M, N);
     if (st) return st;
     st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(gemm_nvfp4_pair_kernel),
                                       static_cast<int>(kSmemPairBytes));
