@@ -231,6 +231,17 @@ PTXSTD_API int ptxstd_gemm_nvfp4(const uint8_t* d_a, const uint8_t* d_sfa, float
                                  const uint8_t* d_b, const uint8_t* d_sfb, float gb,
                                  uint16_t* d_c, int64_t M, int64_t N, int64_t K,
                                  ptxstd_stream stream);
+/* Tile schedule of the CTA-pair NVFP4 GEMM (process-wide; later launches use it).
+ * PTXSTD_SCHEDULE_PERSISTENT (default): one resident CTA pair per two SMs walks a fixed raster
+ *   of tiles; fastest when the GEMM has the GPU to itself.
+ * PTXSTD_SCHEDULE_DYNAMIC: one cluster per tile; running pairs take over the tiles of clusters
+ *   that have not started (cluster launch control: try_cancel_launch, src/launch.rs:154-176), so
+ *   work moves to whichever SMs are free when other kernels hold some of them.
+ * Returns PTXSTD_EINVAL for any other value. */
+#define PTXSTD_SCHEDULE_PERSISTENT 0
+#define PTXSTD_SCHEDULE_DYNAMIC 1
+PTXSTD_API int ptxstd_set_gemm_schedule(int schedule);
+PTXSTD_API int ptxstd_get_gemm_schedule(void);
 /* MXFP8 GEMM (OCP MX): C[M,N] bf16 = sum_k (A[m,k] 2^(sfA[m,k/32]-127)) (B[n,k] 2^(sfB[n,k/32]-127)).
  * A [M,K], B [N,K]: E4M3, K contiguous. sfA, sfB: UE8M0 scales per 32 K elements in the blocked
  * layout of ptxstd_quantize_mxfp8_layout(sf_layout = 1), so quantised activations feed it as they

@@ -96,7 +96,74 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     return true;
 }
 
+// The same wait with acquire at cluster scope, for data that a thread of another CTA of the
+// cluster wrote before its remote (release.cluster) arrive on `bar`.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait_cluster(a, parity)) return true;  // the timer only once it has to wait
+    const uint64_t t0 = global_timer();
+    while (!mbar_try_wait_cluster(a, parity)) {
+        if (global_timer() - t0 > kWaitLimitNs) return false;
+    }
+    return true;
+}
+
+// ---- launch control and register allocation (src/launch.rs) ----------------------------------
+// try_cancel_launch::<CancelDelivery::Block> (:154-176): asks to cancel a cluster of this grid
+// that has not started yet. The 16-byte response is written to `resp` (this CTA's smem, 16-byte
+// aligned) through the async proxy and completes a 16-byte transaction on `bar`, which must
+// expect it. After a response that cancelled nothing, no further request may be issued.
+__device__ __forceinline__ void clc_try_cancel(void* resp, uint64_t* bar) {
+    asm volatile(
+        "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 "
+        "[%0], [%1];" ::"r"(smem_u32(resp)),
+        "r"(smem_u32(bar))
+        : "memory");
+}
+// CancelResponse::first_cta_id (:86-106): x index of the first CTA of the cancelled cluster, or
+// -1 when the request cancelled nothing.
+__device__ __forceinline__ int32_t clc_first_ctaid_x(const void* resp) {
+    uint32_t ok, x;
+    asm volatile(
+        "{\n\t.reg .b128 v;\n\t.reg .pred p;\n\tld.shared.b128 v, [%2];\n\t"
+        "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, v;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, v;\n\t}"
+        : "=r"(ok), "=r"(x)
+        : "r"(smem_u32(resp))
+        : "memory");
+    return ok ? static_cast<int32_t>(x) : -1;
+}
+// increase_max_registers / decrease_max_registers (:204, :240): every warp of a warpgroup
+// executes the same one; N is a multiple of 8 in 24..256. The kernel must be launched with a
+// known register count (__launch_bounds__ with a minimum of one block).
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+    static_assert(N % 8 == 0 && N >= 24 && N <= 256, "register count");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+    static_assert(N % 8 == 0 && N >= 24 && N <= 256, "register count");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---- clusters (src/cluster.rs, src/globals.rs) -----------------------------------------------
+// 32-bit store to a .shared::cluster address (a variable of any CTA of the cluster, via mapa).
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
 // block_rank_in_cluster (globals.rs:283).
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;

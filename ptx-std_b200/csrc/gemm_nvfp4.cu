@@ -23,6 +23,8 @@
 // segments instead of 16-byte pieces of 32 rows per instruction. At 8192 x 28672 x 8192 on a
 // B200 that took a launch from 759 us to 666 us at full clock (913-922 us to 731-738 us once the
 // power cap lowers the clock), against 637 us for a copy of the kernel that stores nothing.
+#include <atomic>
+
 #include "common.cuh"
 #include "data_types.cuh"
 #include "epilogue.cuh"
@@ -76,7 +78,8 @@ struct alignas(1024) Smem {
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-enum : uint32_t { kDetailProducer = 0x1100, kDetailMma = 0x1200, kDetailEpilogue = 0x1300 };
+enum : uint32_t { kDetailProducer = 0x1100, kDetailMma = 0x1200, kDetailEpilogue = 0x1300,
+                  kDetailSched = 0x1400 };
 
 __device__ __forceinline__ void tile_coords(uint32_t t, uint32_t num_m, uint32_t num_n,
                                             uint32_t& mb, uint32_t& nb) {
@@ -293,7 +296,38 @@ __global__ void __launch_bounds__(kThreads, 1)
 // 128 x 4 = the four 512-byte tiles of one stage), so that, like the operand tiles, they complete
 // on the leader's `full` barrier. The leader issues tcgen05.cp.cta_group::2 (each CTA copies its
 // own smem scales into its own TMEM) and tcgen05.mma.cta_group::2.kind::mxf4nvf4 (M = 256).
+//
+// Warp roles, 12 warps in three warpgroups:
+//   warp 0      producer (both CTAs): operand tiles and scales into the P_STAGES ring;
+//   warp 1      TMEM owner; in the leader, the MMA issuer;
+//   warp 2      tile scheduler (leader), dynamic schedule only: the grid holds one cluster per
+//               tile, and a running pair takes over the tiles of clusters not started yet by
+//               cancelling them
+//               (clusterlaunchcontrol.try_cancel, the reference's
+//               try_cancel_launch::<CancelDelivery::Block>, src/launch.rs:154-176). It publishes
+//               each tile index to both CTAs through a ring of kSlots entries in shared memory
+//               (written into the peer with st.shared::cluster, signalled by remote arrives), and
+//               kNoTile once a request cancels nothing;
+//   warp 3      idle;
+//   warps 4-11  epilogue, two per TMEM lane quarter (128 columns each).
+// The persistent schedule (the default) launches one pair per two SMs and every role walks the
+// static raster pair, pair + n_pairs, ... itself. On 8192 x 28672 x 8192 alone on a B200 it ran
+// 681 us against 691 us for the dynamic one, whose per-tile hand-offs cost about 1.5 %; the
+// dynamic schedule is for GEMMs that share the GPU with other kernels.
+// Warpgroup 0 needs few registers and the epilogue's hold a 128-column accumulator row per
+// thread, so warpgroup 0 gives registers back with setmaxnreg.dec (decrease_max_registers,
+// src/launch.rs:240) and the two epilogue warpgroups take them with setmaxnreg.inc
+// (increase_max_registers, :204). The kernel is launched at kRegsLaunch registers per thread.
 constexpr uint32_t P_BM = 256, P_BN = 256, P_HALF = 128;
+constexpr uint32_t kPThreads = 384;
+constexpr uint32_t kPFirstEpiWarp = 4;
+constexpr uint32_t kRegsLaunch = 168;  // 65536 / 384, rounded down to a multiple of 8
+constexpr uint32_t kRegsCtl = 80, kRegsEpi = 208;
+static_assert(128 * kRegsCtl + 256 * kRegsEpi <= kPThreads * kRegsLaunch, "register split");
+constexpr uint32_t kSlots = 4;  // tile-index ring between the scheduler and the other roles
+constexpr uint32_t kNoTile = 0xffffffffu;
+// roles that read every published tile index: producer (both CTAs), MMA, epilogue (both CTAs)
+constexpr uint32_t kSlotReaders = 2 + 1 + 2 * kEpiWarps;
 constexpr uint32_t P_STAGES = 5;
 constexpr uint32_t kPABytes = P_HALF * BKB;            // 16 KiB
 constexpr uint32_t kPBBytes = P_HALF * BKB;            // 16 KiB
@@ -310,11 +344,16 @@ struct alignas(1024) SmemPair {
     uint8_t sfa[P_STAGES][kPSfaBytes];
     uint8_t sfb[P_STAGES][kPSfbBytes];
     uint8_t cstage[kEpiWarps][ptxstd::epi::Box<64>::kBytes];  // epilogue staging, one per warp
+    uint4 clc_resp;  // cluster launch control response (leader)
     uint64_t full[P_STAGES];
     uint64_t empty[P_STAGES];
     uint64_t tfull;
     uint64_t tempty;  // leader's: one arrive per epilogue warp of both CTAs
     uint64_t drain;
+    uint64_t clc_bar;               // leader's: completes when a response has arrived
+    uint64_t slot_full[kSlots];     // both CTAs: the scheduler has published the slot
+    uint64_t slot_empty[kSlots];    // leader's: every reader of both CTAs has read the slot
+    uint32_t slot_tile[kSlots];     // both CTAs: published tile indices
     uint32_t tmem_base;
     uint32_t abort;
 };
@@ -329,7 +368,49 @@ __device__ __forceinline__ bool aborted_pair(SmemPair& s) {
     return *reinterpret_cast<volatile uint32_t*>(&s.abort) != 0u;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+// Entry `seq` of the published tile sequence: waits (bounded) for slot seq % kSlots and returns
+// its tile index, or kNoTile after a timeout (recorded). The caller tells the scheduler it has
+// read the slot with release_slot once every lane that needs the index has it. The leader's
+// readers synchronise with the scheduler (a thread of their own CTA) at CTA scope; the peer's
+// readers, whose slot the scheduler writes remotely, at cluster scope.
+__device__ __forceinline__ uint32_t read_slot(SmemPair& s, uint32_t seq, uint32_t rank,
+                                              uint32_t* err, uint32_t detail) {
+    const uint32_t slot = seq % kSlots, parity = (seq / kSlots) & 1u;
+    const bool ok = rank == 0 ? ptxstd::mbar_wait(&s.slot_full[slot], parity)
+                              : ptxstd::mbar_wait_cluster(&s.slot_full[slot], parity);
+    if (!ok) {
+        if (!aborted_pair(s)) fail_pair(s, err, detail);
+        return kNoTile;
+    }
+    return *reinterpret_cast<volatile uint32_t*>(&s.slot_tile[slot]);
+}
+__device__ __forceinline__ void release_slot(SmemPair& s, uint32_t seq, uint32_t rank) {
+    if (rank == 0)
+        ptxstd::mbar_arrive(&s.slot_empty[seq % kSlots]);
+    else
+        ptxstd::mbar_arrive_cluster(
+            ptxstd::mapa_shared(ptxstd::smem_u32(&s.slot_empty[seq % kSlots]), 0));
+}
+
+// Entry `seq` of this pair's tile sequence, for a role that reads it with one thread.
+// Persistent schedule: the static raster pair, pair + n_pairs, ... (no communication).
+// Dynamic schedule: the scheduler's published entry, released once read.
+template <bool kDynamic>
+__device__ __forceinline__ uint32_t take_tile(SmemPair& s, uint32_t seq, uint32_t rank,
+                                              uint32_t num_tiles, uint32_t* err,
+                                              uint32_t detail) {
+    if constexpr (!kDynamic) {
+        const uint64_t t = (blockIdx.x >> 1) + static_cast<uint64_t>(seq) * (gridDim.x >> 1);
+        return t < num_tiles ? static_cast<uint32_t>(t) : kNoTile;
+    } else {
+        const uint32_t t = read_slot(s, seq, rank, err, detail);
+        if (t != kNoTile) release_slot(s, seq, rank);
+        return t;
+    }
+}
+
+template <bool kDynamic>
+__global__ void __launch_bounds__(kPThreads, 1)
     gemm_nvfp4_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                            const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmSfa,
@@ -342,8 +423,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t warp = ptxstd::warp_id();
     const uint32_t lane = ptxstd::lane_id();
     const uint32_t rank = ptxstd::cluster_ctarank();
-    const uint32_t pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
-    const uint32_t num_m = M / P_BM, num_n = N / P_BN, num_tiles = num_m * num_n, num_k = K / BK;
+    const uint32_t num_m = M / P_BM, num_n = N / P_BN, num_k = K / BK;
+    const uint32_t num_tiles = num_m * num_n;
     const uint32_t sf_tiles_per_row = K / 64;
 
     if (warp == 0 && lane == 0) {
@@ -359,6 +440,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptxstd::mbar_init(&s.tfull, 1);
         ptxstd::mbar_init(&s.tempty, 2 * kEpiWarps);
         ptxstd::mbar_init(&s.drain, 1);
+        ptxstd::mbar_init(&s.clc_bar, 1);
+        for (uint32_t i = 0; i < kSlots; ++i) {
+            ptxstd::mbar_init(&s.slot_full[i], 1);
+            ptxstd::mbar_init(&s.slot_empty[i], kSlotReaders);
+        }
         s.abort = 0;
         ptxstd::fence_mbarrier_init();
     }
@@ -370,15 +456,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptxstd::cluster_sync();
     t5::fence_after_thread_sync();
     const uint32_t tmem = s.tmem_base;
+    // Each role changes its register budget at the top of its own branch, so that the compiler
+    // allocates every branch for the budget it runs with.
 
     if (warp == 0) {
         // ---------------- producer (both CTAs) ----------------
+        ptxstd::setmaxnreg_dec<kRegsCtl>();
         if (ptxstd::elect_one()) {
             uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
-            for (uint32_t t = pair; t < num_tiles && !aborted_pair(s); t += n_pairs) {
-                uint32_t mb, nb;
+            uint32_t t = take_tile<kDynamic>(s, 0, rank, num_tiles, err, kDetailProducer | 0xC0);
+            for (uint32_t seq = 0; t != kNoTile && !aborted_pair(s); ++seq) {
+                uint32_t mb, nb, t_next = kNoTile;
                 tile_coords(t, num_m, num_n, mb, nb);
                 for (uint32_t kb = 0; kb < num_k; ++kb) {
+                    if (kb == 1 || num_k == 1) {
+                        // the next tile index, read inside this tile rather than at its end
+                        t_next = take_tile<kDynamic>(s, seq + 1, rank, num_tiles, err,
+                                                     kDetailProducer | 0xC1);
+                    }
                     if (!mbar_wait(&s.empty[stage], phase ^ 1u)) {
                         fail_pair(s, err, kDetailProducer | 0x80 | stage);
                         break;
@@ -406,6 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         phase ^= 1u;
                     }
                 }
+                t = t_next;
             }
             if (aborted_pair(s) && rank == 0) {
                 for (uint32_t i = 0; i < P_STAGES; ++i)
@@ -414,11 +510,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer (leader) ----------------
+        ptxstd::setmaxnreg_dec<kRegsCtl>();
         if (rank == 0 && ptxstd::elect_one()) {
             uint32_t idesc = 0;
             t5::idesc_mxf4nvf4(/*Ue4m3*/ 0, P_BM, P_BN, idesc);
             uint32_t stage = 0, phase = 0, acc_phase = 0;
-            for (uint32_t t = pair; t < num_tiles && !aborted_pair(s); t += n_pairs) {
+            // the MMA issuer needs only whether another tile follows; it reads the next index
+            // inside the current tile, so that no tile boundary waits on the scheduler
+            uint32_t t = take_tile<kDynamic>(s, 0, 0, num_tiles, err, kDetailMma | 0xC0);
+            for (uint32_t seq = 0; t != kNoTile && !aborted_pair(s); ++seq) {
+                uint32_t t_next = kNoTile;
                 if (!mbar_wait(&s.tempty, acc_phase ^ 1u)) {
                     fail_pair(s, err, kDetailMma | 0x90);
                     break;
@@ -460,24 +561,75 @@ __global__ void __launch_bounds__(kThreads, 1)
                         stage = 0;
                         phase ^= 1u;
                     }
+                    if (kb == 0) {
+                        t_next = take_tile<kDynamic>(s, seq + 1, 0, num_tiles, err,
+                                                     kDetailMma | 0xC1);
+                    }
                 }
                 if (!ok) break;
                 const uint32_t f = ptxstd::smem_u32(&s.tfull);
                 t5::commit_pair(f);
                 t5::commit_pair(ptxstd::mapa_shared(f, 1));
                 acc_phase ^= 1u;
+                t = t_next;
             }
             t5::commit_pair(ptxstd::smem_u32(&s.drain));
             mbar_wait(&s.drain, 0);
         }
+    } else if (warp == 2) {
+        // ---------------- tile scheduler (leader) ----------------
+        ptxstd::setmaxnreg_dec<kRegsCtl>();
+        if (kDynamic && rank == 0 && ptxstd::elect_one()) {
+            uint32_t t = blockIdx.x >> 1;  // this cluster's own tile first
+            uint32_t resp_phase = 0;
+            for (uint32_t seq = 0;; ++seq) {
+                const uint32_t slot = seq % kSlots;
+                // every reader of both CTAs has read this slot's previous entry
+                if (!mbar_wait(&s.slot_empty[slot], ((seq / kSlots) & 1u) ^ 1u)) {
+                    fail_pair(s, err, kDetailSched | slot);
+                    break;
+                }
+                s.slot_tile[slot] = t;
+                ptxstd::st_shared_cluster_u32(
+                    ptxstd::mapa_shared(ptxstd::smem_u32(&s.slot_tile[slot]), 1), t);
+                ptxstd::mbar_arrive(&s.slot_full[slot]);
+                ptxstd::mbar_arrive_cluster(
+                    ptxstd::mapa_shared(ptxstd::smem_u32(&s.slot_full[slot]), 1));
+                if (t == kNoTile) break;
+                // the next tile: cancel a cluster that has not started and take over its tile
+                ptxstd::fence_proxy_async_smem();  // earlier reads of the response come first
+                ptxstd::mbar_arrive_expect_tx(&s.clc_bar, 16);
+                ptxstd::clc_try_cancel(&s.clc_resp, &s.clc_bar);
+                if (!mbar_wait(&s.clc_bar, resp_phase)) {
+                    fail_pair(s, err, kDetailSched | 0x10);
+                    t = kNoTile;
+                    continue;  // publish the end of the sequence
+                }
+                resp_phase ^= 1u;
+                const int32_t x = ptxstd::clc_first_ctaid_x(&s.clc_resp);
+                t = x < 0 ? kNoTile : static_cast<uint32_t>(x) >> 1;
+            }
+        }
+    } else if (warp == 3) {
+        ptxstd::setmaxnreg_dec<kRegsCtl>();  // idle: its share of registers goes to the epilogue
     } else {
-        // ---------------- epilogue: warps 2..9 of both CTAs ----------------
+        // ---------------- epilogue: warps 4..11 of both CTAs ----------------
+        ptxstd::setmaxnreg_inc<kRegsEpi>();
         const uint32_t q = warp & 3u;
-        const uint32_t half = (warp - 2u) >> 2;
+        const uint32_t half = (warp - kPFirstEpiWarp) >> 2;
         uint32_t acc_phase = 0;
         const uint32_t tempty_leader = ptxstd::mapa_shared(ptxstd::smem_u32(&s.tempty), 0);
-        const uint32_t stg = ptxstd::smem_u32(s.cstage[warp - 2u]);
-        for (uint32_t t = pair; t < num_tiles; t += n_pairs) {
+        const uint32_t stg = ptxstd::smem_u32(s.cstage[warp - kPFirstEpiWarp]);
+        for (uint32_t seq = 0;; ++seq) {
+            uint32_t t = 0;
+            if constexpr (kDynamic) {
+                if (lane == 0) t = read_slot(s, seq, rank, err, kDetailEpilogue | 0xC0);
+                t = __shfl_sync(0xffffffffu, t, 0);
+                if (t != kNoTile && lane == 0) release_slot(s, seq, rank);
+            } else {
+                t = take_tile<false>(s, seq, rank, num_tiles, err, 0);
+            }
+            if (t == kNoTile) break;
             bool ok = !aborted_pair(s) && mbar_wait(&s.tfull, acc_phase);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
@@ -539,8 +691,10 @@ int launch_pair(const uint8_t* d_a, const uint8_t* d_sfa, const uint8_t* d_b,
     if (st) return st;
     st = ptxstd::epi::make_store_map<64>(&tc, d_c, M, N);
     if (st) return st;
-    st = ptxstd::set_max_dynamic_smem(reinterpret_cast<const void*>(gemm_nvfp4_pair_kernel),
-                                      static_cast<int>(kSmemPairBytes));
+    const bool dynamic = ptxstd_get_gemm_schedule() == PTXSTD_SCHEDULE_DYNAMIC;
+    const void* kernel = dynamic ? reinterpret_cast<const void*>(gemm_nvfp4_pair_kernel<true>)
+                                 : reinterpret_cast<const void*>(gemm_nvfp4_pair_kernel<false>);
+    st = ptxstd::set_max_dynamic_smem(kernel, static_cast<int>(kSmemPairBytes));
     if (st) return st;
     uint32_t* err = ptxstd::device_error_word();
     if (!err) return PTXSTD_ECUDA;
@@ -550,35 +704,62 @@ int launch_pair(const uint8_t* d_a, const uint8_t* d_sfa, const uint8_t* d_b,
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(kPThreads);
     cfg.dynamicSmemBytes = kSmemPairBytes;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    static int max_pairs[64] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PTXSTD_ECUDA;
-    if (max_pairs[dev] == 0) {
-        cfg.gridDim = dim3(2 * static_cast<uint32_t>(ptxstd::sm_count() / 2));
-        int clusters = 0;
-        if (cudaOccupancyMaxActiveClusters(&clusters, gemm_nvfp4_pair_kernel, &cfg) !=
-                cudaSuccess ||
-            clusters <= 0)
-            return PTXSTD_ECUDA;
-        max_pairs[dev] = clusters;
+    const uint64_t tiles = static_cast<uint64_t>(M / P_BM) * static_cast<uint64_t>(N / P_BN);
+    if (2 * tiles >= (1ull << 31)) return PTXSTD_EINVAL;
+    cudaError_t e;
+    if (dynamic) {
+        // one cluster per tile: the clusters that run first take over the tiles of those that
+        // have not started (cluster launch control), so no tile waits for one particular pair
+        cfg.gridDim = dim3(static_cast<uint32_t>(2 * tiles));
+        e = cudaLaunchKernelEx(&cfg, gemm_nvfp4_pair_kernel<true>, ta, tb, tsa, tsb, tc,
+                               static_cast<uint32_t>(M), static_cast<uint32_t>(N),
+                               static_cast<uint32_t>(K), alpha, err);
+    } else {
+        // persistent: as many pairs as can be resident at once, but no more than tiles
+        static int max_pairs[64] = {};
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return PTXSTD_ECUDA;
+        if (max_pairs[dev] == 0) {
+            cfg.gridDim = dim3(2 * static_cast<uint32_t>(ptxstd::sm_count() / 2));
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, gemm_nvfp4_pair_kernel<false>, &cfg) !=
+                    cudaSuccess ||
+                clusters <= 0)
+                return PTXSTD_ECUDA;
+            max_pairs[dev] = clusters;
+        }
+        const uint64_t pairs = tiles < static_cast<uint64_t>(max_pairs[dev])
+                                   ? tiles
+                                   : static_cast<uint64_t>(max_pairs[dev]);
+        cfg.gridDim = dim3(static_cast<uint32_t>(2 * pairs));
+        e = cudaLaunchKernelEx(&cfg, gemm_nvfp4_pair_kernel<false>, ta, tb, tsa, tsb, tc,
+                               static_cast<uint32_t>(M), static_cast<uint32_t>(N),
+                               static_cast<uint32_t>(K), alpha, err);
     }
-    const uint32_t tiles = static_cast<uint32_t>((M / P_BM) * (N / P_BN));
-    const uint32_t pairs =
-        tiles < static_cast<uint32_t>(max_pairs[dev]) ? tiles : static_cast<uint32_t>(max_pairs[dev]);
-    cfg.gridDim = dim3(2 * pairs);
-    if (cudaLaunchKernelEx(&cfg, gemm_nvfp4_pair_kernel, ta, tb, tsa, tsb, tc,
-                           static_cast<uint32_t>(M), static_cast<uint32_t>(N),
-                           static_cast<uint32_t>(K), alpha, err) != cudaSuccess)
-        return PTXSTD_ECUDA;
+    if (e != cudaSuccess) return PTXSTD_ECUDA;
     return ptxstd::launch_status();
 }
 
 }  // namespace
+
+// Process-wide choice of tile schedule for the persistent CTA-pair GEMMs.
+namespace {
+std::atomic<int> g_gemm_schedule{PTXSTD_SCHEDULE_PERSISTENT};
+}  // namespace
+
+extern "C" int ptxstd_set_gemm_schedule(int schedule) {
+    if (schedule != PTXSTD_SCHEDULE_PERSISTENT && schedule != PTXSTD_SCHEDULE_DYNAMIC)
+        return PTXSTD_EINVAL;
+    g_gemm_schedule.store(schedule);
+    return PTXSTD_OK;
+}
+
+extern "C" int ptxstd_get_gemm_schedule(void) { return g_gemm_schedule.load(); }
 
 extern "C" int ptxstd_gemm_nvfp4(const uint8_t* d_a, const uint8_t* d_sfa, float ga,
                                  const uint8_t* d_b, const uint8_t* d_sfb, float gb,

@@ -109,6 +109,8 @@ _SIGS = {
                                            C.c_void_p]),
     "ptxstd_gemm_fp8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_float, C.c_float, C.c_void_p,
                                   C.c_int64, C.c_int64, C.c_int64, C.c_void_p]),
+    "ptxstd_set_gemm_schedule": (C.c_int, [C.c_int]),
+    "ptxstd_get_gemm_schedule": (C.c_int, []),
     "ptxstd_gemm_nvfp4": (C.c_int, [C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p,
                                     C.c_float, C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
                                     C.c_void_p]),
@@ -213,6 +215,7 @@ def last_device_error(clear: bool = True, stream=None) -> tuple[int, int]:
 
 from . import data_types, tcgen05  # noqa: E402
 from .kernels import (MX_E2M1, MX_E2M3, MX_E3M2, MX_E4M3, MX_E5M2,  # noqa: E402
+                      SCHEDULE_DYNAMIC, SCHEDULE_PERSISTENT, get_gemm_schedule, set_gemm_schedule,
                       gemm_decode, gemm_fp8, gemm_mx, gemm_mxfp8, gemm_mxfp8_sparse, gemm_nvfp4,
                       prune_24, quantize_mx, quantize_mxfp8, quantize_nvfp4,
                       tcgen05_cp_unpack)
@@ -220,5 +223,6 @@ from .kernels import (MX_E2M1, MX_E2M3, MX_E3M2, MX_E4M3, MX_E5M2,  # noqa: E402
 __all__ = ["lib", "check", "PtxStdError", "status_string", "last_device_error", "data_types",
            "tcgen05", "quantize_mxfp8", "quantize_nvfp4", "quantize_mx", "gemm_fp8",
            "gemm_mxfp8", "gemm_mx", "gemm_nvfp4", "gemm_decode", "gemm_mxfp8_sparse", "prune_24",
-           "tcgen05_cp_unpack",
+           "tcgen05_cp_unpack", "set_gemm_schedule", "get_gemm_schedule", "SCHEDULE_PERSISTENT",
+           "SCHEDULE_DYNAMIC",
            "MX_E4M3", "MX_E5M2", "MX_E2M3", "MX_E3M2", "MX_E2M1"]

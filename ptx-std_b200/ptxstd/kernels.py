@@ -160,6 +160,20 @@ def gemm_mxfp8_sparse(vals, meta, sfa, b, sfb, out=None, stream=None):
     return c
 
 
+SCHEDULE_PERSISTENT, SCHEDULE_DYNAMIC = 0, 1
+
+
+def set_gemm_schedule(schedule: int) -> None:
+    """Tile schedule of the CTA-pair NVFP4 GEMM for later calls, process-wide:
+    SCHEDULE_PERSISTENT (default, a fixed raster over resident pairs) or SCHEDULE_DYNAMIC
+    (one cluster per tile; running pairs take over tiles of clusters not yet started)."""
+    check(lib().ptxstd_set_gemm_schedule(int(schedule)), "set_gemm_schedule")
+
+
+def get_gemm_schedule() -> int:
+    return int(lib().ptxstd_get_gemm_schedule())
+
+
 def gemm_nvfp4(a, sfa, ga: float, b, sfb, gb: float, out=None, stream=None):
     """NVFP4 a [M, K/2], b [N, K/2] (uint8, E2M1x2) with blocked E4M3 scales -> bf16 [M, N]."""
     torch = _torch()

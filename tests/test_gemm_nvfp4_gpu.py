@@ -22,6 +22,15 @@ TOL_ACC = 2.0 ** -10
 TOL_OUT = 2.0 ** -8
 
 
+@pytest.fixture(autouse=True, params=[0, 1], ids=["persistent", "dynamic"])
+def schedule(request, ptxstd_lib):
+    """Every case runs under both tile schedules of the CTA-pair kernel: the persistent raster
+    and the cluster-launch-control schedule (one cluster per tile, tiles taken over)."""
+    ptxstd_lib.set_gemm_schedule(request.param)
+    yield request.param
+    ptxstd_lib.set_gemm_schedule(0)
+
+
 def to_blocked(sf: np.ndarray) -> np.ndarray:
     """Row-major [rows, S] scales -> the blocked 128x4 layout (rows % 128 == 0, S % 4 == 0)."""
     rows, S = sf.shape

@@ -48,3 +48,17 @@ def test_mx_type_names(ptxstd_lib):
     assert kernels.MX_TYPES == {"e4m3": 0, "e5m2": 1, "e2m3": 3, "e3m2": 4, "e2m1": 5}
     assert (ptxstd.MX_E4M3, ptxstd.MX_E5M2, ptxstd.MX_E2M3, ptxstd.MX_E3M2,
             ptxstd.MX_E2M1) == (0, 1, 3, 4, 5)
+
+
+def test_gemm_schedule_setting(ptxstd_lib):
+    """The tile-schedule setting round-trips and rejects unknown values (no device needed)."""
+    import ptxstd
+    assert ptxstd.get_gemm_schedule() == ptxstd.SCHEDULE_PERSISTENT
+    try:
+        ptxstd.set_gemm_schedule(ptxstd.SCHEDULE_DYNAMIC)
+        assert ptxstd.get_gemm_schedule() == ptxstd.SCHEDULE_DYNAMIC
+        with pytest.raises(ptxstd.PtxStdError):
+            ptxstd.set_gemm_schedule(2)
+        assert ptxstd.get_gemm_schedule() == ptxstd.SCHEDULE_DYNAMIC
+    finally:
+        ptxstd.set_gemm_schedule(ptxstd.SCHEDULE_PERSISTENT)
