@@ -316,7 +316,10 @@ PTXSTD_API int ptxstd_gemm_mxfp8_sparse(const uint8_t* d_vals, const uint8_t* d_
  * (src/tcgen05/mma.rs:434-453), fp32 accumulation. N % 128 == 0, K % 256 == 0.
  * workspace: device scratch of ptxstd_gemm_decode_workspace_bytes(M, N, K) bytes, 1024-byte
  * aligned, owned by the caller; the call initialises it itself (no zeroing needed). Calls that
- * share a workspace must be stream-ordered. */
+ * share a workspace must be stream-ordered. The size depends on the current device's SM count
+ * (two 8 KiB partial-sum slots per SM, plus the quantised x and N/128 counters), so query it
+ * with the device current that will run the calls. The result is bitwise reproducible: a weight
+ * block split between CTAs is summed from their partials in a fixed order. */
 PTXSTD_API size_t ptxstd_gemm_decode_workspace_bytes(int64_t M, int64_t N, int64_t K);
 PTXSTD_API int ptxstd_gemm_decode(const uint16_t* d_x, const uint8_t* d_w, const uint8_t* d_sfw,
                                   float gw, uint16_t* d_y, int64_t M, int64_t N, int64_t K,

@@ -13,9 +13,10 @@
 //     applied to the fp32 result.
 // The op is weight-streaming (HBM-bound): each W byte is read once.
 //
-// Kernel 1, decode_prep (one CTA per token row plus CTAs that clear the split-K scratch):
+// Kernel 1, decode_prep (one CTA per token row; CTA 0 also clears the per-block counters):
 //   MXFP8-quantises x and writes the f16 B operand pre-swizzled (K-major, 128-byte swizzle, 8 KiB
-//   per 256-K stage) so that the main kernel fetches it with one 1-D bulk copy per stage.
+//   per 256-K stage) so that the main kernel fetches it with one 1-D bulk copy per stage. Its 16
+//   CTAs leave the other SMs free, so the main kernel's weight stream starts at once.
 // Kernel 2, gemm_decode (persistent, one CTA per SM, launched with programmatic dependent launch so
 //   its setup and first weight loads overlap kernel 1):
 //   work = (128-row W block, 256-K stage) units split evenly over the CTAs ("stream-K");
@@ -30,11 +31,13 @@
 //           quarter in kTeams teams that take the units in turn, each warp a 64 * kSubs-element
 //           K slice of its team's units; three A buffers);
 //   warps kEpiWarp .. kEpiWarp + 3 (one per lane quarter): at the end of each W-block segment,
-//           drain the accumulator and reduce the 128 x 16 fp32 partial into the scratch with
-//           red.global.add.v4.f32, off the dequant / MMA path (the MMA already fills the other
-//           accumulator). A per-block counter of finished K stages elects the CTA that completes a
-//           block; its epilogue warps convert the block to bf16, transpose it through shared
-//           memory and write y in 16-byte row chunks.
+//           drain the accumulator, off the dequant / MMA path (the MMA already fills the other
+//           accumulator). A block that lies inside this CTA's range is converted to bf16 straight
+//           from registers, transposed through shared memory and written to y in 16-byte row
+//           chunks. A block shared with neighbouring CTAs is written as an fp32 partial to this
+//           CTA's slot; a per-block counter elects the CTA that arrives last, which sums the
+//           partials of all contributors in CTA order (so the result is the same bits whichever
+//           CTA is last) and writes y the same way.
 // Output routing (decode_out.h): one local y, or, for the N-sharded multi-GPU path, the y of every
 // rank over NVLink (the epilogue's stores go to each rank's copy; counters and bounded waits order
 // the steps; kernel 3, decode_done, waits until every rank's pieces have arrived).
@@ -88,12 +91,16 @@ static_assert(kDCol + kDBufs * kTok <= 512, "TMEM budget");
 static_assert(kTeams <= kABufs && WST % kTeams == 0, "team count vs. A buffers and weight ring");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kPrepThreads = 256;
+constexpr uint32_t kFinMax = 5;  // contributors of a shared block staged in shared memory at once
 
 struct alignas(1024) Smem {
     uint8_t w[WST][kWStageBytes];
     uint8_t x[XST][kXStageBytes];
     uint8_t sf[WST][kSfStageBytes];
+    // finishing a shared block: up to kFinMax contributors' partial rows, fetched at once
+    float4 fin[kFinMax][BM][kTok / 4];
     uint16_t ytile[4][kTok][32];  // per epilogue warp: its 32 block columns x 16 tokens, bf16
+    float fac[4][kTok];           // per epilogue warp: token factors x gw (kept out of registers)
     uint64_t wfull[WST];
     uint64_t wempty[WST];
     uint64_t xfull[XST];
@@ -115,22 +122,62 @@ static_assert(kSmemBytes <= 232448, "shared memory budget");
 enum : uint32_t { kDetailProducer = 0x3100, kDetailMma = 0x3200, kDetailDq = 0x3300,
                   kDetailXProducer = 0x3400, kDetailEpi = 0x3500 };
 
-// Workspace layout (bytes): y32 [N][16] f32 | counters [N/128] u32 (16 B aligned) |
-// x image [K/256][8 KiB] | factors [16] f32.
+// Workspace layout (bytes), for a grid of G CTAs:
+//   partial slots [G][2][128 rows][16 tokens] f32: the fp32 partial sums of the W blocks that a
+//     CTA shares with its neighbours (slot 0: its first segment, slot 1: its last one);
+//   counters [N/128] u32 (1024-byte aligned end): per block, the contributors that have arrived;
+//   x image [K/256][8 KiB]; factors [16] f32.
+// Only the counters must start at zero, and decode_prep clears them (N/128 words) on every call;
+// a slot is always written before it is read.
+constexpr size_t kSlotBytes = static_cast<size_t>(BM) * kTok * 4;  // 8 KiB
 struct Workspace {
-    float* y32;
+    float* slots;
     uint32_t* counters;
     uint8_t* ximg;
     float* factors;
 };
-__host__ __device__ inline size_t ws_counters_off(size_t N) { return N * kTok * 4; }
-__host__ __device__ inline size_t ws_ximg_off(size_t N) {
-    return ws_counters_off(N) + (((N / BM) * 4 + 1023) & ~static_cast<size_t>(1023));
+__host__ __device__ inline size_t ws_counters_off(size_t G) { return G * 2 * kSlotBytes; }
+__host__ __device__ inline size_t ws_ximg_off(size_t G, size_t N) {
+    return ws_counters_off(G) + (((N / BM) * 4 + 1023) & ~static_cast<size_t>(1023));
 }
-__host__ __device__ inline size_t ws_factors_off(size_t N, size_t K) {
-    return ws_ximg_off(N) + K * kTok * 2;
+__host__ __device__ inline size_t ws_factors_off(size_t G, size_t N, size_t K) {
+    return ws_ximg_off(G, N) + K * kTok * 2;
 }
-__host__ __device__ inline size_t ws_bytes(size_t N, size_t K) { return ws_factors_off(N, K) + 64; }
+__host__ __device__ inline size_t ws_bytes(size_t G, size_t N, size_t K) {
+    return ws_factors_off(G, N, K) + 64;
+}
+__host__ __device__ inline Workspace ws_layout(uint8_t* ws, size_t G, size_t N, size_t K) {
+    return Workspace{reinterpret_cast<float*>(ws),
+                     reinterpret_cast<uint32_t*>(ws + ws_counters_off(G)),
+                     ws + ws_ximg_off(G, N),
+                     reinterpret_cast<float*>(ws + ws_factors_off(G, N, K))};
+}
+
+// Stream-K bookkeeping: unit u of U = (N/128) * (K/256) is (block u / S, stage u % S); CTA c of G
+// owns [floor(U c / G), floor(U (c + 1) / G)), so unit u belongs to CTA floor((u G + G - 1) / U).
+__host__ __device__ inline uint64_t unit_begin(uint64_t U, uint64_t G, uint64_t c) {
+    return U * c / G;
+}
+__host__ __device__ inline uint32_t unit_owner(uint64_t U, uint64_t G, uint64_t u) {
+    return static_cast<uint32_t>((u * G + G - 1) / U);
+}
+
+// Host side: CTAs of the GEMM kernel on the current device: one per SM, but at least
+// kMinUnitsPerCta units each, which bounds how many CTAs share a block (and so how many partials
+// the last of them reads back) when there is little work.
+// With K = 8192 (32 units per block), 8 units per CTA keep a shared block to at most 5
+// contributors, which the finishing CTA fetches in one round trip (kFinMax). Measured on a B200
+// against one CTA per SM at M = 16, K = 8192: N = 3584 12.2 us (13.5 before), N = 1024 12.0 us
+// (10.4); at N >= 7168 every SM gets more than 8 units anyway.
+constexpr size_t kMinUnitsPerCta = 8;
+inline size_t decode_grid(size_t N, size_t K) {
+    const size_t units = (N / BM) * (K / BKS);
+    const size_t sms = static_cast<size_t>(ptxstd::sm_count());
+    size_t g = units / kMinUnitsPerCta;
+    if (g < 1) g = 1;
+    return g < sms ? g : sms;
+}
+inline size_t decode_ws_bytes(size_t N, size_t K) { return ws_bytes(decode_grid(N, K), N, K); }
 
 // Byte offset of f16 element (row r < 16, k) in the x image: per 256-K stage 8 KiB made of four
 // 64-element K atoms of 16 rows x 128 bytes, 16-byte chunks XOR-swizzled by row % 8.
@@ -142,11 +189,12 @@ __device__ __forceinline__ uint32_t ximg_offset(uint32_t r, uint32_t k) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Kernel 1: x -> MXFP8 -> f16 B-operand image, per-row factors; clears y32 and the counters.
-// Blocks 0..15 handle token rows (rows >= M write zeros); the rest clear the scratch.
+// Kernel 1: x -> MXFP8 -> f16 B-operand image and per-row factors, one CTA per token row (rows
+// >= M write zeros); CTA 0 also clears the block counters. Sixteen small CTAs leave the other SMs
+// to the GEMM kernel, whose weight stream starts while this one runs.
 __global__ void __launch_bounds__(kPrepThreads)
     decode_prep_kernel(const uint16_t* __restrict__ x, uint32_t M, uint32_t K, uint8_t* ws,
-                       uint32_t N, const ptxstd::decode::Out out) {
+                       uint32_t N, uint32_t G, const ptxstd::decode::Out out) {
     asm volatile("griddepcontrol.launch_dependents;");
     if (out.nranks != 0 && blockIdx.x == 0 && threadIdx.x < out.nranks) {
         // peer-to-peer output: this rank starts a step (see decode_out.h)
@@ -154,19 +202,9 @@ __global__ void __launch_bounds__(kPrepThreads)
         if (threadIdx.x == 0) out.sig[out.rank][pd::kSigStep] += 1u;
         atomicAdd_system(out.sig[threadIdx.x] + pd::kSigReady + out.rank, 1u);
     }
-    Workspace w{reinterpret_cast<float*>(ws),
-                reinterpret_cast<uint32_t*>(ws + ws_counters_off(N)), ws + ws_ximg_off(N),
-                reinterpret_cast<float*>(ws + ws_factors_off(N, K))};
-    if (blockIdx.x >= kTok) {
-        // clear y32 (N*16 floats) and counters with 16-byte stores
-        const size_t n4 = static_cast<size_t>(N) * kTok / 4;
-        const size_t nthr = static_cast<size_t>(gridDim.x - kTok) * blockDim.x;
-        const size_t tid = static_cast<size_t>(blockIdx.x - kTok) * blockDim.x + threadIdx.x;
-        for (size_t i = tid; i < n4; i += nthr)
-            reinterpret_cast<float4*>(w.y32)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (size_t i = tid; i < N / BM; i += nthr) w.counters[i] = 0;
-        return;
-    }
+    const Workspace w = ws_layout(ws, G, N, K);
+    if (blockIdx.x == 0)
+        for (uint32_t i = threadIdx.x; i < N / BM; i += blockDim.x) w.counters[i] = 0;
     const uint32_t r = blockIdx.x;
     __shared__ uint32_t red[kPrepThreads / 32];
     const uint32_t nblk = K / 32;
@@ -286,6 +324,16 @@ __device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t* v) {
 __device__ __forceinline__ void tmem_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+// 16-byte asynchronous copy global (L2) -> this thread's shared memory, and the wait for all of
+// this thread's copies: the partial rows of a shared block are all in flight at once.
+__device__ __forceinline__ void cp_async_16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ptxstd::smem_u32(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
 // A from TMEM: tcgen05.mma.cta_group::1.kind::f16 [d], [a], b_desc, idesc.
 __device__ __forceinline__ void mma_f16_tmem_a(uint32_t d, uint32_t a, uint64_t bdesc,
                                                uint32_t idesc, uint32_t accumulate) {
@@ -295,12 +343,6 @@ __device__ __forceinline__ void mma_f16_tmem_a(uint32_t d, uint32_t a, uint64_t 
         "r"(a), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
-    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b),
-                 "f"(c), "f"(d)
-                 : "memory");
-}
-
 // Bounded wait until a peer-written counter reaches `target` (wrap-safe), acquire at system scope.
 __device__ __forceinline__ bool wait_counter(const uint32_t* p, uint32_t target) {
     const uint64_t t0 = ptxstd::global_timer();
@@ -331,9 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t U = static_cast<uint64_t>(N / BM) * S;
     uint32_t u0, u1;
     unit_range(U, u0, u1);
-    Workspace wsp{reinterpret_cast<float*>(ws),
-                  reinterpret_cast<uint32_t*>(ws + ws_counters_off(N)), ws + ws_ximg_off(N),
-                  reinterpret_cast<float*>(ws + ws_factors_off(N, K))};
+    const Workspace wsp = ws_layout(ws, gridDim.x, N, K);
 
     if (warp == 0 && lane == 0) {
         ptxstd::prefetch_tensormap(&tmW);
@@ -553,10 +593,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("griddepcontrol.wait;" ::: "memory");
         const uint32_t q = warp & 3u;
         const uint32_t row = 32 * q + lane;                    // W row of the block (TMEM lane)
-        const uint32_t col = (warp - kEpiWarp) * 32 + lane;    // block column this thread writes
-        float fac[kTok];
-#pragma unroll
-        for (uint32_t t = 0; t < kTok; ++t) fac[t] = __ldcg(wsp.factors + t) * gw;
+        // the token factors times gw, in shared memory rather than in 16 registers
+        float* fac = s.fac[warp - kEpiWarp];
+        if (lane < kTok) fac[lane] = __ldcg(wsp.factors + lane) * gw;
+        __syncwarp();
         namespace pd = ptxstd::decode;
         if (out.nranks != 0) {
             // Peer-to-peer output: every rank's stream has passed its readers of the previous
@@ -573,11 +613,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         uint32_t dbuf = 0, dphase = 0, sphase = 0;
         const uint32_t e = warp - kEpiWarp;
+        const uint32_t G = gridDim.x, c = blockIdx.x;
         for (uint32_t u = u0; u < u1;) {
             // one W-block segment: units u .. end - 1 of block nb
             const uint32_t nb = u / S;
             const uint32_t end = min(u1, (nb + 1) * S);
-            const uint32_t seg_len = end - u;
             u = end;
             bool ok = mbar_wait(&s.dfull[dbuf], dphase);
             ok = __all_sync(0xffffffffu, ok);
@@ -596,61 +636,102 @@ __global__ void __launch_bounds__(kThreads, 1)
                 dbuf = 0;
                 dphase ^= 1u;
             }
-            // this row's 16 token partials
-            float* dst = wsp.y32 + (static_cast<size_t>(nb) * BM + row) * kTok;
+            // this row's 16 token sums over the segment, with the token factors applied
+            float p[kTok];
 #pragma unroll
-            for (uint32_t t = 0; t < kTok; t += 4)
-                red_add_v4(dst + t, __uint_as_float(acc[t]) * fac[t],
-                           __uint_as_float(acc[t + 1]) * fac[t + 1],
-                           __uint_as_float(acc[t + 2]) * fac[t + 2],
-                           __uint_as_float(acc[t + 3]) * fac[t + 3]);
-            ptxstd::fence_acq_rel_gpu();
-            __syncwarp();
-            // All four warps have reduced (segA), then the first publishes the finished stages
-            // and tells the others whether this CTA completes the block (segB). mbarriers rather
-            // than bar.sync so that every wait stays bounded.
-            if (lane == 0) ptxstd::mbar_arrive(&s.segA);
-            if (warp == kEpiWarp) {
-                bool okA = mbar_wait(&s.segA, sphase);
-                okA = __all_sync(0xffffffffu, okA);
-                if (!okA) {
-                    if (lane == 0) fail(s, err, kDetailEpi | 0x20);
+            for (uint32_t t = 0; t < kTok; ++t) p[t] = __uint_as_float(acc[t]) * fac[t];
+            // CTAs c_first .. c_last contribute to block nb; a block that lies inside one CTA's
+            // range is stored straight from these registers
+            const uint64_t b0 = static_cast<uint64_t>(nb) * S;
+            const uint32_t c_first = unit_owner(U, G, b0), c_last = unit_owner(U, G, b0 + S - 1);
+            bool store = c_first == c_last;
+            if (!store) {
+                // A shared block: this CTA's partial goes to its slot (0 for the segment its range
+                // starts in, 1 otherwise); the CTA that arrives last sums every contributor's
+                // partial in the order c_first .. c_last, so the result does not depend on which
+                // CTA finishes last.
+                const uint32_t side = unit_begin(U, G, c) >= b0 ? 0u : 1u;
+                float4* slot = reinterpret_cast<float4*>(
+                    wsp.slots + ((static_cast<size_t>(c) * 2 + side) * BM + row) * kTok);
+#pragma unroll
+                for (uint32_t i = 0; i < kTok / 4; ++i)
+                    __stcg(slot + i, make_float4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]));
+                ptxstd::fence_acq_rel_gpu();
+                __syncwarp();
+                // All four warps have written (segA); the first counts this CTA in and tells the
+                // others whether it completes the block (segB). mbarriers rather than bar.sync so
+                // that every wait stays bounded.
+                if (lane == 0) ptxstd::mbar_arrive(&s.segA);
+                if (warp == kEpiWarp) {
+                    bool okA = mbar_wait(&s.segA, sphase);
+                    okA = __all_sync(0xffffffffu, okA);
+                    if (!okA) {
+                        if (lane == 0) fail(s, err, kDetailEpi | 0x20);
+                        break;
+                    }
+                    if (lane == 0) {
+                        const uint32_t before = atomicAdd(wsp.counters + nb, 1u);
+                        *reinterpret_cast<volatile uint32_t*>(&s.finalize) =
+                            (before + 1 == c_last - c_first + 1) ? 1u : 0u;
+                        ptxstd::mbar_arrive(&s.segB);
+                    }
+                }
+                bool okB = mbar_wait(&s.segB, sphase);
+                okB = __all_sync(0xffffffffu, okB);
+                if (!okB) {
+                    if (lane == 0) fail(s, err, kDetailEpi | 0x30);
                     break;
                 }
-                if (lane == 0) {
-                    const uint32_t before = atomicAdd(wsp.counters + nb, seg_len);
-                    *reinterpret_cast<volatile uint32_t*>(&s.finalize) =
-                        (before + seg_len == S) ? 1u : 0u;
-                    ptxstd::mbar_arrive(&s.segB);
+                sphase ^= 1u;
+                store = *reinterpret_cast<volatile uint32_t*>(&s.finalize) != 0u;
+                if (store) {
+                    ptxstd::fence_acq_rel_gpu();
+                    float sum[kTok];
+#pragma unroll
+                    for (uint32_t t = 0; t < kTok; ++t) sum[t] = 0.0f;
+                    // every contributor's partial from its slot, this CTA's own included, added
+                    // in contributor order; up to kFinMax rows at a time are fetched together
+                    // into this thread's shared-memory staging rows, so they cost one round trip
+                    for (uint32_t cb = c_first; cb <= c_last; cb += kFinMax) {
+                        const uint32_t nc = min(kFinMax, c_last - cb + 1);
+                        for (uint32_t j = 0; j < nc; ++j) {
+                            const uint32_t cc = cb + j;
+                            const uint32_t sd = unit_begin(U, G, cc) >= b0 ? 0u : 1u;
+                            const float4* src = reinterpret_cast<const float4*>(
+                                wsp.slots + ((static_cast<size_t>(cc) * 2 + sd) * BM + row) * kTok);
+#pragma unroll
+                            for (uint32_t i = 0; i < kTok / 4; ++i)
+                                cp_async_16(&s.fin[j][row][i], src + i);
+                        }
+                        cp_async_wait_all();
+                        for (uint32_t j = 0; j < nc; ++j) {
+#pragma unroll
+                            for (uint32_t i = 0; i < kTok / 4; ++i) {
+                                const float4 f = s.fin[j][row][i];
+                                sum[4 * i] += f.x;
+                                sum[4 * i + 1] += f.y;
+                                sum[4 * i + 2] += f.z;
+                                sum[4 * i + 3] += f.w;
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (uint32_t t = 0; t < kTok; ++t) p[t] = sum[t];
                 }
             }
-            bool okB = mbar_wait(&s.segB, sphase);
-            okB = __all_sync(0xffffffffu, okB);
-            if (!okB) {
-                if (lane == 0) fail(s, err, kDetailEpi | 0x30);
-                break;
-            }
-            sphase ^= 1u;
-            if (*reinterpret_cast<volatile uint32_t*>(&s.finalize)) {
-                ptxstd::fence_acq_rel_gpu();
-                // column `col` of the block: its 16 token sums, as bf16, into this warp's tile
-                const float4* src = reinterpret_cast<const float4*>(
-                    wsp.y32 + (static_cast<size_t>(nb) * BM + col) * kTok);
+            if (store) {
+                // this warp's 32 block rows (= 32 output columns) x 16 tokens, as bf16, into its
+                // tile, then 16 tokens x 32 columns = 64 chunks of 8 columns; lane takes chunks lane
+                // and lane + 32 (token ch / 4, columns 8 (ch % 4) ..) -> 16-byte stores into y[t][..]
+                // of every output (this GPU's only, or every rank's over NVLink)
 #pragma unroll
-                for (uint32_t i = 0; i < kTok / 4; ++i) {
-                    const float4 f = __ldcg(src + i);
-                    const uint32_t p0 = dt::bf16x2_from_f32(f.x, f.y);
-                    const uint32_t p1 = dt::bf16x2_from_f32(f.z, f.w);
-                    s.ytile[e][4 * i + 0][lane] = static_cast<uint16_t>(p0);
-                    s.ytile[e][4 * i + 1][lane] = static_cast<uint16_t>(p0 >> 16);
-                    s.ytile[e][4 * i + 2][lane] = static_cast<uint16_t>(p1);
-                    s.ytile[e][4 * i + 3][lane] = static_cast<uint16_t>(p1 >> 16);
+                for (uint32_t t = 0; t < kTok; t += 2) {
+                    const uint32_t pk = dt::bf16x2_from_f32(p[t], p[t + 1]);
+                    s.ytile[e][t][lane] = static_cast<uint16_t>(pk);
+                    s.ytile[e][t + 1][lane] = static_cast<uint16_t>(pk >> 16);
                 }
                 __syncwarp();
-                // 16 tokens x 32 columns = 64 chunks of 8 columns; lane takes chunks lane and
-                // lane + 32 (token ch / 4, columns 8 (ch % 4) ..) -> 16-byte stores into y[t][..]
-                // of every output (this GPU's only, or every rank's over NVLink)
-                const size_t c0 = out.col0 + static_cast<size_t>(nb) * BM + 32 * e;
+                const size_t c0 = out.col0 + static_cast<size_t>(nb) * BM + 32 * q;
                 const uint32_t nout = out.nranks != 0 ? out.nranks : 1u;
 #pragma unroll
                 for (uint32_t h = 0; h < 2; ++h) {
@@ -665,7 +746,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     }
-
     t5::fence_before_thread_sync();
     __syncthreads();
     t5::fence_after_thread_sync();
@@ -706,14 +786,14 @@ int launch_decode(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float
     if (st) return st;
     uint32_t* err = ptxstd::device_error_word();
     if (!err) return PTXSTD_ECUDA;
-    const int sms = ptxstd::sm_count();
-    decode_prep_kernel<<<sms, kPrepThreads, 0, stream>>>(x, static_cast<uint32_t>(M),
+    const uint32_t grid = static_cast<uint32_t>(decode_grid(static_cast<size_t>(N),
+                                                             static_cast<size_t>(K)));
+    if (grid == 0) return PTXSTD_ECUDA;
+    decode_prep_kernel<<<kTok, kPrepThreads, 0, stream>>>(x, static_cast<uint32_t>(M),
                                                          static_cast<uint32_t>(K), ws,
-                                                         static_cast<uint32_t>(N), out);
+                                                         static_cast<uint32_t>(N), grid, out);
     st = ptxstd::launch_status();
     if (st) return st;
-    const uint64_t units = static_cast<uint64_t>(N / BM) * static_cast<uint64_t>(K / BKS);
-    const uint32_t grid = static_cast<uint32_t>(units < static_cast<uint64_t>(sms) ? units : sms);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
@@ -773,7 +853,7 @@ extern "C" {
 
 size_t ptxstd_gemm_decode_workspace_bytes(int64_t M, int64_t N, int64_t K) {
     if (M <= 0 || N <= 0 || K <= 0) return 0;
-    return ws_bytes(static_cast<size_t>(N), static_cast<size_t>(K));
+    return decode_ws_bytes(static_cast<size_t>(N), static_cast<size_t>(K));
 }
 
 int ptxstd_gemm_decode(const uint16_t* d_x, const uint8_t* d_w, const uint8_t* d_sfw, float gw,
@@ -781,7 +861,7 @@ int ptxstd_gemm_decode(const uint16_t* d_x, const uint8_t* d_w, const uint8_t* d
                        size_t workspace_bytes, ptxstd_stream stream) {
     if (check_args(d_x, d_w, d_sfw, gw, M, N, K, d_workspace) || !d_y || !ptxstd::aligned16(d_y))
         return PTXSTD_EINVAL;
-    if (workspace_bytes < ws_bytes(static_cast<size_t>(N), static_cast<size_t>(K)))
+    if (workspace_bytes < decode_ws_bytes(static_cast<size_t>(N), static_cast<size_t>(K)))
         return PTXSTD_EINVAL;
     return launch_decode(d_x, d_w, d_sfw, gw, local_out(d_y, N), M, N, K,
                          static_cast<uint8_t*>(d_workspace),
@@ -846,7 +926,7 @@ extern "C" int ptxstd_gemm_decode_noalloc(const uint16_t* d_x, const uint8_t* d_
         !ptxstd::aligned16(d_y))
         return PTXSTD_EINVAL;
     // The shape's scratch must fit the fixed array.
-    if (ws_bytes(static_cast<size_t>(N), static_cast<size_t>(K)) >
+    if (decode_ws_bytes(static_cast<size_t>(N), static_cast<size_t>(K)) >
         static_cast<size_t>(PTXSTD_DECODE_NOALLOC_SCRATCH_BYTES))
         return PTXSTD_EINVAL;
     void* scratch = nullptr;

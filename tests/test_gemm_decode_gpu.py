@@ -77,8 +77,9 @@ def test_small_all_outputs(cuda, oracle, M, N, K):
     y1, y2 = _run(cuda, x, W, sfW, gw, calls=2)
     r, c = np.meshgrid(np.arange(M), np.arange(N), indexing="ij")
     _check(oracle, x, W, sfW, gw, y1, r.ravel(), c.ravel())
-    # the second call on the same (re-initialised) workspace gives the same result
-    assert np.allclose(y1, y2, rtol=2.0 ** -7, atol=0)
+    # the second call on the same workspace gives the same bits: a block shared between CTAs is
+    # summed from their partials in a fixed order, whichever CTA finishes last
+    assert np.array_equal(y1, y2)
 
 
 def test_scaled_rows(cuda, oracle):
