@@ -45,7 +45,8 @@ def _check(oracle, A, B, sa, sb, Cg, rows, cols, plain=False):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 128), (128, 256, 1024), (256, 512, 256),
-                                   (384, 768, 640), (1024, 1024, 2048)])
+                                   (384, 768, 640), (512, 256, 128), (1536, 768, 384),
+                                   (1024, 1024, 2048)])
 def test_small_all_outputs(cuda, oracle, M, N, K):
     from ptxstd import workloads
     A = workloads.fp8_operand(M, K, seed=M + K)
