@@ -879,13 +879,20 @@ def time_steps(args, ctx, step, graph: bool):
     into a CUDA graph and replayed (after one untimed replay that uploads it), so that the device
     time is not padded by host-side launch gaps between short kernels; the multi-GPU decode's
     NCCL all-gather is issued by libptxstd on the same stream and is captured with it.
+    The clock sampler runs over the timed steps and over about 20 ms of untimed passes of the same
+    K steps just before them (the same number of passes on every rank). So the clock record is
+    taken under load, and the timed steps start on a busy GPU, not after an idle pause: after 20 ms
+    idle, the first steps of a short timed region ran about 3 % slower on a B200.
     Returns (device ms of the K steps, max over ranks; kernel launches; clock record)."""
     import torch
     dist = ctx.dist
     stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+    one_pass = (time.perf_counter() - t0) / max(args.warmup, 1) * args.steps
     g = None
     launches = 0
     if graph:
@@ -894,12 +901,21 @@ def time_steps(args, ctx, step, graph: bool):
             for i in range(args.steps):
                 launches += step(i)
         torch.cuda.synchronize()
-        g.replay()
+        t0 = time.perf_counter()
+        g.replay()  # uploads the graph
         torch.cuda.synchronize()
+        one_pass = time.perf_counter() - t0
+    # untimed passes before the timed one: ~20 ms, the largest count any rank asks for
+    pre = int(dist.max(float(min(50, max(1, int(0.02 / max(one_pass, 1e-6)) + 1)))))
     sampler = ClockSampler(torch.cuda.current_device()) if dist.rank == 0 else None
     if sampler:
         sampler.start()
-        time.sleep(0.02)
+    for _ in range(pre):
+        if g is not None:
+            g.replay()
+        else:
+            for i in range(args.steps):
+                step(i)
     dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -301,26 +301,6 @@ __device__ __forceinline__ uint32_t bf16x2_fold(uint32_t m2) {
     return max(m2 & 0xFFFFu, m2 >> 16);
 }
 
-// The same amax on the packed float path, which the quantisers use because it issues fewer
-// integer instructions: max.NaN.xorsign.abs.bf16x2 gives each half max(|a|, |b|), and gives a NaN
-// when either operand is NaN. The sign bit (the XOR of the operands' signs) is noise, which
-// bf16x2_absmax_fold masks off. Against the integer form above, the only difference is which NaN
-// pattern a block with a NaN yields. Every consumer of the amax (the UE8M0 and E4M3 scale
-// conversions) maps all NaN patterns to the same code.
-__device__ __forceinline__ uint32_t bf16x2_absmax2(uint32_t a, uint32_t b) {
-    uint32_t r;
-    asm("max.NaN.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
-    return r;
-}
-// The eight values of a 16-byte vector; both halves are still packed.
-__device__ __forceinline__ uint32_t bf16x8_absmax2(const uint4& v) {
-    return bf16x2_absmax2(bf16x2_absmax2(v.x, v.y), bf16x2_absmax2(v.z, v.w));
-}
-// Both halves folded into one: the |amax| bits in the low 16 bits.
-__device__ __forceinline__ uint32_t bf16x2_absmax_fold(uint32_t m2) {
-    return bf16x2_absmax2(m2, __byte_perm(m2, 0u, 0x1032u)) & 0x7FFFu;
-}
-
 // 2^-(code-127) as f32 for a UE8M0 scale code (2^127 .. 2^-127, the last an f32 subnormal);
 // NaN for the NaN code 0xff.
 __device__ __forceinline__ float ue8m0_inverse(uint32_t code) {
@@ -328,26 +308,6 @@ __device__ __forceinline__ float ue8m0_inverse(uint32_t code) {
     const int e = 127 - static_cast<int>(code);
     return e >= -126 ? __uint_as_float(static_cast<uint32_t>(e + 127) << 23)
                      : __uint_as_float(0x00400000u);
-}
-// The same value as bf16 bits. bf16 has f32's exponent range, so 2^127 .. 2^-126 are normal, and
-// 2^-127 is the bf16 subnormal 0x0040. The NaN code gives a NaN.
-__device__ __forceinline__ uint32_t ue8m0_inverse_bf16(uint32_t code) {
-    if (code == 0xFFu) return 0x7FC0u;
-    return code <= 253u ? (254u - code) << 7 : 0x0040u;
-}
-
-// Both bf16 halves of `w` multiplied by the bf16 power of two `s` (ue8m0_inverse_bf16), giving
-// f32 products; .x is the low half (element 0). This uses sm_100's mixed-precision
-// fma.rn.f32.bf16 as a * s + (-0), so the halves need no widening first. The result is the same
-// single RN rounding of the same exact product that bf16x2_mul_f32 computes with the f32 scale.
-// Adding -0 keeps the sign of a zero product.
-__device__ __forceinline__ float2 bf16x2_mul_pow2(uint32_t w, uint32_t s) {
-    float lo, hi;
-    asm("{\n\t.reg .b16 a0, a1, s0, s1;\n\tmov.b32 {a0, a1}, %2;\n\tmov.b32 {s0, s1}, %3;\n\t"
-        "fma.rn.f32.bf16 %0, a0, s0, 0f80000000;\n\tfma.rn.f32.bf16 %1, a1, s0, 0f80000000;\n\t}"
-        : "=f"(lo), "=f"(hi)
-        : "r"(w), "r"(s));
-    return make_float2(lo, hi);
 }
 
 // MXFP8 scale code of a block from its amax: from_f32::<TowardZero, SaturateFinite>(amax) minus

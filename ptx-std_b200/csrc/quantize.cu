@@ -81,17 +81,17 @@ struct Mxfp8 {
     float six_g;  // unused
     __device__ __forceinline__ void operator()(const uint4 v, bool valid, size_t gv, uint32_t lane,
                                                uint8_t* q, uint8_t* sf, size_t sf_cols) const {
-        uint32_t m2 = dt::bf16x8_absmax2(v);
-        m2 = dt::bf16x2_absmax2(m2, __shfl_xor_sync(0xffffffffu, m2, 1));
-        m2 = dt::bf16x2_absmax2(m2, __shfl_xor_sync(0xffffffffu, m2, 2));
-        const uint32_t m = dt::bf16x2_absmax_fold(m2);
+        uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                              dt::bf16x2_absmax_bits(v.z, v.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
         const uint32_t code = dt::mxfp8_scale_code(__uint_as_float(m << 16));
-        const uint32_t inv = dt::ue8m0_inverse_bf16(code);
+        const float inv = dt::ue8m0_inverse(code);
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         uint32_t p[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const float2 f = dt::bf16x2_mul_pow2(w[k], inv);
+            const float2 f = dt::bf16x2_mul_f32(w[k], inv);
             p[k] = dt::e4m3x2_from_f32<false>(f.x, f.y);
         }
         if (valid) {
@@ -107,9 +107,9 @@ struct Nvfp4 {
     float g, six_g;
     __device__ __forceinline__ void operator()(const uint4 v, bool valid, size_t gv, uint32_t lane,
                                                uint8_t* q, uint8_t* sf, size_t sf_cols) const {
-        uint32_t m2 = dt::bf16x8_absmax2(v);
-        m2 = dt::bf16x2_absmax2(m2, __shfl_xor_sync(0xffffffffu, m2, 1));
-        const uint32_t m = dt::bf16x2_absmax_fold(m2);
+        uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                              dt::bf16x2_absmax_bits(v.z, v.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
         // sf = e4m3(amax / (6 g)); r = 1 / (sf * g), or 0 when that product is 0.
         const float s = __fdiv_rn(__uint_as_float(m << 16), six_g);
         const uint32_t code = dt::e4m3x2_from_f32<false>(s, 0.0f) & 0xFFu;
@@ -145,20 +145,20 @@ struct MxAny {
     float six_g;  // unused
     __device__ __forceinline__ void operator()(const uint4 v, bool valid, size_t gv, uint32_t lane,
                                                uint8_t* q, uint8_t* sf, size_t sf_cols) const {
-        uint32_t m2 = dt::bf16x8_absmax2(v);
-        m2 = dt::bf16x2_absmax2(m2, __shfl_xor_sync(0xffffffffu, m2, 1));
-        m2 = dt::bf16x2_absmax2(m2, __shfl_xor_sync(0xffffffffu, m2, 2));
-        const uint32_t m = dt::bf16x2_absmax_fold(m2);
+        uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                              dt::bf16x2_absmax_bits(v.z, v.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
         const uint32_t u = dt::ue8m0_from_f32<false, true>(__uint_as_float(m << 16));
         const uint32_t code = u == 0xFFu ? 0xFFu : (u > kEmax ? u - kEmax : 0u);
-        const uint32_t inv = dt::ue8m0_inverse_bf16(code);
+        const float inv = dt::ue8m0_inverse(code);
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         uint32_t lo, hi;  // this vector's 8 bytes of the payload
         if constexpr (T == 0 || T == 1) {
             uint32_t p[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float2 f = dt::bf16x2_mul_pow2(w[k], inv);
+                const float2 f = dt::bf16x2_mul_f32(w[k], inv);
                 p[k] = T == 0 ? dt::e4m3x2_from_f32<false>(f.x, f.y)
                               : dt::e5m2x2_from_f32<false>(f.x, f.y);
             }
@@ -168,7 +168,7 @@ struct MxAny {
             uint64_t bits = 0;  // element i of the vector at bits 6i .. 6i+5
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float2 f = dt::bf16x2_mul_pow2(w[k], inv);
+                const float2 f = dt::bf16x2_mul_f32(w[k], inv);
                 const uint32_t c2 = T == 3 ? dt::e2m3x2_from_f32<false>(f.x, f.y)
                                            : dt::e3m2x2_from_f32<false>(f.x, f.y);
                 bits |= static_cast<uint64_t>(c2 & 0x3Fu) << (12 * k);
@@ -190,7 +190,7 @@ struct MxAny {
             uint32_t packed = 0;  // 8 nibbles, element 0 in the low nibble
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float2 f = dt::bf16x2_mul_pow2(w[k], inv);
+                const float2 f = dt::bf16x2_mul_f32(w[k], inv);
                 packed |= dt::e2m1x2_from_f32<false>(f.x, f.y) << (8 * k);
             }
             const uint32_t partner = __shfl_xor_sync(0xffffffffu, packed, 1);
@@ -216,15 +216,15 @@ struct Mxfp8Rs {
     uint64_t seed;
     __device__ __forceinline__ void operator()(const uint4 v, bool valid, size_t gv, uint32_t lane,
                                                uint8_t* q, uint8_t* sf, size_t sf_cols) const {
-        uint32_t m2 = dt::bf16x8_absmax2(v);
-        m2 = dt::bf16x2_absmax2(m2, __shfl_xor_sync(0xffffffffu, m2, 1));
-        m2 = dt::bf16x2_absmax2(m2, __shfl_xor_sync(0xffffffffu, m2, 2));
-        const uint32_t m = dt::bf16x2_absmax_fold(m2);
+        uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                              dt::bf16x2_absmax_bits(v.z, v.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
         const uint32_t code = dt::mxfp8_scale_code(__uint_as_float(m << 16));
-        const uint32_t inv = dt::ue8m0_inverse_bf16(code);
+        const float inv = dt::ue8m0_inverse(code);
         const uint64_t h = dt::splitmix64(seed, gv);
-        const float2 a = dt::bf16x2_mul_pow2(v.x, inv), b = dt::bf16x2_mul_pow2(v.y, inv);
-        const float2 c = dt::bf16x2_mul_pow2(v.z, inv), d = dt::bf16x2_mul_pow2(v.w, inv);
+        const float2 a = dt::bf16x2_mul_f32(v.x, inv), b = dt::bf16x2_mul_f32(v.y, inv);
+        const float2 c = dt::bf16x2_mul_f32(v.z, inv), d = dt::bf16x2_mul_f32(v.w, inv);
         const uint32_t lo =
             dt::e4m3x4_from_f32_rs<false>(a.x, a.y, b.x, b.y, static_cast<uint32_t>(h));
         const uint32_t hi =
@@ -244,9 +244,9 @@ struct Nvfp4Rs {
     uint64_t seed;
     __device__ __forceinline__ void operator()(const uint4 v, bool valid, size_t gv, uint32_t lane,
                                                uint8_t* q, uint8_t* sf, size_t sf_cols) const {
-        uint32_t m2 = dt::bf16x8_absmax2(v);
-        m2 = dt::bf16x2_absmax2(m2, __shfl_xor_sync(0xffffffffu, m2, 1));
-        const uint32_t m = dt::bf16x2_absmax_fold(m2);
+        uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                              dt::bf16x2_absmax_bits(v.z, v.w)));
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
         const float s = __fdiv_rn(__uint_as_float(m << 16), six_g);
         const uint32_t code = dt::e4m3x2_from_f32<false>(s, 0.0f) & 0xFFu;
         const float t = __fmul_rn(dt::e4m3_to_f32(code), g);
@@ -279,6 +279,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     const size_t n_chunks = (n_elems + Cfg::kChunkElems - 1) / Cfg::kChunkElems;
     const size_t n_vec = n_elems / 8;
 
+    // Programmatic dependent launch: the next kernel of the stream may start its prologue on the
+    // SMs this grid frees; it reads nothing of ours before its own griddepcontrol.wait.
+    asm volatile("griddepcontrol.launch_dependents;");
+
     if (threadIdx.x == 0) {
         for (uint32_t i = 0; i < ST; ++i) {
             ptxstd::mbar_init(&s.full[i], 1);
@@ -288,6 +292,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         ptxstd::fence_mbarrier_init();
     }
     __syncthreads();
+    // The previous kernel of the stream (which may have produced x, or still read q and sf) has
+    // completed and its memory is visible from here on.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     volatile uint32_t* abort_flag = &s.abort;
 
     if (warp == CW) {
@@ -368,8 +375,21 @@ int launch(const uint16_t* x, size_t n_elems, Op op, uint8_t* q, uint8_t* sf, si
     const size_t chunks = (n_elems + Cfg::kChunkElems - 1) / Cfg::kChunkElems;
     const size_t sms = static_cast<size_t>(ptxstd::sm_count());
     const int grid = static_cast<int>(chunks < sms ? chunks : sms);
-    quantize_kernel<Cfg, Op><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(
-        x, n_elems, op, q, sf, sf_cols, err);
+    // Launched with programmatic stream serialisation, so that back-to-back calls overlap the
+    // launch and the barrier set-up with the previous kernel's last chunks.
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(static_cast<uint32_t>(grid));
+    cfg.blockDim = dim3(Cfg::kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, quantize_kernel<Cfg, Op>, x, n_elems, op, q, sf, sf_cols, err) !=
+        cudaSuccess)
+        return PTXSTD_ECUDA;
     return ptxstd::launch_status();
 }
 
