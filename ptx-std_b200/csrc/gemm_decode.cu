@@ -90,7 +90,7 @@ static_assert(kDCol + kDBufs * kTok <= 512, "TMEM budget");
 // ever two phases ahead of its barrier.
 static_assert(kTeams <= kABufs && WST % kTeams == 0, "team count vs. A buffers and weight ring");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kPrepThreads = 256;
+constexpr uint32_t kPrepThreads = 1024;
 constexpr uint32_t kFinMax = 5;  // contributors of a shared block staged in shared memory at once
 
 struct alignas(1024) Smem {
@@ -188,6 +188,16 @@ __device__ __forceinline__ uint32_t ximg_offset(uint32_t r, uint32_t k) {
            (((byte >> 4) ^ (r & 7)) << 4) + (byte & 15);
 }
 
+// MXFP8 scale code of the 32-element block whose four 16-byte vectors are held by this lane and
+// its three neighbours (lanes 4j .. 4j + 3); all 32 lanes of the warp take part.
+__device__ __forceinline__ uint32_t prep_block_code(const uint4& v) {
+    uint32_t m = dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
+                                          dt::bf16x2_absmax_bits(v.z, v.w)));
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    return dt::mxfp8_scale_code(__uint_as_float(m << 16));
+}
+
 // ---------------------------------------------------------------------------------------------
 // Kernel 1: x -> MXFP8 -> f16 B-operand image and per-row factors, one CTA per token row (rows
 // >= M write zeros); CTA 0 also clears the block counters. Sixteen small CTAs leave the other SMs
@@ -207,20 +217,23 @@ __global__ void __launch_bounds__(kPrepThreads)
         for (uint32_t i = threadIdx.x; i < N / BM; i += blockDim.x) w.counters[i] = 0;
     const uint32_t r = blockIdx.x;
     __shared__ uint32_t red[kPrepThreads / 32];
-    const uint32_t nblk = K / 32;
-    // pass 1: block scale codes and the row's largest code
-    uint32_t maxcode = 0;
+    // 16-byte vectors of the row (K % 256 == 0, so a multiple of 32: every warp runs the loops
+    // below the same number of times, as the block shuffles need). A 32-element block is the
+    // vectors of four neighbouring lanes.
+    const uint32_t nvec = K / 8;
+    const uint4* xrow = reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * K);
+    // pass 1: block scale codes and the row's largest code. A thread's first vector and its code
+    // stay in registers for pass 2 (at K <= 8192 that is the thread's only vector).
+    uint4 v0 = make_uint4(0, 0, 0, 0);
+    uint32_t code0 = 0, maxcode = 0;
     if (r < M) {
-        for (uint32_t b = threadIdx.x; b < nblk; b += blockDim.x) {
-            const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * K + b * 32);
-            uint32_t m = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint4 v = p[i];
-                m = max(m, dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v.x, v.y),
-                                                    dt::bf16x2_absmax_bits(v.z, v.w))));
+        for (uint32_t i = threadIdx.x; i < nvec; i += kPrepThreads) {
+            const uint4 v = xrow[i];
+            const uint32_t code = prep_block_code(v);
+            if (i == threadIdx.x) {
+                v0 = v;
+                code0 = code;
             }
-            const uint32_t code = dt::mxfp8_scale_code(__uint_as_float(m << 16));
             if (code != 0xFFu) maxcode = max(maxcode, code);
         }
     }
@@ -235,20 +248,13 @@ __global__ void __launch_bounds__(kPrepThreads)
                                              : __uint_as_float(0x00400000u))
                              : 0.0f;
     }
-    // pass 2: elements as f16 q * 2^(code - maxcode)
-    for (uint32_t b = threadIdx.x; b < nblk; b += blockDim.x) {
-        uint32_t h[16];
+    // pass 2: elements as f16 q * 2^(code - maxcode), one 16-byte chunk of the image per vector
+    for (uint32_t i = threadIdx.x; i < nvec; i += kPrepThreads) {
+        uint32_t h[4] = {0u, 0u, 0u, 0u};
         if (r < M) {
-            const uint4* p = reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * K + b * 32);
-            uint4 v[4];
-            uint32_t m = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                v[i] = p[i];
-                m = max(m, dt::bf16x2_fold(__vmaxu2(dt::bf16x2_absmax_bits(v[i].x, v[i].y),
-                                                    dt::bf16x2_absmax_bits(v[i].z, v[i].w))));
-            }
-            const uint32_t code = dt::mxfp8_scale_code(__uint_as_float(m << 16));
+            const bool first = i == threadIdx.x;
+            const uint4 v = first ? v0 : xrow[i];
+            const uint32_t code = first ? code0 : prep_block_code(v);
             const float inv = dt::ue8m0_inverse(code);
             // factor 2^(code - maxcode) in f32 (>= 2^-254 is not representable: flush below 2^-149)
             const int d = static_cast<int>(code) - static_cast<int>(maxcode);
@@ -256,30 +262,18 @@ __global__ void __launch_bounds__(kPrepThreads)
                               : d >= -126   ? __uint_as_float(static_cast<uint32_t>(d + 127) << 23)
                               : d >= -149   ? __uint_as_float(1u << (d + 149))
                                             : 0.0f;
+            const uint32_t ww[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t ww[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const uint16_t qq = dt::e4m3x2_from_f32<false>(
-                        __fmul_rn(dt::bf16_lo(ww[k]), inv), __fmul_rn(dt::bf16_hi(ww[k]), inv));
-                    const float2 qf = dt::e4m3x2_to_f32(qq);
-                    uint32_t hh;
-                    asm("cvt.rn.f16x2.f32 %0, %1, %2;"
-                        : "=r"(hh)
-                        : "f"(__fmul_rn(qf.y, rel)), "f"(__fmul_rn(qf.x, rel)));
-                    h[i * 4 + k] = hh;
-                }
+            for (int k = 0; k < 4; ++k) {
+                const uint16_t qq = dt::e4m3x2_from_f32<false>(__fmul_rn(dt::bf16_lo(ww[k]), inv),
+                                                               __fmul_rn(dt::bf16_hi(ww[k]), inv));
+                const float2 qf = dt::e4m3x2_to_f32(qq);
+                asm("cvt.rn.f16x2.f32 %0, %1, %2;"
+                    : "=r"(h[k])
+                    : "f"(__fmul_rn(qf.y, rel)), "f"(__fmul_rn(qf.x, rel)));
             }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) h[i] = 0;
         }
-        // 32 f16 = 64 bytes = four 16-byte chunks of the image
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4*>(w.ximg + ximg_offset(r, b * 32 + c * 8)) =
-                make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+        *reinterpret_cast<uint4*>(w.ximg + ximg_offset(r, i * 8)) = make_uint4(h[0], h[1], h[2], h[3]);
     }
 }
 
