@@ -159,3 +159,37 @@ def test_invalid_arguments(cuda):
     with pytest.raises(ptxstd.PtxStdError):
         ptxstd.quantize_mxfp8(torch.zeros((4, 128), dtype=torch.bfloat16, device="cuda"),
                               sf_layout=1)  # rows % 128 != 0
+
+
+def test_back_to_back_calls_keep_stream_order(cuda, oracle):
+    """The quantisers launch with programmatic dependent launch: a call may start on the SMs that
+    the previous kernel of the stream frees, and waits (griddepcontrol.wait) before it reads x or
+    writes q and sf. In one stream, with no synchronisation between the launches:
+      - a call reads the x that the torch kernel just before it wrote (read after write);
+      - the torch kernel just after a call overwrites that call's x (write after read);
+      - two calls into the same outputs leave the second call's bytes (write after write).
+    """
+    torch = cuda
+    import ptxstd
+    rows, cols = 2048, 4096
+    xb = [_edge_matrix(rows, cols, seed=71), _edge_matrix(rows, cols, seed=72)]
+    xs = [torch.from_numpy(v.view(np.int16)).cuda().view(torch.bfloat16) for v in xb]
+    want = [oracle.quantize_mxfp8(v) for v in xb]
+    x = torch.empty_like(xs[0])
+    n = 6
+    qs = [torch.empty((rows, cols), dtype=torch.uint8, device="cuda") for _ in range(n)]
+    sfs = [torch.empty((rows, cols // 32), dtype=torch.uint8, device="cuda") for _ in range(n)]
+    qw = torch.empty((rows, cols), dtype=torch.uint8, device="cuda")
+    sfw = torch.empty((rows, cols // 32), dtype=torch.uint8, device="cuda")
+    for i in range(n):
+        ptxstd.quantize_mxfp8(xs[(i + 1) % 2], out=(qw, sfw))
+        x.copy_(xs[i % 2])
+        ptxstd.quantize_mxfp8(x, out=(qs[i], sfs[i]))
+        x.fill_(float("nan"))
+        ptxstd.quantize_mxfp8(xs[i % 2], out=(qw, sfw))
+    torch.cuda.synchronize()
+    for i in range(n):
+        assert np.array_equal(qs[i].cpu().numpy(), want[i % 2][0]), i
+        assert np.array_equal(sfs[i].cpu().numpy(), want[i % 2][1]), i
+    assert np.array_equal(qw.cpu().numpy(), want[(n - 1) % 2][0])
+    assert np.array_equal(sfw.cpu().numpy(), want[(n - 1) % 2][1])
