@@ -11,8 +11,9 @@
  *   - Every function returns a ptxstd_status; no C++ exception or abort crosses the boundary.
  *   - Pointers named d_* are device pointers owned by the caller (16-byte aligned unless noted);
  *     h_* are host pointers. Kernels are asynchronous on `stream` (a cudaStream_t, 0 = legacy).
- *     The quantisers and the decode GEMM use programmatic dependent launch. They touch caller
- *     memory only after griddepcontrol.wait, so stream order holds as for any launch.
+ *     The quantisers use programmatic dependent launch and touch caller memory only after
+ *     griddepcontrol.wait, so stream order holds as for any launch. The decode GEMM is launched
+ *     the same way behind its own prep kernel, which is an ordinary launch.
  *   - Narrow codes are stored as in the reference: element 0 in the least significant bits
  *     (src/data_types/vector.rs:1-11); two E2M1 values per byte, element 0 in the low nibble
  *     (src/data_types/float4.rs:5-6).
