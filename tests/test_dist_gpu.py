@@ -134,6 +134,9 @@ def _worker(rank, world, port, out_dir):
 
 def _timeout_worker(rank, world, port, out_dir):
     import sys
+    # a failure-detection test: no NVLink multicast (NVLS) objects in NCCL while a step is left
+    # unfinished on purpose
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [os.path.join(root, "ptx-std_b200"), os.path.join(root, "oracle")]
     import torch
