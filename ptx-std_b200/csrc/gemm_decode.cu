@@ -359,10 +359,54 @@ __device__ __forceinline__ void unit_range(uint64_t U, uint32_t& u0, uint32_t& u
     u1 = static_cast<uint32_t>(U * (blockIdx.x + 1) / gridDim.x);
 }
 
+// The order in which a CTA works through its range [u0, u1), as runs of units of one W block (one
+// accumulator each): run A, the part of the block the range starts in; the whole blocks; run B,
+// the part of the block it ends in. In range order (A, whole blocks, B) the CTA's last run is the
+// head of a block it shares with the next CTA, which finished that block's tail long before, so
+// the call ends on that block's finish (partial, counter, the others' partials fetched and
+// summed). When every CTA holds whole blocks (U / G >= 2 S), the order A, B, whole blocks ends
+// each CTA on a whole block stored straight from registers instead, and the shared blocks are
+// finished while the weight stream goes on; the whole blocks then take their K stages from
+// u0 % S on (wrapping), so that the CTAs keep reading different K stages (and x-image stages) at
+// any moment, as they do in range order. Every role walks the same runs.
+struct UnitRuns {
+    uint32_t nbA, ksA, nA;  // run A: block nbA, stages ksA .. ksA + nA - 1
+    uint32_t nbB, nB;       // run B (if nB > 0): block nbB, stages 0 .. nB - 1
+    uint32_t nbM, nM, rot;  // whole blocks nbM .. nbM + nM - 1, stages rot, rot + 1, ... mod S
+    uint32_t nruns, b_first;
+};
+__device__ __forceinline__ UnitRuns unit_runs(uint32_t u0, uint32_t u1, uint32_t S,
+                                              bool b_first) {
+    UnitRuns o = {};
+    if (u0 >= u1) return o;
+    const uint32_t f1 = min(u1, (u0 / S + 1) * S);  // end of run A
+    o.nbA = u0 / S, o.ksA = u0 % S, o.nA = f1 - u0, o.nruns = 1;
+    if (f1 == u1) return o;
+    const uint32_t l0 = ((u1 - 1) / S) * S;  // start of run B, >= f1
+    o.nbB = l0 / S, o.nB = u1 - l0;
+    o.nbM = f1 / S, o.nM = (l0 - f1) / S;
+    o.b_first = b_first ? 1u : 0u;
+    o.rot = b_first ? u0 % S : 0u;
+    o.nruns = 2 + o.nM;
+    return o;
+}
+// Run r of o: its block, first stage and unit count; unit k of the run is stage (ks0 + k) mod S.
+__device__ __forceinline__ void unit_run(const UnitRuns& o, uint32_t r, uint32_t S, uint32_t& nb,
+                                         uint32_t& ks0, uint32_t& cnt) {
+    const uint32_t rb = o.b_first ? 1u : o.nM + 1;  // the index of run B
+    if (r == 0) {
+        nb = o.nbA, ks0 = o.ksA, cnt = o.nA;
+    } else if (r == rb) {
+        nb = o.nbB, ks0 = 0, cnt = o.nB;
+    } else {
+        nb = o.nbM + r - (o.b_first ? 2u : 1u), ks0 = o.rot, cnt = S;
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmW, const uint8_t* __restrict__ sfW,
                        uint8_t* ws, const __grid_constant__ ptxstd::decode::Out out, uint32_t M,
-                       uint32_t N, uint32_t K, float gw, uint32_t* err) {
+                       uint32_t N, uint32_t K, float gw, uint32_t* err, uint32_t b_first) {
     extern __shared__ uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                        ~static_cast<uintptr_t>(1023));
@@ -416,20 +460,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             // each weight byte is read once: evict-first keeps the partial slots and the x image
             // in L2 (N = 57344: 57.3 -> 56.5 us per call; N = 28672: 34.7 -> 34.0 us)
             const uint64_t pol = ptxstd::policy_evict_first();
-            uint32_t nb = u0 / S, ks = u0 % S;
-            for (uint32_t u = u0; u < u1; ++u, ks = (ks + 1 == S) ? 0 : ks + 1, nb += (ks == 0)) {
+            const UnitRuns ord = unit_runs(u0, u1, S, b_first != 0);
+            bool stop = false;
+            for (uint32_t r = 0, i = 0; r < ord.nruns && !stop; ++r) {
+            uint32_t nb, ks0, cnt;
+            unit_run(ord, r, S, nb, ks0, cnt);
+            for (uint32_t k = 0, ks = ks0; k < cnt; ++k, ++i, ks = (ks + 1 == S) ? 0 : ks + 1) {
                 if (!mbar_wait(&s.wempty[stage], phase ^ 1u)) {
                     fail(s, err, kDetailProducer | stage);
+                    stop = true;
                     break;
                 }
                 // first pass: stage i - kRamp has landed before stage i is requested (its first
                 // phase; it is refilled only after the producer wraps around)
-                const uint32_t i = u - u0;
                 if (i >= kRamp && i < WST && !mbar_wait(&s.wfull[i - kRamp], 0)) {
                     fail(s, err, kDetailProducer | 0x40);
+                    stop = true;
                     break;
                 }
-                if (aborted(s)) break;
+                if (aborted(s)) {
+                    stop = true;
+                    break;
+                }
                 ptxstd::mbar_arrive_expect_tx(&s.wfull[stage], kWRingBytes);
                 ptxstd::tma_load_2d_hint(s.w[stage], &tmW, &s.wfull[stage],
                                          static_cast<int32_t>(ks * (BKS / 2)),
@@ -444,6 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     phase ^= 1u;
                 }
             }
+            }
             if (aborted(s)) {
                 for (uint32_t i = 0; i < WST; ++i)
                     if (issued & (1u << i)) mbar_wait(&s.wfull[i], (issued_parity >> i) & 1u);
@@ -454,13 +507,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ptxstd::elect_one()) {
             asm volatile("griddepcontrol.wait;" ::: "memory");
             uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
-            uint32_t ks = u0 % S;
-            for (uint32_t u = u0; u < u1; ++u, ks = (ks + 1 == S) ? 0 : ks + 1) {
+            const UnitRuns ord = unit_runs(u0, u1, S, b_first != 0);
+            bool stop = false;
+            for (uint32_t r = 0; r < ord.nruns && !stop; ++r) {
+            uint32_t nb, ks0, cnt;
+            unit_run(ord, r, S, nb, ks0, cnt);
+            for (uint32_t k = 0, ks = ks0; k < cnt; ++k, ks = (ks + 1 == S) ? 0 : ks + 1) {
                 if (!mbar_wait(&s.xempty[stage], phase ^ 1u)) {
                     fail(s, err, kDetailXProducer | stage);
+                    stop = true;
                     break;
                 }
-                if (aborted(s)) break;
+                if (aborted(s)) {
+                    stop = true;
+                    break;
+                }
                 ptxstd::mbar_arrive_expect_tx(&s.xfull[stage], kXStageBytes);
                 ptxstd::bulk_load(s.x[stage], wsp.ximg + static_cast<size_t>(ks) * kXStageBytes,
                                   kXStageBytes, &s.xfull[stage]);
@@ -470,6 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     stage = 0;
                     phase ^= 1u;
                 }
+            }
             }
             if (aborted(s)) {
                 for (uint32_t i = 0; i < XST; ++i)
@@ -482,20 +544,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t idesc = 0;
             t5::idesc_dense(/*F16*/ 0, /*F16*/ 0, /*F32*/ 1, BM, kTok, idesc);
             uint32_t stage = 0, phase = 0, abuf = 0, aphase = 0, dbuf = 0, dphase = 0;
-            uint32_t ks = u0 % S;
-            for (uint32_t u = u0; u < u1 && !aborted(s); ++u, ks = (ks + 1 == S) ? 0 : ks + 1) {
-                const bool first = (u == u0) || ks == 0;
-                const bool last = (u + 1 == u1) || ks == S - 1;
+            const UnitRuns ord = unit_runs(u0, u1, S, b_first != 0);
+            bool stop = false;
+            for (uint32_t r = 0; r < ord.nruns && !stop; ++r) {
+            uint32_t nb, ks0, cnt;
+            unit_run(ord, r, S, nb, ks0, cnt);
+            for (uint32_t k = 0; k < cnt; ++k) {
+                if (aborted(s)) {
+                    stop = true;
+                    break;
+                }
+                const bool first = k == 0;        // one accumulator per run
+                const bool last = k + 1 == cnt;
                 if (first) {
                     // the epilogue warps have drained this accumulator's previous segment
                     if (!mbar_wait(&s.dempty[dbuf], dphase ^ 1u)) {
                         fail(s, err, kDetailMma | 0x30);
+                        stop = true;
                         break;
                     }
                 }
                 const uint32_t d = tmem + kDCol + dbuf * kTok;
                 if (!mbar_wait(&s.afull[abuf], aphase) || !mbar_wait(&s.xfull[stage], phase)) {
                     fail(s, err, kDetailMma | stage);
+                    stop = true;
                     break;
                 }
                 t5::fence_after_thread_sync();
@@ -524,6 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     abuf = 0;
                     aphase ^= 1u;
                 }
+            }
             }
             t5::commit(&s.drain);
             mbar_wait(&s.drain, 0);
@@ -606,6 +679,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* fac = s.fac[warp - kEpiWarp];
         if (lane < kTok) fac[lane] = __ldcg(wsp.factors + lane) * gw;
         __syncwarp();
+        const UnitRuns ord = unit_runs(u0, u1, S, b_first != 0);
+        uint32_t n_runs = ord.nruns;
         namespace pd = ptxstd::decode;
         if (out.nranks != 0) {
             // Peer-to-peer output: every rank's stream has passed its readers of the previous
@@ -617,17 +692,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             okr = __all_sync(0xffffffffu, okr);
             if (!okr) {
                 if (lane == 0) fail(s, err, kDetailEpi | 0x40);
-                u1 = u0;  // no stores, no completion signal
+                n_runs = 0;  // no stores, no completion signal
             }
         }
         uint32_t dbuf = 0, dphase = 0, sphase = 0;
         const uint32_t e = warp - kEpiWarp;
         const uint32_t G = gridDim.x, c = blockIdx.x;
-        for (uint32_t u = u0; u < u1;) {
-            // one W-block segment: units u .. end - 1 of block nb
-            const uint32_t nb = u / S;
-            const uint32_t end = min(u1, (nb + 1) * S);
-            u = end;
+        for (uint32_t r = 0; r < n_runs; ++r) {
+            // one W-block run, in the MMA's order
+            uint32_t nb, ks0, cnt;
+            unit_run(ord, r, S, nb, ks0, cnt);
             bool ok = mbar_wait(&s.dfull[dbuf], dphase);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) {
@@ -813,9 +887,12 @@ int launch_decode(const uint16_t* x, const uint8_t* W, const uint8_t* sfW, float
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    // whole blocks first only when every CTA holds at least two blocks' worth of units
+    const uint64_t units = static_cast<uint64_t>(N / BM) * static_cast<uint64_t>(K / BKS);
+    const uint32_t b_first = units / grid >= 2ull * static_cast<uint64_t>(K / BKS) ? 1u : 0u;
     if (cudaLaunchKernelEx(&cfg, gemm_decode_kernel, tw, sfW, ws, out, static_cast<uint32_t>(M),
                            static_cast<uint32_t>(N), static_cast<uint32_t>(K), gw,
-                           err) != cudaSuccess)
+                           err, b_first) != cudaSuccess)
         return PTXSTD_ECUDA;
     st = ptxstd::launch_status();
     if (st || out.nranks == 0) return st;
