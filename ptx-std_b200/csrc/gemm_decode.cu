@@ -19,7 +19,8 @@
 //   CTAs leave the other SMs free, so the main kernel's weight stream starts at once.
 // Kernel 2, gemm_decode (persistent, one CTA per SM, launched with programmatic dependent launch so
 //   its setup and first weight loads overlap kernel 1):
-//   work = (128-row W block, 256-K stage) units split evenly over the CTAs ("stream-K");
+//   work = (128-row W block, 256-K stage) units split evenly over the CTAs ("stream-K"), each
+//           CTA walking its range in the order of unit_runs;
 //   warp 0: weight producer: W tile 128 x 128 bytes + W scales 2 KiB per stage into an 8-stage
 //           ring that the dequant warps release as soon as they have read it (so the HBM stream
 //           never waits on MMA completion, nor on kernel 1), loaded with an L2 evict-first policy;
