@@ -93,16 +93,22 @@ class ClockSampler:
             nv = self.nvml
             smax = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
 
+            def sample():
+                try:
+                    sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                    r = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                    self.samples.append((sm, smax, r))
+                except Exception:
+                    pass
+
             def poll():
                 while not self._stop.is_set():
-                    try:
-                        sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
-                        r = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
-                        self.samples.append((sm, smax, r))
-                    except Exception:
-                        pass
+                    sample()
                     time.sleep(0.002)
 
+            # the caller's stop() also samples once itself, right after the timed region, so that
+            # a region whose host thread holds the interpreter lock still gets a sample under load
+            self._sample = sample
             self.thread = threading.Thread(target=poll, daemon=True)
             self.thread.start()
             return
@@ -127,6 +133,7 @@ class ClockSampler:
 
     def stop(self) -> dict:
         if self.nvml is not None:
+            self._sample()
             self._stop.set()
             self.thread.join(timeout=2)
             sm = [x[0] for x in self.samples]
